@@ -1,0 +1,497 @@
+#!/usr/bin/env python3
+"""Headline benchmark: BASELINE configuration 2 -- one MoE layer of the
+Inkling shape decoding one token (router f32 [258 x 7168] + sigmoid top-6 of
+256 routed experts with Q2_K gate/up and Q3_K down, ff 2048, + 2 shared Q4_K
+experts), weights resident in HBM, experts sharded over the GPUs.
+
+A step is one token through one layer. Steps rotate over --layers distinct
+layer instances (default 4, 4 x 152.6 MB touched per rotation > 126 MB L2)
+and over hidden states seeds 1..64, so weights are never L2-resident.
+
+value  = whole-job quantized-matvec HBM throughput: algorithmic bytes of
+         the steps (152.6 MB/token) / device time (max over ranks).
+e2e    = the same through the reference-facing C ABI (include/sepia_gpu.h:
+         sepia_gpu_begin / sepia_gpu_moe_layer / sepia_gpu_end) with host
+         buffers: x uploaded and the layer output read back every step.
+Run:   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import re
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Q-matvec HBM GB/s (% of 8 TB/s); synthetic Inkling-shape decode tok/s"
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="sepia", choices=["sepia", "reference"])
+    ap.add_argument("--layers", type=int, default=4, help="distinct layer instances rotated per step")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--parity", action="store_true", help="check one step against the CPU oracle")
+    return ap.parse_args()
+
+
+def peak_hbm():
+    try:
+        d = json.loads(PEAKS.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ------------------------------------------------------------------- clocks
+class Clocks:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.p = None
+        self.index = index
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return None
+        time.sleep(0.25)
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except Exception:
+            self.p.kill()
+            return None
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [s.strip() for s in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------- CPU
+def cpu_token_seconds(shape, budget_s=12.0):
+    """Time the CPU oracle (a port of the reference's qlinear loop; the
+    reference has no Q2_K/Q3_K) on one token of the layer: router linear +
+    6 routed SwiGLU experts + 2 shared, all host threads. Returns
+    (seconds per token, threads, sample description)."""
+    import numpy as np
+    from oracle import oracle as O
+    from sepia_b200 import synth
+    O.build()
+    n = O.nproc()
+    rng = np.random.default_rng(11)
+    s = shape
+    g = synth.matrix_host(rng, s.gate_type, s.ff, s.hidden)
+    u = synth.matrix_host(rng, s.up_type, s.ff, s.hidden)
+    d = synth.matrix_host(rng, s.down_type, s.hidden, s.ff)
+    sg = synth.matrix_host(rng, s.sh_gate_type, s.ff, s.hidden)
+    su = synth.matrix_host(rng, s.sh_up_type, s.ff, s.hidden)
+    sd = synth.matrix_host(rng, s.sh_down_type, s.hidden, s.ff)
+    rw = (rng.standard_normal((s.n_routed + s.n_shared, s.hidden)) * 0.02).astype(np.float32)
+    x = synth.hidden_state(1, s.hidden)
+    reps = 0
+    t_tot = 0.0
+    while True:
+        t0 = time.perf_counter()
+        O.linear(rw, x, nthreads=n)
+        for _ in range(s.topk):
+            O.expert_swiglu(s.gate_type, g, s.up_type, u, s.down_type, d, s.hidden, s.ff, x, nthreads=n)
+        for _ in range(s.n_shared):
+            O.expert_swiglu(s.sh_gate_type, sg, s.sh_up_type, su, s.sh_down_type, sd, s.hidden, s.ff, x, 0.5,
+                            nthreads=n)
+        t_tot += time.perf_counter() - t0
+        reps += 1
+        if t_tot > budget_s or reps >= 50:
+            break
+    return t_tot / reps, n, f"{reps} token(s) of config 2 (router + 6 routed + 2 shared SwiGLU) on {n} threads"
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from sepia_b200.synth import MoeShape
+    shape = MoeShape()
+    import numpy as np
+    from oracle import oracle as O
+    from sepia_b200 import synth
+    O.build()
+    n = O.nproc()
+    s = shape
+    rng = np.random.default_rng(11)
+    mats = [synth.matrix_host(rng, t, r, c) for t, r, c in [
+        (s.gate_type, s.ff, s.hidden), (s.up_type, s.ff, s.hidden), (s.down_type, s.hidden, s.ff),
+        (s.sh_gate_type, s.ff, s.hidden), (s.sh_up_type, s.ff, s.hidden), (s.sh_down_type, s.hidden, s.ff)]]
+    rw = (rng.standard_normal((s.n_routed + s.n_shared, s.hidden)) * 0.02).astype(np.float32)
+
+    def step(i):
+        x = synth.hidden_state(1 + i % 64, s.hidden)
+        O.linear(rw, x, nthreads=n)
+        for _ in range(s.topk):
+            O.expert_swiglu(s.gate_type, mats[0], s.up_type, mats[1], s.down_type, mats[2], s.hidden, s.ff, x,
+                            nthreads=n)
+        for _ in range(s.n_shared):
+            O.expert_swiglu(s.sh_gate_type, mats[3], s.sh_up_type, mats[4], s.sh_down_type, mats[5], s.hidden,
+                            s.ff, x, 0.5, nthreads=n)
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(i)
+    dt = time.perf_counter() - t0
+    gbs = args.steps * shape.token_bytes() / dt / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (BASELINE config 2 distributions)",
+            "config": {"workload": "config2_moe_layer_decode_1tok", "hidden": 7168, "ff": 2048, "experts": 256,
+                       "topk": 6, "shared": 2, "types": "Q2_K gate/up, Q3_K down, Q4_K shared"},
+            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": n, "kind": "port",
+                             "sample": f"{args.steps} tokens of config 2 on {n} threads (oracle port of the "
+                                       "reference qlinear loop; the reference lacks Q2_K/Q3_K)"},
+            "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "decode_tok_s": round(args.steps / dt, 3)}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- traffic
+def committed_traffic():
+    """dram bytes per launch of k_gateup from the committed ncu summary."""
+    p = ROOT / "profiles" / "k_gateup_moe_layer.md"
+    try:
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+        return float(m.group(1)) if m else None
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------- main
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+    from sepia_b200 import lib as LIB
+    from sepia_b200.moe import MoeLayerDevice
+    from sepia_b200.synth import MoeShape, hidden_state
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    L = LIB.load()
+    shape = MoeShape()
+    layers = [MoeLayerDevice.random(shape, seed=100 + l, rank=rank, world=world) for l in range(args.layers)]
+    X = torch.stack([torch.from_numpy(hidden_state(s, shape.hidden)) for s in range(1, 65)]).cuda()
+    out = torch.empty(shape.hidden, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def step(i):
+        layers[i % len(layers)].forward(X[i % 64], out, group=group)
+
+    if args.parity and rank == 0 and world == 1:
+        parity_check(layers[0], X[0])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = Clocks(local) if rank == 0 else None
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = clk.stop() if clk else None
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tok_bytes = shape.token_bytes()
+    gbs = args.steps * tok_bytes / (ms / 1e3) / 1e9
+    launches_per_step = 3 if world == 1 else 4
+
+    # ---- per-kernel live timing (same workload, events between launches) ----
+    kt = per_kernel_times(layers, X, args, world, group)
+    peak, peak_kind = peak_hbm()
+    s = shape
+    from sepia_b200 import quants as Q
+    gu_bytes = (s.topk * s.ff * (Q.row_bytes(s.gate_type, s.hidden) + Q.row_bytes(s.up_type, s.hidden))
+                + s.n_shared * s.ff * (Q.row_bytes(s.sh_gate_type, s.hidden) + Q.row_bytes(s.sh_up_type, s.hidden))
+                + 4 * s.hidden + 4 * (s.topk + s.n_shared) * s.ff)
+    dn_bytes = (s.topk * s.hidden * Q.row_bytes(s.down_type, s.ff) + s.n_shared * s.hidden * Q.row_bytes(s.sh_down_type, s.ff)
+                + 4 * (s.topk + s.n_shared) * s.ff + 4 * s.hidden)
+    rt_bytes = s.router_bytes() + 4 * s.n_routed + 4 * s.hidden
+    roof = None
+    if kt and world == 1:
+        ach = gu_bytes / (kt["k_gateup"] / 1e3) / 1e9
+        roof = {"bound": "hbm", "kernel": "k_gateup", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(ach / peak, 4), "peak_kind": peak_kind, "traffic": committed_traffic(),
+                "algorithmic_bytes_per_launch": gu_bytes,
+                "per_kernel_us": {k: round(v * 1e3, 2) for k, v in kt.items()},
+                "per_kernel_gbs": {"k_router": round(rt_bytes / (kt["k_router"] / 1e3) / 1e9, 1),
+                                   "k_gateup": round(ach, 1),
+                                   "k_down": round(dn_bytes / (kt["k_down"] / 1e3) / 1e9, 1)}}
+
+    # ---- e2e through the C ABI with host buffers ----
+    e2e = None
+    if not args.no_e2e and world == 1:
+        e2e = abi_e2e(layers, args, shape)
+    elif world > 1:
+        e2e = sharded_e2e(layers, args, shape, group)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        sec, n, sample = cpu_token_seconds(shape)
+        cpu = {"value": round(tok_bytes / sec / 1e9, 4), "unit": "GB/s", "cores": n, "kind": "port",
+               "sample": sample, "tok_s": round(1.0 / sec, 3)}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (BASELINE config 2 distributions, device-generated, seeded)",
+                "config": {"workload": "config2_moe_layer_decode_1tok", "hidden": 7168, "ff": 2048, "experts": 256,
+                           "topk": 6, "shared": 2, "types": "Q2_K gate/up, Q3_K down, Q4_K shared, f32 router",
+                           "parallelism": f"ep{world}" if world > 1 else "single", "layer_instances": args.layers,
+                           "l2": f"inputs larger than L2: {args.layers} rotating layer instances x "
+                                 f"{tok_bytes / 1e6:.1f} MB/step", "bytes_per_token": tok_bytes},
+                "pct_of_8tbs": round(100 * gbs / 8000, 2), "pct_of_measured_peak": round(100 * gbs / peak, 2),
+                "decode_tok_s": round(args.steps / (ms / 1e3), 1),
+                "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": launches_per_step * args.steps,
+                "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def per_kernel_times(layers, X, args, world, group):
+    """Average device time of each kernel of the layer, CUDA events on the
+    launching stream, over `steps` steps of the same rotation."""
+    import torch
+    from sepia_b200.lib import load, ok
+    L = load()
+    st = torch.cuda.current_stream()
+    n = max(20, min(args.steps, 200))
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n)]
+    out = torch.empty(layers[0].shape.hidden, device="cuda")
+    for i in range(n):
+        D = layers[i % len(layers)]
+        x = X[i % 64]
+        Ls, ws = C.byref(D.struct), C.byref(D.ws)
+        ev[i][0].record(st)
+        ok(L.sepia_cuda_moe_router(Ls, x.data_ptr(), ws, st.cuda_stream))
+        ev[i][1].record(st)
+        ok(L.sepia_cuda_moe_gateup(Ls, x.data_ptr(), ws, st.cuda_stream))
+        ev[i][2].record(st)
+        ok(L.sepia_cuda_moe_down(Ls, ws, out.data_ptr(), 1 if world > 1 else 0, st.cuda_stream))
+        ev[i][3].record(st)
+    torch.cuda.synchronize()
+    names = ["k_router", "k_gateup", "k_down"]
+    tot = {k: 0.0 for k in names}
+    for i in range(n):
+        for j, k in enumerate(names):
+            tot[k] += ev[i][j].elapsed_time(ev[i][j + 1])
+    return {k: v / n for k, v in tot.items()}
+
+
+def abi_e2e(layers, args, shape):
+    """Per step: write x into a Shared buffer's host mirror, sepia_gpu_begin
+    (uploads it), sepia_gpu_moe_layer, sepia_gpu_end (downloads the output,
+    waits), read the output on the host. Weights sit in Private buffers."""
+    import numpy as np
+    import torch
+    from cuda.bindings import runtime as rt
+    from sepia_b200.lib import SepiaGpuMoeDesc, load
+    from sepia_b200.synth import hidden_state
+    G = load()
+    assert G.sepia_gpu_init(b"cuda") == 1
+    s = shape
+    sg, su, sd, ssg, ssu, ssd = s.strides()
+    descs, bufs = [], []
+
+    def dev_copy(dst_buf, dst_off, src_t):
+        ptr = G.sepia_gpu_gpu_addr(dst_buf) + dst_off
+        err, = rt.cudaMemcpy(ptr, src_t.data_ptr(), src_t.numel() * src_t.element_size(),
+                             rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice)
+        assert err == rt.cudaError_t.cudaSuccess
+
+    for D in layers:
+        ne = D.gate.numel() + D.up.numel() + D.down.numel()
+        nsh = D.sh_gate.numel() + D.sh_up.numel() + D.sh_down.numel()
+        be, bsh = G.sepia_gpu_alloc(ne, 1), G.sepia_gpu_alloc(nsh, 1)
+        brw, brb = G.sepia_gpu_alloc(D.router_w.numel() * 4, 1), G.sepia_gpu_alloc(D.router_bias.numel() * 4, 1)
+        assert be and bsh and brw and brb
+        dev_copy(be, 0, D.gate)
+        dev_copy(be, D.gate.numel(), D.up)
+        dev_copy(be, D.gate.numel() + D.up.numel(), D.down)
+        dev_copy(bsh, 0, D.sh_gate)
+        dev_copy(bsh, D.sh_gate.numel(), D.sh_up)
+        dev_copy(bsh, D.sh_gate.numel() + D.sh_up.numel(), D.sh_down)
+        dev_copy(brw, 0, D.router_w)
+        dev_copy(brb, 0, D.router_bias)
+        d = SepiaGpuMoeDesc()
+        d.hidden, d.ff, d.n_routed, d.n_shared, d.topk = s.hidden, s.ff, s.n_routed, s.n_shared, s.topk
+        d.route_scale, d.global_scale = s.route_scale, s.global_scale
+        d.router_w, d.router_bias = brw, brb
+        d.gate_type, d.up_type, d.down_type = s.gate_type, s.up_type, s.down_type
+        d.experts, d.gate_off, d.up_off, d.down_off = be, 0, D.gate.numel(), D.gate.numel() + D.up.numel()
+        d.gate_stride, d.up_stride, d.down_stride = sg, su, sd
+        d.sh_gate_type, d.sh_up_type, d.sh_down_type = s.sh_gate_type, s.sh_up_type, s.sh_down_type
+        d.shared, d.sh_gate_off, d.sh_up_off = bsh, 0, D.sh_gate.numel()
+        d.sh_down_off = D.sh_gate.numel() + D.sh_up.numel()
+        d.sh_gate_stride, d.sh_up_stride, d.sh_down_stride = ssg, ssu, ssd
+        descs.append(d)
+        bufs += [be, bsh, brw, brb]
+    xs = [hidden_state(i, s.hidden) for i in range(1, 65)]
+    bx, bo = G.sepia_gpu_alloc(s.hidden * 4, 0), G.sepia_gpu_alloc(s.hidden * 4, 0)
+    hx, ho = G.sepia_gpu_host_ptr(bx), G.sepia_gpu_host_ptr(bo)
+    res = np.empty(s.hidden, np.float32)
+    chk = 0.0
+
+    def step(i):
+        nonlocal chk
+        C.memmove(hx, xs[i % 64].ctypes.data, s.hidden * 4)
+        assert G.sepia_gpu_begin() == 1
+        assert G.sepia_gpu_moe_layer(C.byref(descs[i % len(descs)]), bx, bo, None, None) == 1
+        assert G.sepia_gpu_end() == 1
+        C.memmove(res.ctypes.data, ho, s.hidden * 4)
+        chk += float(res[0])
+
+    torch.cuda.synchronize()
+    for i in range(max(3, args.warmup)):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(i)
+    dt = time.perf_counter() - t0
+    for b in bufs + [bx, bo]:
+        G.sepia_gpu_free(b)
+    return {"value": round(args.steps * s.token_bytes() / dt / 1e9, 1), "unit": "GB/s",
+            "h2d_bytes_per_step": 2 * s.hidden * 4, "d2h_bytes_per_step": s.hidden * 4,
+            "ms_per_step": round(1e3 * dt / args.steps, 4), "tok_s": round(args.steps / dt, 1),
+            "path": "sepia_gpu_begin + sepia_gpu_moe_layer + sepia_gpu_end (host-buffer ABI)"}
+
+
+def sharded_e2e(layers, args, shape, group):
+    """N > 1: pinned host x -> device, the sharded layer (router, own experts,
+    NCCL all-reduce of slot terms, combine), device -> pinned host output;
+    wall clock per step, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from sepia_b200.synth import hidden_state
+    s = shape
+    hx = [torch.from_numpy(hidden_state(i, s.hidden)).pin_memory() for i in range(1, 65)]
+    ho = torch.empty(s.hidden, dtype=torch.float32).pin_memory()
+    xd = torch.empty(s.hidden, dtype=torch.float32, device="cuda")
+    out = torch.empty(s.hidden, dtype=torch.float32, device="cuda")
+
+    def step(i):
+        xd.copy_(hx[i % 64], non_blocking=True)
+        layers[i % len(layers)].forward(xd, out, group=group)
+        ho.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(i)
+    dt = torch.tensor([time.perf_counter() - t0], device="cuda")
+    dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+    dt = float(dt.item())
+    return {"value": round(args.steps * s.token_bytes() / dt / 1e9, 1), "unit": "GB/s",
+            "h2d_bytes_per_step": s.hidden * 4, "d2h_bytes_per_step": s.hidden * 4,
+            "ms_per_step": round(1e3 * dt / args.steps, 4), "tok_s": round(args.steps / dt, 1),
+            "path": "raw entry points + torch.distributed NCCL all-reduce"}
+
+
+def parity_check(D, x):
+    """One step of the bench's own device-generated layer against the oracle
+    (the selected experts are copied back to the host)."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    out = torch.empty(D.shape.hidden, device="cuda")
+    D.forward(x, out)
+    torch.cuda.synchronize()
+    idx = D.topk_idx.cpu().numpy()
+    s = D.shape
+    xh = x.cpu().numpy()
+    logits = O.linear(D.router_w.cpu().numpy(), xh)
+    ri, rw = O.route_select(logits, D.router_bias.cpu().numpy(), s.n_routed, s.n_shared, s.topk, s.route_scale,
+                            s.global_scale)
+    assert np.array_equal(ri, idx), (ri, idx)
+    ref = np.zeros(s.hidden, np.float32)
+    for j, e in enumerate(idx):
+        g, u, d = D.expert_bytes_host(int(e))
+        ref += O.expert_swiglu(s.gate_type, g, s.up_type, u, s.down_type, d, s.hidden, s.ff, xh, nthreads=8) * rw[j]
+    sg, su, sd = D.strides[3:]
+    for k in range(s.n_shared):
+        from sepia_b200 import quants as Q
+        ng = Q.row_bytes(s.sh_gate_type, s.hidden) * s.ff
+        nu = Q.row_bytes(s.sh_up_type, s.hidden) * s.ff
+        nd = Q.row_bytes(s.sh_down_type, s.ff) * s.hidden
+        ref += O.expert_swiglu(s.sh_gate_type, D.sh_gate[k * sg:k * sg + ng].cpu().numpy(), s.sh_up_type,
+                               D.sh_up[k * su:k * su + nu].cpu().numpy(), s.sh_down_type,
+                               D.sh_down[k * sd:k * sd + nd].cpu().numpy(), s.hidden, s.ff, xh, rw[s.topk + k],
+                               nthreads=8)
+    err = O.rel_err(out.cpu().numpy(), ref)
+    print(f"parity: router ids {list(idx)} match; max_rel_err {err:.2e}", file=sys.stderr)
+    assert err <= 1e-4
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,143 @@
+/* include/sepia_cuda.h -- CUDA-native entry points of libsepia_cuda.so.
+ *
+ * These take raw device pointers and a cudaStream_t (passed as void*; NULL
+ * selects the library's own stream) and are stream-ordered: nothing here
+ * synchronises, allocates, or touches host memory, so a caller may capture
+ * sequences of them in a CUDA graph. They are what the reference-shaped
+ * ABI in sepia_gpu.h is built on, and what bench.py and the multi-GPU
+ * expert-sharded path call directly. All return 1 on success and 0 on a
+ * rejected argument or launch failure (message in sepia_cuda_last_error()).
+ * Each cites the reference code whose semantics it reproduces.
+ */
+#ifndef SEPIA_CUDA_H
+#define SEPIA_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ggml type ids (src/quants.h:6-10 plus ggml's numbering for the four
+ * formats the reference lacks) */
+enum {
+    SEPIA_CUDA_T_F32 = 0, SEPIA_CUDA_T_F16 = 1, SEPIA_CUDA_T_Q8_0 = 8, SEPIA_CUDA_T_Q2_K = 10,
+    SEPIA_CUDA_T_Q3_K = 11, SEPIA_CUDA_T_Q4_K = 12, SEPIA_CUDA_T_Q5_K = 13, SEPIA_CUDA_T_Q6_K = 14,
+    SEPIA_CUDA_T_IQ2_XXS = 16, SEPIA_CUDA_T_IQ2_XS = 17, SEPIA_CUDA_T_IQ3_XXS = 18,
+    SEPIA_CUDA_T_IQ1_S = 19, SEPIA_CUDA_T_IQ4_XS = 23
+};
+
+/* ------------------------------------------------------------ runtime */
+const char *sepia_cuda_last_error(void);
+/* Synchronises `stream`, then returns and clears the device error word
+ * (0 = none, 1 = a kernel's bounded wait timed out, 2 = bad arguments seen
+ * on the device). Returns -1 if the synchronisation itself failed. */
+int sepia_cuda_device_error(void *stream);
+int sepia_cuda_sm_count(void);
+/* ggml geometry: elements per block, bytes per block, bytes per row of n
+ * elements (-1 when unsupported or ragged). src/quants.c:28-56. */
+int sepia_cuda_block_elems(int ggml_type);
+int sepia_cuda_block_bytes(int ggml_type);
+int64_t sepia_cuda_row_bytes(int ggml_type, int64_t n);
+
+/* ------------------------------------------------ quantized matvec */
+/* out[0..n) = dequant(raw) bit-exactly (src/quants.c:250 dequantize_row). */
+int sepia_cuda_dequant(int ggml_type, const void *raw, float *out, int64_t n, void *stream);
+/* y[v, o] = sum_i dequant(W[o, :])[i] * x[v, i] for v < n_vec, fp32
+ * accumulation (src/sepia.c:742-753 qlinear; metal/matvec_q.metal). W is
+ * row-major [out_dim, in_dim] ggml blocks at any byte alignment. */
+int sepia_cuda_matvec_q(int ggml_type, const void *w, const float *x, float *y,
+                        int64_t out_dim, int64_t in_dim, int64_t n_vec, void *stream);
+/* f32 helpers with double accumulation (src/sepia.c:720-740, 755, 801-816) */
+int sepia_cuda_matvec_f32(const float *w, const float *x, float *y, int64_t out_dim, int64_t in_dim, void *stream);
+int sepia_cuda_rmsnorm(const float *w, const float *x, float *y, int64_t rows, int64_t n, float eps, void *stream);
+int sepia_cuda_silu_mul(const float *g, const float *u, float *z, int64_t n, void *stream);
+int sepia_cuda_sconv(const float *w, const float *hist, const float *in, float *out,
+                     int64_t C, int64_t K, int64_t T, void *stream);
+int sepia_cuda_sconv_hist_roll(float *hist, const float *in, int64_t C, int64_t K, int64_t T, void *stream);
+
+/* ----------------------------------------------------------- MoE layer */
+/* Device description of one MoE layer (src/sepia.c:583-626 LayerWeights'
+ * MoE fields, with the experts quantized as in real mode). Routed expert e
+ * lives at gate + slot(e)*gate_stride (likewise up/down) where slot(e) =
+ * expert_slot[e] if expert_slot is non-NULL, else e / world when world > 1,
+ * else e. Expert sharding: routed expert e is computed on rank
+ * e % world, shared expert s on rank s % world; every rank computes the same
+ * router output. */
+typedef struct {
+    int64_t hidden, ff;
+    int32_t n_routed, n_shared, topk;
+    float route_scale, global_scale;
+    const float *router_w;     /* [n_routed + n_shared, hidden] */
+    const float *router_bias;  /* [n_routed] selection-only bias */
+    int32_t gate_type, up_type, down_type;
+    const void *gate, *up, *down;
+    int64_t gate_stride, up_stride, down_stride;
+    int32_t sh_gate_type, sh_up_type, sh_down_type;
+    const void *sh_gate, *sh_up, *sh_down;
+    int64_t sh_gate_stride, sh_up_stride, sh_down_stride;
+    int32_t rank, world;
+    const int32_t *expert_slot;
+} SepiaMoeLayer;
+
+/* Device scratch of one layer call, carved from one caller allocation. */
+typedef struct {
+    float *logits;          /* [n_routed + n_shared] */
+    int32_t *topk_idx;      /* [topk] */
+    float *weights;         /* [topk + n_shared] routed weights then shared gammas */
+    float *h;               /* [topk + n_shared, ff] SwiGLU activations */
+    float *slots;           /* [topk + n_shared, hidden] per-slot terms (sharded mode) */
+    unsigned int *counter;  /* router completion counter; zero before first use */
+} SepiaMoeWork;
+
+size_t sepia_cuda_moe_work_bytes(const SepiaMoeLayer *L);
+/* base: 256-byte aligned device memory of at least moe_work_bytes(L) bytes,
+ * zeroed once by the caller (the router counter resets itself). */
+int sepia_cuda_moe_work_carve(const SepiaMoeLayer *L, void *base, size_t bytes, SepiaMoeWork *ws);
+/* Router logits (fp64 accumulation) + on-device moe_route_select
+ * (src/sepia.c:1329-1375) -> ws->logits, ws->topk_idx, ws->weights. */
+int sepia_cuda_moe_router(const SepiaMoeLayer *L, const float *x, const SepiaMoeWork *ws, void *stream);
+/* Experts after the router: gate/up+SwiGLU then down. write_slots = 0:
+ * out = sum_j w_j E_j(x) + sum_s S_s(x) in the reference order.
+ * write_slots = 1: ws->slots[j] = this rank's term for slot j (zero for
+ * slots owned by other ranks); after a sum all-reduce of ws->slots across
+ * ranks, sepia_cuda_moe_combine gives the same bits as world = 1. */
+int sepia_cuda_moe_experts(const SepiaMoeLayer *L, const float *x, const SepiaMoeWork *ws, float *out,
+                           int write_slots, void *stream);
+/* The two halves of sepia_cuda_moe_experts, separately launchable (used to
+ * time each kernel): gate/up+SwiGLU into ws->h, then down + combine. */
+int sepia_cuda_moe_gateup(const SepiaMoeLayer *L, const float *x, const SepiaMoeWork *ws, void *stream);
+int sepia_cuda_moe_down(const SepiaMoeLayer *L, const SepiaMoeWork *ws, float *out, int write_slots, void *stream);
+int sepia_cuda_moe_combine(const SepiaMoeLayer *L, const SepiaMoeWork *ws, float *out, void *stream);
+/* router + experts (world must be 1 or the layer already sharded with
+ * write_slots handled by the caller). */
+int sepia_cuda_moe_layer(const SepiaMoeLayer *L, const float *x, const SepiaMoeWork *ws, float *out, void *stream);
+/* Selection only: top-k of given scores by the reference's strict-'>' scan
+ * (src/sepia.c:1336-1347; lowest index wins ties). */
+int sepia_cuda_topk_select(const float *scores, int32_t n, int32_t topk, int32_t *idx, void *stream);
+
+/* ------------------------------------------------- banded attention */
+/* rel_logits[t,h,r] = sum_d r_vec[t,h,d] * rel_proj[d,r] (src/sepia.c:1201-1208) */
+int sepia_cuda_rel_project(const float *r_vec, const float *rel_proj, float *rel_logits,
+                           int64_t T, int64_t H, int64_t d_rel, int64_t rel_extent, void *stream);
+/* Split-KV banded attention (src/sepia.c:1210-1262). kv_f16 selects fp16
+ * K/V caches (else fp32); kv_lo/kv_hi/tau are DEVICE arrays of length T;
+ * max_kv bounds kv_hi-kv_lo+1 and sizes the split; ws holds the per-split
+ * partials (sepia_cuda_banded_attn_ws_bytes). */
+size_t sepia_cuda_banded_attn_ws_bytes(int64_t T, int64_t H, int64_t Hkv, int64_t Dh, int64_t max_kv);
+int sepia_cuda_banded_attn(int kv_f16, const float *q, const void *k, const void *v, const float *rel_logits,
+                           float *out, const int64_t *kv_lo, const int64_t *kv_hi, const float *tau,
+                           int64_t T, int64_t H, int64_t Hkv, int64_t Dh, int64_t rel_extent,
+                           int64_t q_pos_base, int64_t kv_dim, float inv_head_dim, int64_t max_kv,
+                           void *ws, size_t ws_bytes, void *stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,283 @@
+// sepia_b200/csrc/attn.cu -- banded relative-position attention
+// (ABI sepia_gpu_rel_project / sepia_gpu_banded_attn, src/sepia_gpu.h:
+// 209-231; CPU oracle attn_forward_chunk, src/sepia.c:1195-1262; Metal twin
+// metal/banded_attn.metal).
+//
+// Per query token t (position q_pos = q_pos_base + t) and head h:
+//   s[kv] = dot(q[t,h], k[kv,hk]) * inv_head_dim
+//           + (q_pos - kv < rel_extent ? rel_logits[t,h,q_pos-kv] * tau[t] : 0)
+//   out[t,h] = softmax_kv(s) . v[kv,hk],  kv in [kv_lo[t], kv_hi[t]],
+// with hk = h / (H/Hkv) (GQA) and q already scaled by tau by the caller.
+//
+// Decode at long context is a read of the whole K/V band, so the kernel is
+// split-KV ("flash decoding"): grid (splits, Hkv, T); one CTA owns a chunk
+// of kv positions of one KV head and ALL query heads of that GQA group, so
+// each K/V row crosses HBM exactly once. Each CTA writes (m, l, acc[Dh])
+// per head; k_attn_combine merges the splits in split order (deterministic).
+// K/V may be fp32 (the reference cache) or fp16 (the decode configuration).
+#include "../../include/sepia_cuda.h"
+#include "runtime.h"
+#include "common.cuh"
+
+#include <cuda_fp16.h>
+#include <algorithm>
+
+namespace sepia {
+
+constexpr int kAttnThreads = 128;
+constexpr int kAttnKT = 64;          // kv positions per tile
+constexpr int kAttnMaxDh = 128;
+constexpr int kAttnMaxG = 16;        // query heads per KV head
+constexpr int kAttnPad = 4;          // smem row padding (floats) against bank conflicts
+
+struct AttnParams {
+    const float *q;            // [T, H, Dh]
+    const void *k, *v;         // [cap, kv_dim]
+    const float *rel_logits;   // [T, H, E]
+    const int64_t *kv_lo, *kv_hi;
+    const float *tau;
+    float *part;               // [T, H, S, Dh + 2]
+    int64_t T, H, Hkv, Dh, E, q_pos_base, kv_dim;
+    float inv_head_dim;
+    int S;
+    int64_t max_chunk;         // kv positions per split (upper bound)
+};
+
+template <typename KV>
+__device__ __forceinline__ float kv_at(const KV *p, int64_t i);
+template <>
+__device__ __forceinline__ float kv_at<float>(const float *p, int64_t i) { return __ldg(p + i); }
+template <>
+__device__ __forceinline__ float kv_at<__half>(const __half *p, int64_t i) { return __half2float(p[i]); }
+
+template <typename KV>
+__global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P) {
+    extern __shared__ __align__(16) float sm[];
+    const int s = blockIdx.x, hk = blockIdx.y;
+    const int64_t t = blockIdx.z;
+    const int G = (int)(P.H / P.Hkv), Dh = (int)P.Dh;
+    const int ld = Dh + kAttnPad;
+    float *sq = sm;                              // [G][ld]
+    float *sk = sq + G * ld;                     // [KT][ld]
+    float *sv = sk + kAttnKT * ld;               // [KT][ld]
+    float *ss = sv + kAttnKT * ld;               // [G][KT]
+    float *sml = ss + G * kAttnKT;               // [G][2] running m, l
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t lo = P.kv_lo[t], hi = P.kv_hi[t];
+    const int64_t n = hi - lo + 1;
+    const int64_t chunk = (n + P.S - 1) / P.S;
+    const int64_t c0 = lo + (int64_t)s * chunk;
+    const int64_t c1 = min(hi + 1, c0 + chunk);
+    const int64_t q_pos = P.q_pos_base + t;
+    const float tau = P.tau[t];
+    const KV *K = reinterpret_cast<const KV *>(P.k);
+    const KV *V = reinterpret_cast<const KV *>(P.v);
+
+    for (int i = tid; i < G * Dh; i += kAttnThreads) {
+        const int g = i / Dh, d = i % Dh;
+        sq[g * ld + d] = P.q[(t * P.H + (int64_t)hk * G + g) * P.Dh + d];
+    }
+    if (tid < G) { sml[2 * tid] = -INFINITY; sml[2 * tid + 1] = 0.0f; }
+
+    // PV ownership: warp w owns heads g = w, w+4, ...; lane owns dims lane + 32j
+    constexpr int kHPW = kAttnMaxG / 4;
+    float acc[kHPW][kAttnMaxDh / 32];
+#pragma unroll
+    for (int a = 0; a < kHPW; a++)
+#pragma unroll
+        for (int j = 0; j < kAttnMaxDh / 32; j++) acc[a][j] = 0.0f;
+    __syncthreads();
+
+    for (int64_t base = c0; base < c1; base += kAttnKT) {
+        const int nt = (c1 - base < kAttnKT) ? (int)(c1 - base) : kAttnKT;
+        // ---- stage K and V rows of this KV head (converted to fp32) ----
+        for (int i = tid; i < nt * Dh; i += kAttnThreads) {
+            const int r = i / Dh, d = i % Dh;
+            const int64_t off = (base + r) * P.kv_dim + (int64_t)hk * Dh + d;
+            sk[r * ld + d] = kv_at<KV>(K, off);
+            sv[r * ld + d] = kv_at<KV>(V, off);
+        }
+        __syncthreads();
+        // ---- scores: thread -> (kv row r, heads g = gi, gi+stride...) ----
+        {
+            const int r = tid % kAttnKT;
+            const int g0 = tid / kAttnKT;            // 0 or 1
+            const int gstep = kAttnThreads / kAttnKT; // 2
+            if (r < nt) {
+                const int64_t kv = base + r;
+                const int64_t dist = q_pos - kv;
+                for (int g = g0; g < G; g += gstep) {
+                    float d0 = 0.f, d1 = 0.f;
+                    const float *qr = sq + g * ld, *kr = sk + r * ld;
+                    for (int d = 0; d < Dh; d += 2) {
+                        d0 = fmaf(qr[d], kr[d], d0);
+                        d1 = fmaf(qr[d + 1], kr[d + 1], d1);
+                    }
+                    float sc = (d0 + d1) * P.inv_head_dim;
+                    if (dist < P.E && dist >= 0)
+                        sc += P.rel_logits[(t * P.H + (int64_t)hk * G + g) * P.E + dist] * tau;
+                    ss[g * kAttnKT + r] = sc;
+                }
+            } else {
+                for (int g = g0; g < G; g += gstep) ss[g * kAttnKT + r] = -INFINITY;
+            }
+        }
+        __syncthreads();
+        // ---- online softmax update + PV, per head owned by this warp ----
+#pragma unroll
+        for (int a = 0; a < kHPW; a++) {
+            const int g = warp + 4 * a;
+            if (g < G) {
+                const float v0 = ss[g * kAttnKT + lane], v1 = ss[g * kAttnKT + lane + 32];
+                const float tmax = warp_max(fmaxf(v0, v1));
+                const float m_old = sml[2 * g];
+                const float m_new = fmaxf(m_old, tmax);
+                const float corr = (m_old == -INFINITY) ? 0.0f : expf(m_old - m_new);
+                const float p0 = (v0 == -INFINITY) ? 0.0f : expf(v0 - m_new);
+                const float p1 = (v1 == -INFINITY) ? 0.0f : expf(v1 - m_new);
+                ss[g * kAttnKT + lane] = p0;
+                ss[g * kAttnKT + lane + 32] = p1;
+                const float psum = warp_sum(p0 + p1);
+                __syncwarp();
+                if (lane == 0) { sml[2 * g] = m_new; sml[2 * g + 1] = sml[2 * g + 1] * corr + psum; }
+#pragma unroll
+                for (int j = 0; j < kAttnMaxDh / 32; j++) acc[a][j] *= corr;
+                for (int r = 0; r < nt; r++) {
+                    const float pr = ss[g * kAttnKT + r];
+#pragma unroll
+                    for (int j = 0; j < kAttnMaxDh / 32; j++) {
+                        const int d = lane + 32 * j;
+                        if (d < Dh) acc[a][j] = fmaf(pr, sv[r * ld + d], acc[a][j]);
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+    // ---- write this split's partial per head ----
+#pragma unroll
+    for (int a = 0; a < kHPW; a++) {
+        const int g = warp + 4 * a;
+        if (g < G) {
+            const int64_t h = (int64_t)hk * G + g;
+            float *pp = P.part + ((t * P.H + h) * P.S + s) * (P.Dh + 2);
+            if (lane == 0) { pp[0] = sml[2 * g]; pp[1] = sml[2 * g + 1]; }
+#pragma unroll
+            for (int j = 0; j < kAttnMaxDh / 32; j++) {
+                const int d = lane + 32 * j;
+                if (d < Dh) pp[2 + d] = acc[a][j];
+            }
+        }
+    }
+}
+
+// out[t,h,:] = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M), splits in order.
+__global__ void k_attn_combine(const float *part, float *out, int64_t TH, int S, int64_t Dh) {
+    const int64_t th = blockIdx.x;
+    if (th >= TH) return;
+    const float *pp = part + th * S * (Dh + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < S; s++) M = fmaxf(M, pp[s * (Dh + 2)]);
+    float L = 0.0f;
+    for (int s = 0; s < S; s++) {
+        const float m = pp[s * (Dh + 2)];
+        if (m != -INFINITY) L += pp[s * (Dh + 2) + 1] * expf(m - M);
+    }
+    for (int64_t d = threadIdx.x; d < Dh; d += blockDim.x) {
+        float a = 0.0f;
+        for (int s = 0; s < S; s++) {
+            const float m = pp[s * (Dh + 2)];
+            if (m != -INFINITY) a += pp[s * (Dh + 2) + 2 + d] * expf(m - M);
+        }
+        out[th * Dh + d] = a / L;
+    }
+}
+
+// rel_logits[t,h,r] = sum_d r_vec[t,h,d] * rel_proj[d,r] (double accumulation)
+__global__ void k_rel_project(const float *r_vec, const float *rel_proj, float *rel_logits, int64_t TH,
+                              int64_t d_rel, int64_t E) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= TH * E) return;
+    const int64_t th = i / E, r = i % E;
+    const float *rv = r_vec + th * d_rel;
+    double acc = 0.0;
+    for (int64_t d = 0; d < d_rel; d++) acc = fma((double)rv[d], (double)rel_proj[d * E + r], acc);
+    rel_logits[i] = (float)acc;
+}
+
+int attn_splits(int64_t T, int64_t Hkv, int64_t max_n) {
+    const int sms = dev_info().sm_count > 0 ? dev_info().sm_count : 148;
+    int64_t want = (4 * (int64_t)sms + T * Hkv - 1) / (T * Hkv);
+    const int64_t by_len = (max_n + kAttnKT - 1) / kAttnKT;   // at least one tile per split
+    want = std::max<int64_t>(1, std::min<int64_t>(want, by_len));
+    return (int)std::min<int64_t>(want, 256);
+}
+
+size_t attn_part_bytes(int64_t T, int64_t H, int S, int64_t Dh) {
+    return (size_t)T * (size_t)H * (size_t)S * (size_t)(Dh + 2) * sizeof(float);
+}
+
+int launch_banded_attn(int kv_f16, const float *q, const void *k, const void *v, const float *rel_logits, float *out,
+                       const int64_t *kv_lo_d, const int64_t *kv_hi_d, const float *tau_d, int64_t T, int64_t H,
+                       int64_t Hkv, int64_t Dh, int64_t E, int64_t q_pos_base, int64_t kv_dim, float inv_head_dim,
+                       int S, float *part, cudaStream_t st) {
+    if (T <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || Dh <= 0 || E < 0 || kv_dim < Hkv * Dh)
+        return fail("banded_attn: bad geometry T=%lld H=%lld Hkv=%lld Dh=%lld E=%lld kv_dim=%lld", (long long)T,
+                    (long long)H, (long long)Hkv, (long long)Dh, (long long)E, (long long)kv_dim);
+    if (Dh > kAttnMaxDh) return fail("banded_attn: Dh=%lld exceeds %d", (long long)Dh, kAttnMaxDh);
+    if (H / Hkv > kAttnMaxG) return fail("banded_attn: %lld query heads per KV head exceeds %d", (long long)(H / Hkv), kAttnMaxG);
+    if (!q || !k || !v || !out || !kv_lo_d || !kv_hi_d || !tau_d || !part || (E > 0 && !rel_logits))
+        return fail("banded_attn: null pointer");
+    if (S < 1) return fail("banded_attn: bad split count");
+    AttnParams P;
+    P.q = q; P.k = k; P.v = v; P.rel_logits = rel_logits; P.kv_lo = kv_lo_d; P.kv_hi = kv_hi_d; P.tau = tau_d;
+    P.part = part; P.T = T; P.H = H; P.Hkv = Hkv; P.Dh = Dh; P.E = E; P.q_pos_base = q_pos_base; P.kv_dim = kv_dim;
+    P.inv_head_dim = inv_head_dim; P.S = S; P.max_chunk = 0;
+    const int G = (int)(H / Hkv);
+    const int ld = (int)Dh + kAttnPad;
+    const size_t smem = sizeof(float) * ((size_t)G * ld + 2 * (size_t)kAttnKT * ld + (size_t)G * kAttnKT + 2 * G);
+    const void *fn = kv_f16 ? (const void *)k_attn_split<__half> : (const void *)k_attn_split<float>;
+    if (!ensure_smem(fn, (int)smem)) return 0;
+    dim3 grid((unsigned)S, (unsigned)Hkv, (unsigned)T);
+    if (kv_f16) k_attn_split<__half><<<grid, kAttnThreads, smem, st>>>(P);
+    else k_attn_split<float><<<grid, kAttnThreads, smem, st>>>(P);
+    if (!check(cudaGetLastError(), "banded_attn launch")) return 0;
+    k_attn_combine<<<(unsigned)(T * H), 128, 0, st>>>(part, out, T * H, S, Dh);
+    return check(cudaGetLastError(), "banded_attn combine launch");
+}
+
+int launch_rel_project(const float *r_vec, const float *rel_proj, float *rel_logits, int64_t T, int64_t H,
+                       int64_t d_rel, int64_t E, cudaStream_t st) {
+    if (T <= 0 || H <= 0 || d_rel <= 0 || E <= 0 || !r_vec || !rel_proj || !rel_logits)
+        return fail("rel_project: bad arguments");
+    const int64_t n = T * H * E;
+    k_rel_project<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(r_vec, rel_proj, rel_logits, T * H, d_rel, E);
+    return check(cudaGetLastError(), "rel_project launch");
+}
+
+}  // namespace sepia
+
+using namespace sepia;
+
+extern "C" size_t sepia_cuda_banded_attn_ws_bytes(int64_t T, int64_t H, int64_t Hkv, int64_t Dh, int64_t max_kv) {
+    if (T <= 0 || H <= 0 || Hkv <= 0 || Dh <= 0) return 0;
+    return attn_part_bytes(T, H, attn_splits(T, Hkv, max_kv), Dh);
+}
+
+extern "C" int sepia_cuda_banded_attn(int kv_f16, const float *q, const void *k, const void *v, const float *rel_logits,
+                                      float *out, const int64_t *kv_lo, const int64_t *kv_hi, const float *tau,
+                                      int64_t T, int64_t H, int64_t Hkv, int64_t Dh, int64_t rel_extent,
+                                      int64_t q_pos_base, int64_t kv_dim, float inv_head_dim, int64_t max_kv,
+                                      void *ws, size_t ws_bytes, void *stream) {
+    const int S = attn_splits(T, Hkv, max_kv > 0 ? max_kv : 1);
+    if (!ws || ws_bytes < attn_part_bytes(T, H, S, Dh))
+        return fail("banded_attn: workspace of %zu bytes < %zu needed", ws_bytes, attn_part_bytes(T, H, S, Dh));
+    return launch_banded_attn(kv_f16, q, k, v, rel_logits, out, kv_lo, kv_hi, tau, T, H, Hkv, Dh, rel_extent,
+                              q_pos_base, kv_dim, inv_head_dim, S, (float *)ws, as_stream(stream));
+}
+
+extern "C" int sepia_cuda_rel_project(const float *r_vec, const float *rel_proj, float *rel_logits, int64_t T,
+                                      int64_t H, int64_t d_rel, int64_t rel_extent, void *stream) {
+    return launch_rel_project(r_vec, rel_proj, rel_logits, T, H, d_rel, rel_extent, as_stream(stream));
+}

@@ -1,0 +1,716 @@
+// sepia_b200/csrc/moe.cu -- one MoE layer for one token, entirely on device.
+//
+// Replaces the reference's host-synchronised sequence in
+// real_mlp_moe_forward_gpu (src/sepia.c:3831-3974: router matvec, SYNC,
+// host moe_route_select, per-expert gate/up/silu/down dispatches, SYNC, host
+// combine) with three kernels and no host round trip:
+//   k_router      logits = W_r x (fp64 accumulation, as dotf does), then the
+//                 last CTA to finish runs moe_route_select (src/sepia.c:
+//                 1329-1375): sigmoid + selection bias, top-k by the strict
+//                 '>' scan (lowest index wins ties), log-sigmoid/LSE weights
+//                 over the k raw logits plus the shared-sink logits.
+//   k_gateup      for every selected routed expert and every shared expert,
+//                 gate and up row tiles stream through shared memory and the
+//                 epilogue writes h = silu(g)*u (times gamma for shared
+//                 experts, mlp_moe_forward's order, src/sepia.c:1432-1444).
+//   k_down        row tiles of every active expert's down matrix; the
+//                 epilogue sums sum_j w_j*E_j + sum_s S_s in the reference
+//                 order (routed j = 0..k-1, then shared) -- or, for expert
+//                 sharding, writes each slot's term separately so an
+//                 all-reduce plus k_combine reproduces the same sums bit for
+//                 bit on any number of GPUs.
+#include "../../include/sepia_cuda.h"
+#include "runtime.h"
+#include "stream.cuh"
+
+#include <algorithm>
+
+namespace sepia {
+
+constexpr int kMaxSlots = 16;      // topk + n_shared
+constexpr int kRouterWarps = 8;
+constexpr int kGuStagesMax = 8;
+constexpr int kDnStagesMax = 8;
+constexpr int kTRG = 8;            // max rows per gate/up unit
+constexpr int kTRD = 4;            // rows per down unit
+constexpr int kDnSlotGroups = 4;   // down consumer warp groups (slots split over them)
+constexpr int kDnSPW = 2;           // slots per down consumer warp (<= 8 slots total)
+
+// --------------------------------------------------------------- device-side layer
+struct MoeDev {
+    int64_t hidden, ff;
+    int n_routed, n_shared, topk;
+    float route_scale, global_scale;
+    const float *router_w, *router_bias;
+    int gate_type, up_type, down_type, sh_gate_type, sh_up_type, sh_down_type;
+    const uint8_t *gate, *up, *down, *sh_gate, *sh_up, *sh_down;
+    int64_t gate_stride, up_stride, down_stride, sh_gate_stride, sh_up_stride, sh_down_stride;
+    int64_t rb_gate, rb_up, rb_down, rb_sh_gate, rb_sh_up, rb_sh_down;
+    int rank, world;
+    const int32_t *expert_slot;
+    int *err;
+};
+
+// Active slots of this rank, in the reference's combine order.
+// slot j < topk: routed expert idx[j]; slot topk+s: shared expert s.
+__device__ __forceinline__ int active_slots(const MoeDev &L, const int32_t *idx, int (&slots)[kMaxSlots]) {
+    int n = 0;
+    for (int j = 0; j < L.topk; j++) {
+        const int e = idx[j];
+        if (e >= 0 && e < L.n_routed && (e % L.world) == L.rank) slots[n++] = j;
+    }
+    for (int s = 0; s < L.n_shared; s++)
+        if ((s % L.world) == L.rank) slots[n++] = L.topk + s;
+    return n;
+}
+
+__device__ __forceinline__ int64_t local_expert(const MoeDev &L, int e) {
+    if (L.expert_slot) return L.expert_slot[e];
+    return L.world > 1 ? e / L.world : e;
+}
+
+// ============================================================== router
+// sigmoid as the reference computes it (1/(1+expf(-x)) in float), with
+// expf taken as the correctly rounded float of the double exponential.
+__device__ __forceinline__ float sigmoid_ref(float x) {
+    const float e = (float)exp(-(double)x);
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+}
+__device__ __forceinline__ float logsigmoid_ref(float x) {
+    if (x >= 0.0f) return -log1pf((float)exp(-(double)x));
+    return x - log1pf((float)exp((double)x));
+}
+
+__global__ void __launch_bounds__(kRouterWarps * 32) k_router(const MoeDev L, const float *x, float *logits,
+                                                               int32_t *topk_idx, float *weights,
+                                                               unsigned int *counter) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_total = L.n_routed + L.n_shared;
+    const int row = blockIdx.x * kRouterWarps + warp;
+    if (row < n_total) {
+        const float *w = L.router_w + (int64_t)row * L.hidden;
+        double acc = 0.0;
+        const bool vec = ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15) == 0;
+        const int64_t n4 = vec ? (L.hidden / 4) : 0;
+        for (int64_t i = lane; i < n4; i += 32) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(w) + i);
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(x) + i);
+            acc = fma((double)a.x, (double)b.x, acc);
+            acc = fma((double)a.y, (double)b.y, acc);
+            acc = fma((double)a.z, (double)b.z, acc);
+            acc = fma((double)a.w, (double)b.w, acc);
+        }
+        for (int64_t i = n4 * 4 + lane; i < L.hidden; i += 32) acc = fma((double)w[i], (double)x[i], acc);
+        acc = warp_sum_d(acc);
+        if (lane == 0) logits[row] = (float)acc;
+    }
+    // ---- last CTA performs the selection ----
+    __shared__ unsigned int s_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = (atomicAdd(counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+
+    __shared__ float s_score[1024];
+    __shared__ float s_bv[kRouterWarps];
+    __shared__ int s_bi[kRouterWarps];
+    __shared__ int s_sel[kMaxSlots];
+    const volatile float *lg = logits;
+    for (int i = threadIdx.x; i < L.n_routed; i += blockDim.x)
+        s_score[i] = __fadd_rn(sigmoid_ref(lg[i]), L.router_bias[i]);
+    __syncthreads();
+    for (int j = 0; j < L.topk; j++) {
+        // block argmax: first index of the maximum among unused entries
+        float bv = 0.0f;
+        int bi = -1;
+        for (int i = threadIdx.x; i < L.n_routed; i += blockDim.x) {
+            bool used = false;
+            for (int q = 0; q < j; q++) used |= (s_sel[q] == i);
+            if (used) continue;
+            const float v = s_score[i];
+            if (bi < 0 || v > bv) { bv = v; bi = i; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) { s_bv[warp] = bv; s_bi[warp] = bi; }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float v = s_bv[0];
+            int b = s_bi[0];
+            for (int w2 = 1; w2 < kRouterWarps; w2++) {
+                const int oi = s_bi[w2];
+                if (oi >= 0 && (b < 0 || s_bv[w2] > v || (s_bv[w2] == v && oi < b))) { v = s_bv[w2]; b = oi; }
+            }
+            s_sel[j] = b;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        const int n_sel = L.topk + L.n_shared;
+        float lp[kMaxSlots];
+        for (int j = 0; j < n_sel; j++) {
+            const float l = (j < L.topk) ? lg[s_sel[j]] : lg[L.n_routed + (j - L.topk)];
+            lp[j] = logsigmoid_ref(l);
+        }
+        float lmax = lp[0];
+        for (int j = 1; j < n_sel; j++) lmax = fmaxf(lmax, lp[j]);
+        double se = 0.0;
+        for (int j = 0; j < n_sel; j++) se += exp((double)(lp[j] - lmax));
+        const double lse = (double)lmax + log(se);
+        const double sc = (double)L.route_scale * (double)L.global_scale;
+        for (int j = 0; j < n_sel; j++) weights[j] = (float)(exp((double)lp[j] - lse) * sc);
+        for (int j = 0; j < L.topk; j++) topk_idx[j] = s_sel[j];
+        *counter = 0u;   // ready for the next launch
+        __threadfence();
+    }
+}
+
+// Selection only (bit-exact part of the router): top-k of given scores.
+__global__ void k_topk(const float *scores, int n, int topk, int32_t *idx) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    for (int j = 0; j < topk; j++) {
+        int best = -1;
+        for (int i = 0; i < n; i++) {
+            bool used = false;
+            for (int q = 0; q < j; q++) used |= (idx[q] == i);
+            if (used) continue;
+            if (best < 0 || scores[i] > scores[best]) best = i;
+        }
+        idx[j] = best;
+    }
+}
+
+// ============================================================== shared GEMV pieces
+template <int T, int TRW>
+__device__ __forceinline__ void rows_dot(const uint8_t *base, int64_t rb, int nr, int sb, int p,
+                                         const XPart &xp, int64_t in_dim, float (&acc)[TRW]) {
+    const int sbb = fmt_sb_bytes(T);
+    const int sbs[1] = {sb};
+    const XPart(&xa)[1] = *reinterpret_cast<const XPart(*)[1]>(&xp);
+#pragma unroll
+    for (int i = 0; i < TRW; i++)
+        acc[i] = (i < nr) ? row_parts_dot<T, 1>(base + i * rb, sbb, sbs, p, xa, in_dim) : 0.0f;
+}
+
+template <int TRW>
+__device__ __noinline__ void rows_dot_dyn(int t, const uint8_t *base, int64_t rb, int nr, int sb, int p,
+                                          const XPart &xp, int64_t in_dim, float (&acc)[TRW]) {
+    switch (t) {
+    case T_F32: rows_dot<T_F32, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    case T_F16: rows_dot<T_F16, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    case T_Q8_0: rows_dot<T_Q8_0, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    case T_Q2_K: rows_dot<T_Q2_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    case T_Q3_K: rows_dot<T_Q3_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    case T_Q4_K: rows_dot<T_Q4_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    case T_Q5_K: rows_dot<T_Q5_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    case T_Q6_K: rows_dot<T_Q6_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    case T_IQ2_XXS: rows_dot<T_IQ2_XXS, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    case T_IQ2_XS: rows_dot<T_IQ2_XS, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    case T_IQ3_XXS: rows_dot<T_IQ3_XXS, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    case T_IQ1_S: rows_dot<T_IQ1_S, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    case T_IQ4_XS: rows_dot<T_IQ4_XS, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    default:
+        for (int i = 0; i < TRW; i++) acc[i] = 0.0f;
+    }
+}
+
+// Specialised fast path for the formats of the headline configuration; any
+// other type goes through the (slower, generic) dynamic dispatcher.
+template <int TRW>
+__device__ __forceinline__ void rows_dot_any(int t, const uint8_t *base, int64_t rb, int nr, int sb, int p,
+                                             const XPart &xp, int64_t in_dim, float (&acc)[TRW]) {
+    if (t == T_Q2_K) rows_dot<T_Q2_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc);
+    else if (t == T_Q3_K) rows_dot<T_Q3_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc);
+    else if (t == T_Q4_K) rows_dot<T_Q4_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc);
+    else rows_dot_dyn<TRW>(t, base, rb, nr, sb, p, xp, in_dim, acc);
+}
+
+// ============================================================== gate/up + SwiGLU
+struct GuParams {
+    MoeDev L;
+    const float *x;
+    const int32_t *idx;
+    const float *weights;
+    float *h;                 // [slots, ff]
+    int tr_routed, tr_shared; // rows per unit for each kind
+    int nwc;                  // column warps (per matrix group)
+    int stages;
+    uint32_t slot_bytes, up_off;
+};
+
+__device__ __forceinline__ void gu_unit(const GuParams &P, const int (&slots)[kMaxSlots], int n_act, int64_t u,
+                                        int &slot, int64_t &r0, int &nr, const uint8_t *&g_src,
+                                        const uint8_t *&u_src, int64_t &rbg, int64_t &rbu, int &tg, int &tu) {
+    const MoeDev &L = P.L;
+    const int64_t tiles_r = (L.ff + P.tr_routed - 1) / P.tr_routed;
+    const int64_t tiles_s = (L.ff + P.tr_shared - 1) / P.tr_shared;
+    int64_t rem = u;
+    for (int a = 0; a < n_act; a++) {
+        const int s = slots[a];
+        const bool routed = s < L.topk;
+        const int64_t tiles = routed ? tiles_r : tiles_s;
+        if (rem < tiles) {
+            const int tr = routed ? P.tr_routed : P.tr_shared;
+            slot = s;
+            r0 = rem * tr;
+            nr = (int)imin64(tr, L.ff - r0);
+            if (routed) {
+                const int64_t le = local_expert(L, P.idx[s]);
+                rbg = L.rb_gate; rbu = L.rb_up; tg = L.gate_type; tu = L.up_type;
+                g_src = L.gate + le * L.gate_stride + r0 * rbg;
+                u_src = L.up + le * L.up_stride + r0 * rbu;
+            } else {
+                const int64_t sh = s - L.topk;
+                rbg = L.rb_sh_gate; rbu = L.rb_sh_up; tg = L.sh_gate_type; tu = L.sh_up_type;
+                g_src = L.sh_gate + sh * L.sh_gate_stride + r0 * rbg;
+                u_src = L.sh_up + sh * L.sh_up_stride + r0 * rbu;
+            }
+            return;
+        }
+        rem -= tiles;
+    }
+    slot = -1;
+}
+
+__global__ void __launch_bounds__(17 * 32, 1) k_gateup(const GuParams P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_cons = 2 * P.nwc;
+    const MoeDev &L = P.L;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kGuStagesMax;
+    float *red = reinterpret_cast<float *>(smem + 256);   // [2][nwc][kTRG]
+    uint8_t *stage0 = smem + 256 + ((2 * 16 * kTRG * 4 + 127) & ~127);
+
+    int slots[kMaxSlots];
+    const int n_act = active_slots(L, P.idx, slots);
+    int64_t n_units = 0;
+    {
+        const int64_t tiles_r = (L.ff + P.tr_routed - 1) / P.tr_routed;
+        const int64_t tiles_s = (L.ff + P.tr_shared - 1) / P.tr_shared;
+        for (int a = 0; a < n_act; a++) n_units += (slots[a] < L.topk) ? tiles_r : tiles_s;
+    }
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P.stages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], n_cons);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == n_cons) {
+        if (lane == 0) {
+            int64_t k = 0;
+            for (int64_t u = blockIdx.x; u < n_units; u += gridDim.x, k++) {
+                const int st = (int)(k % P.stages);
+                if (k >= P.stages && !mbar_wait(&empty[st], (uint32_t)(((k / P.stages) - 1) & 1), L.err)) break;
+                int slot, nr, tg, tu;
+                int64_t r0, rbg, rbu;
+                const uint8_t *gs, *us;
+                gu_unit(P, slots, n_act, u, slot, r0, nr, gs, us, rbg, rbu, tg, tu);
+                const ByteRange rg{gs, (uint32_t)(nr * rbg)}, ru{us, (uint32_t)(nr * rbu)};
+                uint8_t *dst = stage0 + (size_t)st * P.slot_bytes;
+                mbar_arrive_expect_tx(&full[st], range_copy_bytes(rg) + range_copy_bytes(ru));
+                range_issue(dst, rg, &full[st]);
+                range_issue(dst + P.up_off, ru, &full[st]);
+            }
+            const int64_t issued = k;
+            for (int64_t j = (issued > P.stages ? issued - P.stages : 0); j < issued; j++)
+                mbar_wait(&full[j % P.stages], (uint32_t)((j / P.stages) & 1), nullptr);
+        }
+        return;
+    }
+
+    const int grp = warp / P.nwc, cw = warp % P.nwc, p = lane & 7;
+    const int sb = 4 * cw + (lane >> 3);
+    XPart xp;
+    load_xpart(xp, P.x, L.hidden, sb, p);
+    const int my_row = rs_row<kTRG>(lane);
+
+    int64_t k = 0;
+    for (int64_t u = blockIdx.x; u < n_units; u += gridDim.x, k++) {
+        const int st = (int)(k % P.stages);
+        if (!mbar_wait(&full[st], (uint32_t)((k / P.stages) & 1), L.err)) break;
+        int slot, nr, tg, tu;
+        int64_t r0, rbg, rbu;
+        const uint8_t *gs, *us;
+        gu_unit(P, slots, n_act, u, slot, r0, nr, gs, us, rbg, rbu, tg, tu);
+        const uint8_t *dst = stage0 + (size_t)st * P.slot_bytes;
+        float acc[kTRG];
+        if (grp == 0) rows_dot_any<kTRG>(tg, range_data(dst, ByteRange{gs, 0}), rbg, nr, sb, p, xp, L.hidden, acc);
+        else rows_dot_any<kTRG>(tu, range_data(dst + P.up_off, ByteRange{us, 0}), rbu, nr, sb, p, xp, L.hidden, acc);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        warp_reduce_scatter<kTRG>(acc, lane);
+        if ((lane & 3) == 0) red[(grp * P.nwc + cw) * kTRG + my_row] = acc[0];
+        consumer_sync(n_cons * 32);
+        const int t = threadIdx.x;
+        if (t < nr) {
+            float gsum = 0.0f, usum = 0.0f;
+            for (int c = 0; c < P.nwc; c++) {
+                gsum += red[c * kTRG + t];
+                usum += red[(P.nwc + c) * kTRG + t];
+            }
+            const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, (float)exp(-(double)gsum)));
+            float hv = __fmul_rn(__fmul_rn(gsum, sig), usum);
+            if (slot >= L.topk) hv = __fmul_rn(hv, P.weights[slot]);   // shared: gamma inside h
+            P.h[(int64_t)slot * L.ff + r0 + t] = hv;
+        }
+        consumer_sync(n_cons * 32);
+    }
+}
+
+// ============================================================== down + combine
+struct DnParams {
+    MoeDev L;
+    const int32_t *idx;
+    const float *weights;
+    const float *h;          // [slots, ff]
+    float *out;              // [hidden]            (combine mode)
+    float *slots_out;        // [slots, hidden]     (slot mode) or nullptr
+    int nwc;                 // column warps (ceil(nsb_ff / 4))
+    int stages;
+    uint32_t slot_bytes;
+    int64_t n_units;
+};
+
+__global__ void __launch_bounds__(17 * 32, 1) k_down(const DnParams P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_cons = kDnSlotGroups * P.nwc;
+    const MoeDev &L = P.L;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kDnStagesMax;
+    float *red = reinterpret_cast<float *>(smem + 256);   // [kMaxSlots][nwc][kTRD]
+    uint8_t *stage0 = smem + 256 + ((kMaxSlots * 16 * kTRD * 4 + 127) & ~127);
+
+    int slots[kMaxSlots];
+    const int n_act = active_slots(L, P.idx, slots);
+    // per-active-slot source base, row bytes, type and stage offset
+    const uint8_t *sbase[kMaxSlots];
+    int64_t srb[kMaxSlots];
+    int stype[kMaxSlots];
+    uint32_t soff[kMaxSlots];
+    {
+        uint32_t off = 0;
+        for (int a = 0; a < n_act; a++) {
+            const int s = slots[a];
+            if (s < L.topk) {
+                sbase[a] = L.down + local_expert(L, P.idx[s]) * L.down_stride;
+                srb[a] = L.rb_down; stype[a] = L.down_type;
+            } else {
+                sbase[a] = L.sh_down + (int64_t)(s - L.topk) * L.sh_down_stride;
+                srb[a] = L.rb_sh_down; stype[a] = L.sh_down_type;
+            }
+            soff[a] = off;
+            off += slot_bytes_for((uint64_t)kTRD * srb[a]);
+        }
+    }
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P.stages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], n_cons);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == n_cons) {
+        if (lane == 0) {
+            int64_t k = 0;
+            for (int64_t u = blockIdx.x; u < P.n_units; u += gridDim.x, k++) {
+                const int st = (int)(k % P.stages);
+                if (k >= P.stages && !mbar_wait(&empty[st], (uint32_t)(((k / P.stages) - 1) & 1), L.err)) break;
+                const int64_t r0 = u * kTRD;
+                const int nr = (int)imin64(kTRD, L.hidden - r0);
+                uint32_t tx = 0;
+                for (int a = 0; a < n_act; a++) tx += range_copy_bytes(ByteRange{sbase[a] + r0 * srb[a], (uint32_t)(nr * srb[a])});
+                mbar_arrive_expect_tx(&full[st], tx);
+                uint8_t *dst = stage0 + (size_t)st * P.slot_bytes;
+                for (int a = 0; a < n_act; a++)
+                    range_issue(dst + soff[a], ByteRange{sbase[a] + r0 * srb[a], (uint32_t)(nr * srb[a])}, &full[st]);
+            }
+            const int64_t issued = k;
+            for (int64_t j = (issued > P.stages ? issued - P.stages : 0); j < issued; j++)
+                mbar_wait(&full[j % P.stages], (uint32_t)((j / P.stages) & 1), nullptr);
+        }
+        return;
+    }
+
+    const int sg = warp / P.nwc, cw = warp % P.nwc, p = lane & 7;
+    const int sb = 4 * cw + (lane >> 3);
+    // this warp's slots: active indices a = sg, sg + G, ...
+    XPart xp[kDnSPW];
+#pragma unroll
+    for (int q = 0; q < kDnSPW; q++) {
+        const int a = sg + q * kDnSlotGroups;
+        if (a < n_act) load_xpart(xp[q], P.h + (int64_t)slots[a] * L.ff, L.ff, sb, p);
+    }
+    const int my_row = rs_row<kTRD>(lane);
+
+    int64_t k = 0;
+    for (int64_t u = blockIdx.x; u < P.n_units; u += gridDim.x, k++) {
+        const int st = (int)(k % P.stages);
+        if (!mbar_wait(&full[st], (uint32_t)((k / P.stages) & 1), L.err)) break;
+        const int64_t r0 = u * kTRD;
+        const int nr = (int)imin64(kTRD, L.hidden - r0);
+        const uint8_t *dst = stage0 + (size_t)st * P.slot_bytes;
+        float acc[kDnSPW][kTRD];
+#pragma unroll
+        for (int q = 0; q < kDnSPW; q++) {
+            const int a = sg + q * kDnSlotGroups;
+            if (a < n_act) {
+                rows_dot_any<kTRD>(stype[a], range_data(dst + soff[a], ByteRange{sbase[a] + r0 * srb[a], 0}), srb[a],
+                                   nr, sb, p, xp[q], L.ff, acc[q]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+#pragma unroll
+        for (int q = 0; q < kDnSPW; q++) {
+            const int a = sg + q * kDnSlotGroups;
+            if (a < n_act) {
+                warp_reduce_scatter<kTRD>(acc[q], lane);
+                if ((lane & 7) == 0) red[(a * P.nwc + cw) * kTRD + my_row] = acc[q][0];
+            }
+        }
+        consumer_sync(n_cons * 32);
+        const int t = threadIdx.x;
+        if (t < nr) {
+            float o = 0.0f;
+            int a = 0;
+            const int n_slots = L.topk + L.n_shared;
+            for (int s = 0; s < n_slots; s++) {
+                float term = 0.0f;
+                if (a < n_act && slots[a] == s) {
+                    float e = 0.0f;
+                    for (int c = 0; c < P.nwc; c++) e += red[(a * P.nwc + c) * kTRD + t];
+                    term = (s < L.topk) ? __fmul_rn(e, P.weights[s]) : e;
+                    a++;
+                    if (!P.slots_out) o = __fadd_rn(o, term);
+                }
+                if (P.slots_out) P.slots_out[(int64_t)s * L.hidden + r0 + t] = term;
+            }
+            if (!P.slots_out) P.out[r0 + t] = o;
+        }
+        consumer_sync(n_cons * 32);
+    }
+}
+
+// out[r] = sum over slots in order (after an all-reduce of the slot terms).
+__global__ void k_combine(const float *slots, int n_slots, int64_t hidden, float *out) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= hidden) return;
+    float o = 0.0f;
+    for (int s = 0; s < n_slots; s++) o = __fadd_rn(o, slots[(int64_t)s * hidden + r]);
+    out[r] = o;
+}
+
+// ============================================================== host side
+static int to_dev(const SepiaMoeLayer *in, MoeDev &L) {
+    if (!in) return fail("moe: null layer");
+    L.hidden = in->hidden; L.ff = in->ff;
+    L.n_routed = in->n_routed; L.n_shared = in->n_shared; L.topk = in->topk;
+    L.route_scale = in->route_scale; L.global_scale = in->global_scale;
+    L.router_w = in->router_w; L.router_bias = in->router_bias;
+    L.gate_type = in->gate_type; L.up_type = in->up_type; L.down_type = in->down_type;
+    L.sh_gate_type = in->sh_gate_type; L.sh_up_type = in->sh_up_type; L.sh_down_type = in->sh_down_type;
+    L.gate = (const uint8_t *)in->gate; L.up = (const uint8_t *)in->up; L.down = (const uint8_t *)in->down;
+    L.sh_gate = (const uint8_t *)in->sh_gate; L.sh_up = (const uint8_t *)in->sh_up; L.sh_down = (const uint8_t *)in->sh_down;
+    L.gate_stride = in->gate_stride; L.up_stride = in->up_stride; L.down_stride = in->down_stride;
+    L.sh_gate_stride = in->sh_gate_stride; L.sh_up_stride = in->sh_up_stride; L.sh_down_stride = in->sh_down_stride;
+    L.rank = in->rank; L.world = in->world < 1 ? 1 : in->world;
+    L.expert_slot = in->expert_slot;
+    L.err = dev_info().err;
+    if (L.hidden <= 0 || L.ff <= 0 || L.n_routed <= 0 || L.topk <= 0 || L.topk > L.n_routed || L.n_shared < 0 ||
+        L.topk + L.n_shared > kMaxSlots || L.n_routed > 1024)
+        return fail("moe: bad geometry hidden=%lld ff=%lld routed=%d shared=%d topk=%d (max %d slots, 1024 experts)",
+                    (long long)L.hidden, (long long)L.ff, L.n_routed, L.n_shared, L.topk, kMaxSlots);
+    if (L.rank < 0 || L.rank >= L.world) return fail("moe: rank %d outside world %d", L.rank, L.world);
+    if (!L.router_w || !L.router_bias) return fail("moe: router weights missing");
+    L.rb_gate = host_row_bytes(L.gate_type, L.hidden);
+    L.rb_up = host_row_bytes(L.up_type, L.hidden);
+    L.rb_down = host_row_bytes(L.down_type, L.ff);
+    if (L.rb_gate <= 0 || L.rb_up <= 0 || L.rb_down <= 0) return fail("moe: unsupported routed expert types/dims");
+    if (L.n_shared > 0) {
+        L.rb_sh_gate = host_row_bytes(L.sh_gate_type, L.hidden);
+        L.rb_sh_up = host_row_bytes(L.sh_up_type, L.hidden);
+        L.rb_sh_down = host_row_bytes(L.sh_down_type, L.ff);
+        if (L.rb_sh_gate <= 0 || L.rb_sh_up <= 0 || L.rb_sh_down <= 0) return fail("moe: unsupported shared expert types/dims");
+    } else {
+        L.rb_sh_gate = L.rb_sh_up = L.rb_sh_down = 0;
+    }
+    if ((L.hidden + kQK - 1) / kQK > 64 || (L.ff + kQK - 1) / kQK > 16)
+        return fail("moe: hidden <= 16384 and ff <= 4096 supported (hidden=%lld ff=%lld)", (long long)L.hidden, (long long)L.ff);
+    return 1;
+}
+
+static int pick_tr(int64_t rb_pair, int64_t budget) {
+    int tr = kTRG;
+    while (tr > 1 && (int64_t)tr * rb_pair > budget) tr >>= 1;
+    return tr;
+}
+
+int launch_router(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaStream_t st) {
+    const int n_total = L.n_routed + L.n_shared;
+    const int grid = (n_total + kRouterWarps - 1) / kRouterWarps;
+    k_router<<<grid, kRouterWarps * 32, 0, st>>>(L, x, ws->logits, ws->topk_idx, ws->weights, ws->counter);
+    return check(cudaGetLastError(), "moe router launch");
+}
+
+int launch_gateup(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaStream_t st) {
+    DevInfo &di = dev_info();
+    GuParams G;
+    G.L = L; G.x = x; G.idx = ws->topk_idx; G.weights = ws->weights; G.h = ws->h;
+    G.nwc = (int)((L.hidden + kQK - 1) / kQK + 3) / 4;
+    if (2 * G.nwc > 16) return fail("moe: hidden %lld too large for the gate/up kernel (max 8192)", (long long)L.hidden);
+    const int64_t budget = 40 * 1024;
+    G.tr_routed = pick_tr(L.rb_gate + L.rb_up, budget);
+    G.tr_shared = L.n_shared ? pick_tr(L.rb_sh_gate + L.rb_sh_up, budget) : G.tr_routed;
+    const uint32_t sr_g = slot_bytes_for((uint64_t)G.tr_routed * L.rb_gate), sr_u = slot_bytes_for((uint64_t)G.tr_routed * L.rb_up);
+    const uint32_t ss_g = L.n_shared ? slot_bytes_for((uint64_t)G.tr_shared * L.rb_sh_gate) : 0;
+    const uint32_t ss_u = L.n_shared ? slot_bytes_for((uint64_t)G.tr_shared * L.rb_sh_up) : 0;
+    G.up_off = std::max(sr_g, ss_g);
+    G.slot_bytes = G.up_off + std::max(sr_u, ss_u);
+    const int head_g = 256 + ((2 * 16 * kTRG * 4 + 127) & ~127);
+    G.stages = kGuStagesMax;
+    while (G.stages > 2 && head_g + (int64_t)G.stages * G.slot_bytes > di.smem_optin) G.stages--;
+    const int64_t smem_g = head_g + (int64_t)G.stages * G.slot_bytes;
+    if (smem_g > di.smem_optin) return fail("moe: gate/up tile needs %lld B of shared memory", (long long)smem_g);
+    if (!ensure_smem((const void *)k_gateup, (int)smem_g)) return 0;
+    const int n_slots = L.topk + L.n_shared;
+    const int64_t max_units = (int64_t)n_slots * ((L.ff + G.tr_routed - 1) / std::min(G.tr_routed, G.tr_shared));
+    const int grid_g = (int)std::min<int64_t>(max_units, di.sm_count);
+    k_gateup<<<grid_g, (2 * G.nwc + 1) * 32, (size_t)smem_g, st>>>(G);
+    return check(cudaGetLastError(), "moe gate/up launch");
+}
+
+int launch_down(const MoeDev &L, const SepiaMoeWork *ws, float *out, float *slots_out, cudaStream_t st) {
+    DevInfo &di = dev_info();
+    const int n_slots = L.topk + L.n_shared;
+    DnParams D;
+    D.L = L; D.idx = ws->topk_idx; D.weights = ws->weights; D.h = ws->h; D.out = out; D.slots_out = slots_out;
+    D.nwc = (int)((L.ff + kQK - 1) / kQK + 3) / 4;
+    if (kDnSlotGroups * D.nwc > 16) return fail("moe: ff %lld too large for the down kernel (max 4096)", (long long)L.ff);
+    if (n_slots > kDnSlotGroups * kDnSPW) return fail("moe: topk + n_shared = %d > %d", n_slots, kDnSlotGroups * kDnSPW);
+    // worst-case stage: every slot active, each with its own row bytes
+    uint64_t sbytes = 0;
+    for (int s = 0; s < n_slots; s++)
+        sbytes += slot_bytes_for((uint64_t)kTRD * (s < L.topk ? L.rb_down : L.rb_sh_down));
+    D.slot_bytes = (uint32_t)sbytes;
+    const int head_d = 256 + ((kMaxSlots * 16 * kTRD * 4 + 127) & ~127);
+    D.stages = kDnStagesMax;
+    while (D.stages > 2 && head_d + (int64_t)D.stages * D.slot_bytes > di.smem_optin) D.stages--;
+    const int64_t smem_d = head_d + (int64_t)D.stages * D.slot_bytes;
+    if (smem_d > di.smem_optin) return fail("moe: down tile needs %lld B of shared memory", (long long)smem_d);
+    if (!ensure_smem((const void *)k_down, (int)smem_d)) return 0;
+    D.n_units = (L.hidden + kTRD - 1) / kTRD;
+    const int grid_d = (int)std::min<int64_t>(D.n_units, di.sm_count);
+    k_down<<<grid_d, (kDnSlotGroups * D.nwc + 1) * 32, (size_t)smem_d, st>>>(D);
+    return check(cudaGetLastError(), "moe down launch");
+}
+
+int launch_experts(const MoeDev &L, const float *x, const SepiaMoeWork *ws, float *out, float *slots_out,
+                   cudaStream_t st) {
+    return launch_gateup(L, x, ws, st) && launch_down(L, ws, out, slots_out, st);
+}
+
+}  // namespace sepia
+
+using namespace sepia;
+
+extern "C" size_t sepia_cuda_moe_work_bytes(const SepiaMoeLayer *L) {
+    if (!L) return 0;
+    const size_t n_total = (size_t)L->n_routed + (size_t)L->n_shared;
+    const size_t n_slots = (size_t)L->topk + (size_t)L->n_shared;
+    size_t b = 0;
+    auto add = [&](size_t n) { b += (n + 255) & ~(size_t)255; };
+    add(n_total * 4);                 // logits
+    add((size_t)L->topk * 4);         // topk_idx
+    add(n_slots * 4);                 // weights
+    add(n_slots * (size_t)L->ff * 4); // h
+    add(n_slots * (size_t)L->hidden * 4);  // slots
+    add(256);                         // counter
+    return b;
+}
+
+extern "C" int sepia_cuda_moe_work_carve(const SepiaMoeLayer *L, void *base, size_t bytes, SepiaMoeWork *ws) {
+    if (!L || !base || !ws) return fail("moe_work_carve: null argument");
+    if (bytes < sepia_cuda_moe_work_bytes(L)) return fail("moe_work_carve: %zu bytes < %zu needed", bytes, sepia_cuda_moe_work_bytes(L));
+    if (reinterpret_cast<uintptr_t>(base) & 255) return fail("moe_work_carve: base must be 256-byte aligned");
+    const size_t n_total = (size_t)L->n_routed + (size_t)L->n_shared;
+    const size_t n_slots = (size_t)L->topk + (size_t)L->n_shared;
+    uint8_t *p = (uint8_t *)base;
+    auto take = [&](size_t n) { uint8_t *r = p; p += (n + 255) & ~(size_t)255; return r; };
+    ws->logits = (float *)take(n_total * 4);
+    ws->topk_idx = (int32_t *)take((size_t)L->topk * 4);
+    ws->weights = (float *)take(n_slots * 4);
+    ws->h = (float *)take(n_slots * (size_t)L->ff * 4);
+    ws->slots = (float *)take(n_slots * (size_t)L->hidden * 4);
+    ws->counter = (unsigned int *)take(256);
+    return 1;
+}
+
+extern "C" int sepia_cuda_moe_router(const SepiaMoeLayer *Lh, const float *x, const SepiaMoeWork *ws, void *stream) {
+    MoeDev L;
+    if (!to_dev(Lh, L)) return 0;
+    if (!x || !ws) return fail("moe_router: null argument");
+    return launch_router(L, x, ws, as_stream(stream));
+}
+
+extern "C" int sepia_cuda_moe_experts(const SepiaMoeLayer *Lh, const float *x, const SepiaMoeWork *ws, float *out,
+                                      int write_slots, void *stream) {
+    MoeDev L;
+    if (!to_dev(Lh, L)) return 0;
+    if (!x || !ws || (!out && !write_slots)) return fail("moe_experts: null argument");
+    return launch_experts(L, x, ws, out, write_slots ? ws->slots : nullptr, as_stream(stream));
+}
+
+extern "C" int sepia_cuda_moe_gateup(const SepiaMoeLayer *Lh, const float *x, const SepiaMoeWork *ws, void *stream) {
+    MoeDev L;
+    if (!to_dev(Lh, L)) return 0;
+    if (!x || !ws) return fail("moe_gateup: null argument");
+    return launch_gateup(L, x, ws, as_stream(stream));
+}
+
+extern "C" int sepia_cuda_moe_down(const SepiaMoeLayer *Lh, const SepiaMoeWork *ws, float *out, int write_slots,
+                                   void *stream) {
+    MoeDev L;
+    if (!to_dev(Lh, L)) return 0;
+    if (!ws || (!out && !write_slots)) return fail("moe_down: null argument");
+    return launch_down(L, ws, out, write_slots ? ws->slots : nullptr, as_stream(stream));
+}
+
+extern "C" int sepia_cuda_moe_combine(const SepiaMoeLayer *Lh, const SepiaMoeWork *ws, float *out, void *stream) {
+    if (!Lh || !ws || !out) return fail("moe_combine: null argument");
+    const int n_slots = Lh->topk + Lh->n_shared;
+    const int threads = 256;
+    k_combine<<<(unsigned)((Lh->hidden + threads - 1) / threads), threads, 0, as_stream(stream)>>>(ws->slots, n_slots,
+                                                                                                  Lh->hidden, out);
+    return check(cudaGetLastError(), "moe combine launch");
+}
+
+extern "C" int sepia_cuda_moe_layer(const SepiaMoeLayer *Lh, const float *x, const SepiaMoeWork *ws, float *out,
+                                    void *stream) {
+    MoeDev L;
+    if (!to_dev(Lh, L)) return 0;
+    if (!x || !ws || !out) return fail("moe_layer: null argument");
+    cudaStream_t st = as_stream(stream);
+    if (!launch_router(L, x, ws, st)) return 0;
+    return launch_experts(L, x, ws, out, nullptr, st);
+}
+
+extern "C" int sepia_cuda_topk_select(const float *scores, int32_t n, int32_t topk, int32_t *idx, void *stream) {
+    if (!scores || !idx || n <= 0 || topk <= 0 || topk > n) return fail("topk_select: bad arguments");
+    k_topk<<<1, 32, 0, as_stream(stream)>>>(scores, n, topk, idx);
+    return check(cudaGetLastError(), "topk launch");
+}

@@ -1,0 +1,102 @@
+"""GPU: banded attention against the oracle's restatement of
+attn_forward_chunk's inner loop (src/sepia.c:1210-1262), on the edge cases the
+reference's --gpu-compare-attn harness builds (src/sepia.c:5246-5254):
+T=1 decode, prefill chunks, band edge mid-chunk, sliding windows, tau != 1 at
+a large position, GQA; plus BASELINE configuration 4 (H=64, Hkv=8, Dh=128,
+fp16 K/V, windows 4096 / global, rel_extent 256) at reduced context."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+def make_case(rng, T, H, Hkv, Dh, E, base, window, tau_v, f16=False):
+    kv_dim = Hkv * Dh
+    cap = base + T
+    q = rng.standard_normal(T * H * Dh).astype(np.float32) * 4
+    k = rng.standard_normal(cap * kv_dim).astype(np.float32)
+    v = rng.standard_normal(cap * kv_dim).astype(np.float32)
+    if f16:
+        k = k.astype(np.float16).astype(np.float32)
+        v = v.astype(np.float16).astype(np.float32)
+    rl = (rng.standard_normal(T * H * E) * 0.5).astype(np.float32) if E else np.zeros(1, np.float32)
+    pos = base + np.arange(T)
+    lo = np.maximum(0, pos - window + 1) if window else np.zeros(T, np.int64)
+    lo = lo.astype(np.int64)
+    hi = pos.astype(np.int64)
+    tau = np.full(T, tau_v, np.float32)
+    return dict(q=q, k=k, v=v, rl=rl, lo=lo, hi=hi, tau=tau, T=T, H=H, Hkv=Hkv, Dh=Dh, E=E, base=base,
+                kv_dim=kv_dim)
+
+
+CASES = {
+    "decode_t1": (1, 8, 2, 64, 32, 100, 0, 1.0),
+    "prefill_chunk": (16, 4, 4, 32, 24, 0, 0, 1.0),
+    "band_edge_mid_chunk": (12, 4, 2, 32, 8, 3, 0, 1.0),
+    "sliding_window": (9, 6, 3, 48, 16, 200, 64, 1.0),
+    "tau_far_position": (2, 8, 1, 128, 64, 3000, 0, 1.37),
+    "no_band": (3, 4, 2, 16, 0, 40, 0, 1.0),
+    "dh_odd": (4, 6, 2, 40, 10, 70, 32, 1.0),
+}
+
+
+def run_gpu(c, f16=False):
+    import torch
+    from sepia_b200 import ops
+    dev = lambda a, dt=None: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    k, v = dev(c["k"]), dev(c["v"])
+    if f16:
+        k, v = k.half(), v.half()
+    out = ops.banded_attn(dev(c["q"]), k, v, dev(c["rl"]) if c["E"] else None, dev(c["lo"]), dev(c["hi"]),
+                          dev(c["tau"]), c["T"], c["H"], c["Hkv"], c["Dh"], c["E"], c["base"], c["kv_dim"],
+                          1.0 / c["Dh"])
+    return out.cpu().numpy()
+
+
+def run_oracle(oracle, c):
+    return oracle.banded_attn(c["q"], c["k"], c["v"], c["rl"], c["lo"], c["hi"], c["tau"], c["T"], c["H"],
+                              c["Hkv"], c["Dh"], c["E"], c["base"], c["kv_dim"], 1.0 / c["Dh"], nthreads=8)
+
+
+@pytest.mark.parametrize("name", list(CASES))
+@pytest.mark.parametrize("f16", [False, True])
+def test_banded_attn_cases(lib, oracle, name, f16):
+    rng = np.random.default_rng(abs(hash(name)) % 1000)
+    c = make_case(rng, *CASES[name], f16=f16)
+    assert oracle.rel_err(run_gpu(c, f16), run_oracle(oracle, c)) <= TOL
+
+
+@pytest.mark.parametrize("window", [4096, 0])
+def test_config4_shape(lib, oracle, window):
+    rng = np.random.default_rng(4)
+    c = make_case(rng, 1, 64, 8, 128, 256, 6000, window, 1.0 if window else 1.21, f16=True)
+    assert oracle.rel_err(run_gpu(c, True), run_oracle(oracle, c)) <= TOL
+
+
+def test_abi_banded_attn_and_rel_project(lib, oracle):
+    from test_gpu_abi import get, put
+    G = lib
+    assert G.sepia_gpu_init(b"metal") == 1
+    rng = np.random.default_rng(8)
+    c = make_case(rng, 5, 8, 2, 64, 16, 20, 0, 1.1)
+    T, H, d_rel, E = c["T"], c["H"], 16, c["E"]
+    r_vec = rng.standard_normal(T * H * d_rel).astype(np.float32)
+    rel_proj = (rng.standard_normal(d_rel * E) * 0.1).astype(np.float32)
+    rl_want = oracle.rel_project(r_vec, rel_proj, T, H, d_rel, E)
+    c["rl"] = rl_want
+    bq, bk, bv = put(G, c["q"]), put(G, c["k"]), put(G, c["v"])
+    brv, brp = put(G, r_vec), put(G, np.concatenate([np.zeros(4, np.float32), rel_proj]))
+    brl, bo = put(G, np.zeros(T * H * E, np.float32)), put(G, np.zeros(T * H * c["Dh"], np.float32))
+    lo = np.ascontiguousarray(c["lo"], np.int64)
+    hi = np.ascontiguousarray(c["hi"], np.int64)
+    tau = np.ascontiguousarray(c["tau"], np.float32)
+    assert G.sepia_gpu_begin() == 1
+    assert G.sepia_gpu_rel_project_off(brv, brp, 16, brl, T, H, d_rel, E) == 1
+    assert G.sepia_gpu_banded_attn(bq, bk, bv, brl, bo, lo.ctypes.data, hi.ctypes.data, tau.ctypes.data, T, H,
+                                   c["Hkv"], c["Dh"], E, c["base"], c["kv_dim"], np.float32(1.0 / c["Dh"])) == 1
+    assert G.sepia_gpu_end() == 1
+    assert oracle.rel_err(get(G, brl, T * H * E), rl_want) <= 1e-6
+    assert oracle.rel_err(get(G, bo, T * H * c["Dh"]), run_oracle(oracle, c)) <= TOL

@@ -1,0 +1,123 @@
+"""GPU: the device-resident MoE layer against the oracle's mlp_moe_forward
+restatement (src/sepia.c:1377-1470, router src/sepia.c:1329-1375).
+
+Router ids must match exactly; expert outputs within max relative error 1e-4.
+Expert sharding (world > 1) must reproduce the world = 1 result bit for bit.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from sepia_b200 import quants as Q
+from sepia_b200.synth import MoeShape, hidden_state, moe_layer_host
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+SHAPES = {
+    "baseline_types_small": MoeShape(hidden=1024, ff=512, n_routed=64),
+    "baseline_types_full_dims": MoeShape(hidden=7168, ff=2048, n_routed=12),
+    "inkling_real_types": MoeShape(hidden=6144, ff=3072, n_routed=12, gate_type=Q.IQ2_XS, up_type=Q.IQ2_XS,
+                                   down_type=Q.IQ3_XXS, sh_gate_type=Q.Q5_K, sh_up_type=Q.Q5_K,
+                                   sh_down_type=Q.Q6_K),
+    "iq4_down_q8_shared": MoeShape(hidden=2048, ff=1024, n_routed=16, gate_type=Q.IQ2_XS, up_type=Q.IQ2_XS,
+                                   down_type=Q.IQ4_XS, sh_gate_type=Q.Q8_0, sh_up_type=Q.Q8_0,
+                                   sh_down_type=Q.Q8_0),
+    "no_shared_topk8": MoeShape(hidden=1024, ff=256, n_routed=32, n_shared=0, topk=8),
+}
+
+
+@pytest.fixture(scope="module")
+def layers(lib):
+    import torch
+    from sepia_b200.moe import MoeLayerDevice
+    out = {}
+    for name, shape in SHAPES.items():
+        H = moe_layer_host(shape, seed=5)
+        out[name] = (H, MoeLayerDevice.from_host(H))
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.parametrize("name", list(SHAPES))
+def test_moe_layer_vs_oracle(layers, oracle, name):
+    import torch
+    H, D = layers[name]
+    for seed in (1, 2, 3, 17, 64):
+        x = hidden_state(seed, H.hidden)
+        want, logits, idx, w = oracle.moe_layer(H, x, nthreads=8)
+        xd = torch.from_numpy(x).cuda()
+        out = torch.empty(H.hidden, dtype=torch.float32, device="cuda")
+        D.forward(xd, out)
+        torch.cuda.synchronize()
+        assert np.array_equal(D.topk_idx.cpu().numpy(), idx), (name, seed)
+        assert oracle.rel_err(D.logits.cpu().numpy(), logits) <= 1e-6
+        assert oracle.rel_err(D.weights.cpu().numpy(), w) <= 1e-5
+        assert oracle.rel_err(out.cpu().numpy(), want) <= TOL, (name, seed)
+
+
+def test_router_bitexact_logits(layers, oracle):
+    """fp64-accumulated router logits round to the same floats as dotf."""
+    import torch
+    H, D = layers["baseline_types_full_dims"]
+    for seed in range(1, 9):
+        x = hidden_state(seed, H.hidden)
+        want = oracle.linear(H.router_w, x)
+        D.forward(torch.from_numpy(x).cuda(), torch.empty(H.hidden, device="cuda"))
+        torch.cuda.synchronize()
+        got = D.logits.cpu().numpy()
+        assert np.count_nonzero(got.view(np.uint32) != want.view(np.uint32)) <= 1
+
+
+def test_topk_select_ties(lib, oracle):
+    import torch
+    from sepia_b200 import ops
+    rng = np.random.default_rng(0)
+    for trial in range(20):
+        s = rng.integers(0, 5, size=256).astype(np.float32) / 4   # many exact ties
+        want = oracle.topk_scores(s, 6)
+        got = ops.topk_select(torch.from_numpy(s).cuda(), 6).cpu().numpy()
+        assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+def test_expert_sharding_bit_identical(layers, world):
+    """Each rank computes its own experts into slot terms; summing the slot
+    buffers (what the NCCL all-reduce does) and combining reproduces the
+    single-GPU output exactly. Ranks are emulated one after another on one GPU."""
+    import torch
+    from sepia_b200.lib import load, ok
+    from sepia_b200.moe import MoeLayerDevice
+    H, D1 = layers["baseline_types_small"]
+    ranks = [MoeLayerDevice.from_host(H, rank=r, world=world) for r in range(world)]
+    L = load()
+    for seed in (4, 9, 33):
+        x = torch.from_numpy(hidden_state(seed, H.hidden)).cuda()
+        ref = torch.empty(H.hidden, device="cuda")
+        D1.forward(x, ref)
+        total = torch.zeros_like(ranks[0].slots)
+        for R in ranks:
+            st = torch.cuda.current_stream().cuda_stream
+            ok(L.sepia_cuda_moe_router(C.byref(R.struct), x.data_ptr(), C.byref(R.ws), st))
+            ok(L.sepia_cuda_moe_experts(C.byref(R.struct), x.data_ptr(), C.byref(R.ws), None, 1, st))
+            total += R.slots
+        R0 = ranks[0]
+        R0.slots.copy_(total)
+        out = torch.empty(H.hidden, device="cuda")
+        ok(L.sepia_cuda_moe_combine(C.byref(R0.struct), C.byref(R0.ws), out.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int32), ref.view(torch.int32)), seed
+
+
+def test_repeat_is_deterministic(layers):
+    import torch
+    H, D = layers["baseline_types_full_dims"]
+    x = torch.from_numpy(hidden_state(7, H.hidden)).cuda()
+    a = torch.empty(H.hidden, device="cuda")
+    b = torch.empty(H.hidden, device="cuda")
+    D.forward(x, a)
+    D.forward(x, b)
+    torch.cuda.synchronize()
+    assert torch.equal(a.view(torch.int32), b.view(torch.int32))
