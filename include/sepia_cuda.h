@@ -1,7 +1,8 @@
 /* include/sepia_cuda.h -- CUDA-native entry points of libsepia_cuda.so.
  *
  * These take raw device pointers and a cudaStream_t (passed as void*; NULL
- * selects the library's own stream) and are stream-ordered: nothing here
+ * is the legacy default stream, as in the CUDA runtime) and are
+ * stream-ordered: nothing here
  * synchronises, allocates, or touches host memory, so a caller may capture
  * sequences of them in a CUDA graph. They are what the reference-shaped
  * ABI in sepia_gpu.h is built on, and what bench.py and the multi-GPU

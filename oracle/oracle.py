@@ -73,7 +73,7 @@ def lib():
                                        C.c_int64, C.c_int64, C.c_float, F32P, F32P, C.c_int]
         L.or_rel_project.argtypes = [F32P, F32P, F32P, C.c_int64, C.c_int64, C.c_int64, C.c_int64]
         L.or_banded_attn.argtypes = [F32P, F32P, F32P, F32P, F32P, I64P, I64P, F32P] + \
-            [C.c_int64] * 8 + [C.c_float, C.c_int]
+            [C.c_int64] * 7 + [C.c_float, C.c_int]
         L.or_moe_layer.restype = C.c_int
         L.or_moe_layer.argtypes = [C.c_void_p, F32P, F32P, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
         L.or_f16_to_f32.restype = C.c_float

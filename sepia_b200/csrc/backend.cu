@@ -157,13 +157,16 @@ int wait_stream(const char *what) {
     if (!check(cudaEventRecord(g.done, g.stream), "cudaEventRecord")) return 0;
     double limit = 120.0;
     if (const char *e = getenv("SEPIA_CUDA_END_TIMEOUT_S")) limit = atof(e) > 0 ? atof(e) : limit;
+    // spin for the first 2 ms (decode steps finish in tens of microseconds),
+    // then back off to sleeping polls
     const double t0 = now_s();
     for (;;) {
         cudaError_t q = cudaEventQuery(g.done);
         if (q == cudaSuccess) break;
         if (q != cudaErrorNotReady) return check(q, what);
-        if (now_s() - t0 > limit) return fail("%s: device did not finish within %.0f s", what, limit);
-        usleep(20);
+        const double el = now_s() - t0;
+        if (el > limit) return fail("%s: device did not finish within %.0f s", what, limit);
+        if (el > 2e-3) usleep(50);
     }
     DevInfo &di = dev_info();
     if (di.err) {

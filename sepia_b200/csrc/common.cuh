@@ -2,6 +2,7 @@
 // error reporting, exact fp16 widening, warp reductions, and the sm_100a
 // async-copy primitives (mbarrier + cp.async.bulk) the streaming GEMVs use.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>

@@ -33,8 +33,7 @@ constexpr int kGuStagesMax = 8;
 constexpr int kDnStagesMax = 8;
 constexpr int kTRG = 8;            // max rows per gate/up unit
 constexpr int kTRD = 4;            // rows per down unit
-constexpr int kDnSlotGroups = 4;   // down consumer warp groups (slots split over them)
-constexpr int kDnSPW = 2;           // slots per down consumer warp (<= 8 slots total)
+constexpr int kDnMaxSlots = 8;     // topk + n_shared handled by the down kernel
 
 // --------------------------------------------------------------- device-side layer
 struct MoeDev {
@@ -84,25 +83,39 @@ __device__ __forceinline__ float logsigmoid_ref(float x) {
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router(const MoeDev L, const float *x, float *logits,
                                                                int32_t *topk_idx, float *weights,
                                                                unsigned int *counter) {
+    // one CTA per logit row; the 8 warps split the row into contiguous
+    // chunks and their fp64 partials are summed in warp order (deterministic)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_total = L.n_routed + L.n_shared;
-    const int row = blockIdx.x * kRouterWarps + warp;
-    if (row < n_total) {
+    const int row = blockIdx.x;
+    __shared__ double s_part[kRouterWarps];
+    {
         const float *w = L.router_w + (int64_t)row * L.hidden;
         double acc = 0.0;
-        const bool vec = ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15) == 0;
-        const int64_t n4 = vec ? (L.hidden / 4) : 0;
-        for (int64_t i = lane; i < n4; i += 32) {
-            const float4 a = __ldg(reinterpret_cast<const float4 *>(w) + i);
-            const float4 b = __ldg(reinterpret_cast<const float4 *>(x) + i);
-            acc = fma((double)a.x, (double)b.x, acc);
-            acc = fma((double)a.y, (double)b.y, acc);
-            acc = fma((double)a.z, (double)b.z, acc);
-            acc = fma((double)a.w, (double)b.w, acc);
+        const bool vec = ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15) == 0 &&
+                         (L.hidden % (4 * kRouterWarps)) == 0;
+        if (vec) {
+            const int64_t per = L.hidden / 4 / kRouterWarps;
+            const float4 *w4 = reinterpret_cast<const float4 *>(w) + warp * per;
+            const float4 *x4 = reinterpret_cast<const float4 *>(x) + warp * per;
+#pragma unroll 4
+            for (int64_t i = lane; i < per; i += 32) {
+                const float4 a4 = __ldg(w4 + i), b4 = __ldg(x4 + i);
+                acc = fma((double)a4.x, (double)b4.x, acc);
+                acc = fma((double)a4.y, (double)b4.y, acc);
+                acc = fma((double)a4.z, (double)b4.z, acc);
+                acc = fma((double)a4.w, (double)b4.w, acc);
+            }
+        } else {
+            for (int64_t i = threadIdx.x; i < L.hidden; i += blockDim.x) acc = fma((double)w[i], (double)x[i], acc);
         }
-        for (int64_t i = n4 * 4 + lane; i < L.hidden; i += 32) acc = fma((double)w[i], (double)x[i], acc);
         acc = warp_sum_d(acc);
-        if (lane == 0) logits[row] = (float)acc;
+        if (lane == 0) s_part[warp] = acc;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double t = 0.0;
+            for (int i = 0; i < kRouterWarps; i++) t += s_part[i];
+            logits[row] = (float)t;
+        }
     }
     // ---- last CTA performs the selection ----
     __shared__ unsigned int s_last;
@@ -198,37 +211,40 @@ __device__ __forceinline__ void rows_dot(const uint8_t *base, int64_t rb, int nr
         acc[i] = (i < nr) ? row_parts_dot<T, 1>(base + i * rb, sbb, sbs, p, xa, in_dim) : 0.0f;
 }
 
+// Generic rows: exact per-part decode + FFMA with UNSCALED activations
+// (any format, including the fast ones when the kernel is runtime-typed).
+template <int T, int TRW>
+__device__ __forceinline__ void rows_dot_generic(const uint8_t *base, int64_t rb, int nr, int sb, int p,
+                                                 const XPart &xp, int64_t in_dim, float (&acc)[TRW]) {
+    const int sbb = fmt_sb_bytes(T);
+    const int64_t first = (int64_t)sb * kQK + 32 * p;
+    const int nvalid = first < in_dim ? (int)imin64(32, in_dim - first) : 0;
+#pragma unroll
+    for (int i = 0; i < TRW; i++)
+        acc[i] = (i < nr && nvalid > 0) ? dot_generic(T, base + i * rb + (int64_t)sb * sbb, p, xp, nvalid) : 0.0f;
+}
+
 template <int TRW>
-__device__ __noinline__ void rows_dot_dyn(int t, const uint8_t *base, int64_t rb, int nr, int sb, int p,
-                                          const XPart &xp, int64_t in_dim, float (&acc)[TRW]) {
+__device__ __forceinline__ void rows_dot_rt(int t, const uint8_t *base, int64_t rb, int nr, int sb, int p,
+                                            const XPart &xp, int64_t in_dim, float (&acc)[TRW]) {
     switch (t) {
-    case T_F32: rows_dot<T_F32, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
-    case T_F16: rows_dot<T_F16, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
-    case T_Q8_0: rows_dot<T_Q8_0, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
-    case T_Q2_K: rows_dot<T_Q2_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
-    case T_Q3_K: rows_dot<T_Q3_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
-    case T_Q4_K: rows_dot<T_Q4_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
-    case T_Q5_K: rows_dot<T_Q5_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
-    case T_Q6_K: rows_dot<T_Q6_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
-    case T_IQ2_XXS: rows_dot<T_IQ2_XXS, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
-    case T_IQ2_XS: rows_dot<T_IQ2_XS, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
-    case T_IQ3_XXS: rows_dot<T_IQ3_XXS, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
-    case T_IQ1_S: rows_dot<T_IQ1_S, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
-    case T_IQ4_XS: rows_dot<T_IQ4_XS, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+#define SEPIA_RT_CASE(TT) case TT: rows_dot_generic<TT, TRW>(base, rb, nr, sb, p, xp, in_dim, acc); break;
+    SEPIA_RT_CASE(T_F32) SEPIA_RT_CASE(T_F16) SEPIA_RT_CASE(T_Q8_0) SEPIA_RT_CASE(T_Q2_K) SEPIA_RT_CASE(T_Q3_K)
+    SEPIA_RT_CASE(T_Q4_K) SEPIA_RT_CASE(T_Q5_K) SEPIA_RT_CASE(T_Q6_K) SEPIA_RT_CASE(T_IQ2_XXS)
+    SEPIA_RT_CASE(T_IQ2_XS) SEPIA_RT_CASE(T_IQ3_XXS) SEPIA_RT_CASE(T_IQ1_S) SEPIA_RT_CASE(T_IQ4_XS)
+#undef SEPIA_RT_CASE
     default:
         for (int i = 0; i < TRW; i++) acc[i] = 0.0f;
     }
 }
 
-// Specialised fast path for the formats of the headline configuration; any
-// other type goes through the (slower, generic) dynamic dispatcher.
-template <int TRW>
-__device__ __forceinline__ void rows_dot_any(int t, const uint8_t *base, int64_t rb, int nr, int sb, int p,
-                                             const XPart &xp, int64_t in_dim, float (&acc)[TRW]) {
-    if (t == T_Q2_K) rows_dot<T_Q2_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc);
-    else if (t == T_Q3_K) rows_dot<T_Q3_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc);
-    else if (t == T_Q4_K) rows_dot<T_Q4_K, TRW>(base, rb, nr, sb, p, xp, in_dim, acc);
-    else rows_dot_dyn<TRW>(t, base, rb, nr, sb, p, xp, in_dim, acc);
+// TK >= 0: compile-time fast format (the kernel's activations are scaled);
+// TK < 0: runtime format t through the generic decoder.
+template <int TK, int TRW>
+__device__ __forceinline__ void rows_dot_k(int t, const uint8_t *base, int64_t rb, int nr, int sb, int p,
+                                           const XPart &xp, int64_t in_dim, float (&acc)[TRW]) {
+    if constexpr (TK >= 0) rows_dot<TK, TRW>(base, rb, nr, sb, p, xp, in_dim, acc);
+    else rows_dot_rt<TRW>(t, base, rb, nr, sb, p, xp, in_dim, acc);
 }
 
 // ============================================================== gate/up + SwiGLU
@@ -278,7 +294,9 @@ __device__ __forceinline__ void gu_unit(const GuParams &P, const int (&slots)[kM
     slot = -1;
 }
 
+template <int TG, int TS>   // gate/up format of routed / shared experts; -1 = any (runtime)
 __global__ void __launch_bounds__(17 * 32, 1) k_gateup(const GuParams P) {
+    constexpr bool kScaled = TG >= 0 && TS >= 0;
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_cons = 2 * P.nwc;
@@ -332,7 +350,7 @@ __global__ void __launch_bounds__(17 * 32, 1) k_gateup(const GuParams P) {
     const int grp = warp / P.nwc, cw = warp % P.nwc, p = lane & 7;
     const int sb = 4 * cw + (lane >> 3);
     XPart xp;
-    load_xpart(xp, P.x, L.hidden, sb, p);
+    load_xpart<kScaled>(xp, P.x, L.hidden, sb, p);
     const int my_row = rs_row<kTRG>(lane);
 
     int64_t k = 0;
@@ -345,8 +363,15 @@ __global__ void __launch_bounds__(17 * 32, 1) k_gateup(const GuParams P) {
         gu_unit(P, slots, n_act, u, slot, r0, nr, gs, us, rbg, rbu, tg, tu);
         const uint8_t *dst = stage0 + (size_t)st * P.slot_bytes;
         float acc[kTRG];
-        if (grp == 0) rows_dot_any<kTRG>(tg, range_data(dst, ByteRange{gs, 0}), rbg, nr, sb, p, xp, L.hidden, acc);
-        else rows_dot_any<kTRG>(tu, range_data(dst + P.up_off, ByteRange{us, 0}), rbu, nr, sb, p, xp, L.hidden, acc);
+        const bool shared = slot >= L.topk;
+        const uint8_t *gsrc = range_data(dst, ByteRange{gs, 0}), *usrc = range_data(dst + P.up_off, ByteRange{us, 0});
+        if (grp == 0) {
+            if (shared) rows_dot_k<TS, kTRG>(tg, gsrc, rbg, nr, sb, p, xp, L.hidden, acc);
+            else rows_dot_k<TG, kTRG>(tg, gsrc, rbg, nr, sb, p, xp, L.hidden, acc);
+        } else {
+            if (shared) rows_dot_k<TS, kTRG>(tu, usrc, rbu, nr, sb, p, xp, L.hidden, acc);
+            else rows_dot_k<TG, kTRG>(tu, usrc, rbu, nr, sb, p, xp, L.hidden, acc);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
         warp_reduce_scatter<kTRG>(acc, lane);
@@ -382,10 +407,16 @@ struct DnParams {
     int64_t n_units;
 };
 
+// TD / TSD: down format of routed / shared experts (-1 = any, runtime);
+// SPW: slots per consumer warp (the slots are split over groups = 8 / SPW
+// warp groups, each warp keeps its slots' activations in registers).
+template <int TD, int TSD, int SPW>
 __global__ void __launch_bounds__(17 * 32, 1) k_down(const DnParams P) {
+    constexpr bool kScaled = TD >= 0 && TSD >= 0;
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_cons = kDnSlotGroups * P.nwc;
+    constexpr int kGroups = kDnMaxSlots / SPW;
+    const int n_cons = kGroups * P.nwc;
     const MoeDev &L = P.L;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kDnStagesMax;
@@ -449,11 +480,11 @@ __global__ void __launch_bounds__(17 * 32, 1) k_down(const DnParams P) {
     const int sg = warp / P.nwc, cw = warp % P.nwc, p = lane & 7;
     const int sb = 4 * cw + (lane >> 3);
     // this warp's slots: active indices a = sg, sg + G, ...
-    XPart xp[kDnSPW];
+    XPart xp[SPW];
 #pragma unroll
-    for (int q = 0; q < kDnSPW; q++) {
-        const int a = sg + q * kDnSlotGroups;
-        if (a < n_act) load_xpart(xp[q], P.h + (int64_t)slots[a] * L.ff, L.ff, sb, p);
+    for (int q = 0; q < SPW; q++) {
+        const int a = sg + q * kGroups;
+        if (a < n_act) load_xpart<kScaled>(xp[q], P.h + (int64_t)slots[a] * L.ff, L.ff, sb, p);
     }
     const int my_row = rs_row<kTRD>(lane);
 
@@ -464,20 +495,21 @@ __global__ void __launch_bounds__(17 * 32, 1) k_down(const DnParams P) {
         const int64_t r0 = u * kTRD;
         const int nr = (int)imin64(kTRD, L.hidden - r0);
         const uint8_t *dst = stage0 + (size_t)st * P.slot_bytes;
-        float acc[kDnSPW][kTRD];
+        float acc[SPW][kTRD];
 #pragma unroll
-        for (int q = 0; q < kDnSPW; q++) {
-            const int a = sg + q * kDnSlotGroups;
+        for (int q = 0; q < SPW; q++) {
+            const int a = sg + q * kGroups;
             if (a < n_act) {
-                rows_dot_any<kTRD>(stype[a], range_data(dst + soff[a], ByteRange{sbase[a] + r0 * srb[a], 0}), srb[a],
-                                   nr, sb, p, xp[q], L.ff, acc[q]);
+                const uint8_t *src = range_data(dst + soff[a], ByteRange{sbase[a] + r0 * srb[a], 0});
+                if (slots[a] >= L.topk) rows_dot_k<TSD, kTRD>(stype[a], src, srb[a], nr, sb, p, xp[q], L.ff, acc[q]);
+                else rows_dot_k<TD, kTRD>(stype[a], src, srb[a], nr, sb, p, xp[q], L.ff, acc[q]);
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
 #pragma unroll
-        for (int q = 0; q < kDnSPW; q++) {
-            const int a = sg + q * kDnSlotGroups;
+        for (int q = 0; q < SPW; q++) {
+            const int a = sg + q * kGroups;
             if (a < n_act) {
                 warp_reduce_scatter<kTRD>(acc[q], lane);
                 if ((lane & 7) == 0) red[(a * P.nwc + cw) * kTRD + my_row] = acc[q][0];
@@ -554,6 +586,50 @@ static int to_dev(const SepiaMoeLayer *in, MoeDev &L) {
     return 1;
 }
 
+typedef void (*GuKernel)(const GuParams);
+typedef void (*DnKernel)(const DnParams);
+
+// Kernel instances: every (routed, shared) pair of the fast formats gets a
+// specialised kernel; anything else runs the runtime-typed generic kernel.
+template <int A>
+static GuKernel gu_for_shared(int b) {
+    if (b == T_Q2_K) return k_gateup<A, T_Q2_K>;
+    if (b == T_Q3_K) return k_gateup<A, T_Q3_K>;
+    if (b == T_Q4_K) return k_gateup<A, T_Q4_K>;
+    return k_gateup<-1, -1>;
+}
+template <int A>
+static DnKernel dn_for_shared(int b) {
+    if (b == T_Q2_K) return k_down<A, T_Q2_K, 1>;
+    if (b == T_Q3_K) return k_down<A, T_Q3_K, 1>;
+    if (b == T_Q4_K) return k_down<A, T_Q4_K, 1>;
+    return k_down<-1, -1, 1>;
+}
+
+static GuKernel pick_gateup(const MoeDev &L) {
+    const int a = L.gate_type;
+    const int b = L.n_shared ? L.sh_gate_type : a;
+    const bool same = L.up_type == a && (!L.n_shared || L.sh_up_type == b);
+    if (same && fast_format(a) && fast_format(b)) {
+        if (a == T_Q2_K) return gu_for_shared<T_Q2_K>(b);
+        if (a == T_Q3_K) return gu_for_shared<T_Q3_K>(b);
+        if (a == T_Q4_K) return gu_for_shared<T_Q4_K>(b);
+    }
+    return k_gateup<-1, -1>;
+}
+
+static DnKernel pick_down(const MoeDev &L, int spw) {
+    const int a = L.down_type;
+    const int b = L.n_shared ? L.sh_down_type : a;
+    if (spw == 2) return k_down<-1, -1, 2>;
+    if (fast_format(a) && fast_format(b)) {
+        if (a == T_Q2_K) return dn_for_shared<T_Q2_K>(b);
+        if (a == T_Q3_K) return dn_for_shared<T_Q3_K>(b);
+        if (a == T_Q4_K) return dn_for_shared<T_Q4_K>(b);
+    }
+    return k_down<-1, -1, 1>;
+}
+
 static int pick_tr(int64_t rb_pair, int64_t budget) {
     int tr = kTRG;
     while (tr > 1 && (int64_t)tr * rb_pair > budget) tr >>= 1;
@@ -562,7 +638,7 @@ static int pick_tr(int64_t rb_pair, int64_t budget) {
 
 int launch_router(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaStream_t st) {
     const int n_total = L.n_routed + L.n_shared;
-    const int grid = (n_total + kRouterWarps - 1) / kRouterWarps;
+    const int grid = n_total;
     k_router<<<grid, kRouterWarps * 32, 0, st>>>(L, x, ws->logits, ws->topk_idx, ws->weights, ws->counter);
     return check(cudaGetLastError(), "moe router launch");
 }
@@ -586,11 +662,12 @@ int launch_gateup(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaS
     while (G.stages > 2 && head_g + (int64_t)G.stages * G.slot_bytes > di.smem_optin) G.stages--;
     const int64_t smem_g = head_g + (int64_t)G.stages * G.slot_bytes;
     if (smem_g > di.smem_optin) return fail("moe: gate/up tile needs %lld B of shared memory", (long long)smem_g);
-    if (!ensure_smem((const void *)k_gateup, (int)smem_g)) return 0;
+    const GuKernel kern = pick_gateup(L);
+    if (!ensure_smem((const void *)kern, (int)smem_g)) return 0;
     const int n_slots = L.topk + L.n_shared;
     const int64_t max_units = (int64_t)n_slots * ((L.ff + G.tr_routed - 1) / std::min(G.tr_routed, G.tr_shared));
     const int grid_g = (int)std::min<int64_t>(max_units, di.sm_count);
-    k_gateup<<<grid_g, (2 * G.nwc + 1) * 32, (size_t)smem_g, st>>>(G);
+    kern<<<grid_g, (2 * G.nwc + 1) * 32, (size_t)smem_g, st>>>(G);
     return check(cudaGetLastError(), "moe gate/up launch");
 }
 
@@ -600,8 +677,9 @@ int launch_down(const MoeDev &L, const SepiaMoeWork *ws, float *out, float *slot
     DnParams D;
     D.L = L; D.idx = ws->topk_idx; D.weights = ws->weights; D.h = ws->h; D.out = out; D.slots_out = slots_out;
     D.nwc = (int)((L.ff + kQK - 1) / kQK + 3) / 4;
-    if (kDnSlotGroups * D.nwc > 16) return fail("moe: ff %lld too large for the down kernel (max 4096)", (long long)L.ff);
-    if (n_slots > kDnSlotGroups * kDnSPW) return fail("moe: topk + n_shared = %d > %d", n_slots, kDnSlotGroups * kDnSPW);
+    if (n_slots > kDnMaxSlots) return fail("moe: topk + n_shared = %d > %d", n_slots, kDnMaxSlots);
+    const int spw = (8 * D.nwc <= 16) ? 1 : 2;       // one slot per warp when the warps fit
+    if ((kDnMaxSlots / spw) * D.nwc > 16) return fail("moe: ff %lld too large for the down kernel (max 4096)", (long long)L.ff);
     // worst-case stage: every slot active, each with its own row bytes
     uint64_t sbytes = 0;
     for (int s = 0; s < n_slots; s++)
@@ -612,10 +690,11 @@ int launch_down(const MoeDev &L, const SepiaMoeWork *ws, float *out, float *slot
     while (D.stages > 2 && head_d + (int64_t)D.stages * D.slot_bytes > di.smem_optin) D.stages--;
     const int64_t smem_d = head_d + (int64_t)D.stages * D.slot_bytes;
     if (smem_d > di.smem_optin) return fail("moe: down tile needs %lld B of shared memory", (long long)smem_d);
-    if (!ensure_smem((const void *)k_down, (int)smem_d)) return 0;
+    const DnKernel kern = pick_down(L, spw);
+    if (!ensure_smem((const void *)kern, (int)smem_d)) return 0;
     D.n_units = (L.hidden + kTRD - 1) / kTRD;
     const int grid_d = (int)std::min<int64_t>(D.n_units, di.sm_count);
-    k_down<<<grid_d, (kDnSlotGroups * D.nwc + 1) * 32, (size_t)smem_d, st>>>(D);
+    kern<<<grid_d, ((kDnMaxSlots / spw) * D.nwc + 1) * 32, (size_t)smem_d, st>>>(D);
     return check(cudaGetLastError(), "moe down launch");
 }
 

@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(17 * 32) k_matvec(const MvParams P) {
     XPart xp[C];
     if (P.n_vec == 1) {
 #pragma unroll
-        for (int j = 0; j < C; j++) load_xpart(xp[j], P.x, P.in_dim, sb[j], p);
+        for (int j = 0; j < C; j++) load_xpart<fast_format(T)>(xp[j],P.x, P.in_dim, sb[j], p);
     }
     const int wlane = (32 / TRW) - 1;   // lanes sharing one row after the reduce-scatter
     const int my_row = rs_row<TRW>(lane);
@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(17 * 32) k_matvec(const MvParams P) {
         for (int v = 0; v < P.n_vec; v++) {
             if (P.n_vec > 1) {
 #pragma unroll
-                for (int j = 0; j < C; j++) load_xpart(xp[j], P.x + (int64_t)v * P.in_dim, P.in_dim, sb[j], p);
+                for (int j = 0; j < C; j++) load_xpart<fast_format(T)>(xp[j],P.x + (int64_t)v * P.in_dim, P.in_dim, sb[j], p);
             }
             float acc[TRW];
 #pragma unroll

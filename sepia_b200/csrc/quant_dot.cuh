@@ -1,0 +1,190 @@
+// sepia_b200/csrc/quant_dot.cuh -- per-lane dot products of one 32-element
+// part of a quantized row with the activations the lane holds in registers.
+//
+// Exact products without integer->float conversions
+// ---------------------------------------------------
+// An unpacked quant field v (2-4 bits) that sits at bit position P of a
+// 32-bit word, with every other bit cleared, IS the IEEE single whose value
+// is v * 2^(P-149) (a subnormal: exponent field zero, the field inside the
+// mantissa). So one LOP3 (mask in place) turns packed bits into an exact
+// float, and FFMA(field, x * 2^(125-P-e), acc) adds exactly v * x * 2^-(24+e)
+// -- the same rounding as a plain fp32 dot of the dequantized integer with x.
+// The lane pre-scales its activations once per kernel ("scaled" XPart):
+// element i (byte i%4 of a packed word) is scaled for the field position
+// P = {4, 12, 20, 20}[i%4], and e is the exponent of the part's largest |x|
+// (clamped to [-2, 100]) so nothing overflows or underflows. Products come
+// out in units of 2^-(24+e); `inv` restores them. This relies on subnormal
+// FMA inputs being honoured (no -ftz / fast-math), the nvcc default.
+// Q2_K, Q3_K and Q4_K use it; the other formats decode each part to floats
+// exactly (decode_part_exact) and use unscaled activations.
+#pragma once
+#include "quant_formats.cuh"
+
+namespace sepia {
+
+__host__ __device__ constexpr bool fast_format(int t) { return t == T_Q2_K || t == T_Q3_K || t == T_Q4_K; }
+
+struct XPart {
+    float v[32];    // activations (scaled for the fast formats)
+    float s16[2];   // unscaled sums of elements 0..15 and 16..31
+    float inv;      // 2^(24+e): restores the scaled products (fast formats)
+};
+
+__device__ __forceinline__ float pow2f(int k) { return __int_as_float((127 + k) << 23); }
+
+template <bool SCALED>
+__device__ __forceinline__ void xpart_finish(XPart &x) {
+    float a = 0.f, b = 0.f, m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        a += x.v[i];
+        b += x.v[16 + i];
+        m = fmaxf(m, fmaxf(fabsf(x.v[i]), fabsf(x.v[16 + i])));
+    }
+    x.s16[0] = a;
+    x.s16[1] = b;
+    if constexpr (SCALED) {
+        int e = (m > 0.f) ? ((__float_as_int(m) >> 23) & 0xFF) - 127 : 0;
+        e = max(-2, min(e, 100));
+        x.inv = pow2f(24 + e);
+        const float s0 = pow2f(125 - 4 - e), s1 = pow2f(125 - 12 - e), s2 = pow2f(125 - 20 - e);
+#pragma unroll
+        for (int i = 0; i < 32; i++) x.v[i] *= ((i & 3) == 0) ? s0 : (((i & 3) == 1) ? s1 : s2);
+    } else {
+        x.inv = 1.0f;
+    }
+}
+
+// 8 consecutive 32-bit words at p: plain word loads when 4-byte aligned,
+// otherwise aligned loads + funnel shifts (blocks of 110/210/66/... bytes).
+__device__ __forceinline__ void rd8w(const uint8_t *p, uint32_t (&w)[8]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *base = reinterpret_cast<const uint32_t *>(a & ~(uintptr_t)3);
+    if ((a & 3) == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) w[i] = base[i];
+    } else {
+        const uint32_t sh = (uint32_t)(a & 3) * 8;
+        uint32_t prev = base[0];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t next = base[i + 1];
+            w[i] = __funnelshift_r(prev, next, sh);
+            prev = next;
+        }
+    }
+}
+
+__device__ __forceinline__ float fbits(uint32_t u) { return __uint_as_float(u); }
+
+// exact small-integer -> float (n < 2^23) without the slow conversion pipe
+__device__ __forceinline__ float u2f_small(uint32_t n) { return __uint_as_float(0x4B000000u | n) - 8388608.0f; }
+
+// ------------------------------------------------------------ Q2_K
+// part p: 32 consecutive qs bytes (half p>>2), 2-bit field at shift
+// s = 2(p&3); two 16-element groups with (scale, min) nibbles.
+__device__ __forceinline__ float dot_q2_k(const uint8_t *b, int p, const XPart &x) {
+    const float d = cvt16<true>(rd16(b + 80)), dmin = cvt16<true>(rd16(b + 82));
+    const uint32_t rot = (uint32_t)(4 - 2 * (p & 3)) & 31u;     // field -> bits 4..5 of each byte
+    uint32_t w[8];
+    rd8w(b + 16 + 32 * (p >> 2), w);
+    const uint32_t scw = rd16(b + 2 * p);
+    float acc = 0.f;
+#pragma unroll
+    for (int g = 0; g < 2; g++) {
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t t = __funnelshift_l(w[4 * g + k], w[4 * g + k], rot);
+            const float *xv = x.v + 16 * g + 4 * k;
+            s0 = fmaf(fbits(t & 0x00000030u), xv[0], s0);
+            s1 = fmaf(fbits(t & 0x00003000u), xv[1], s1);
+            s0 = fmaf(fbits(t & 0x00300000u), xv[2], s0);
+            s1 = fmaf(fbits((t >> 8) & 0x00300000u), xv[3], s1);
+        }
+        const uint32_t sc = (scw >> (8 * g)) & 255u;
+        const float dl = d * u2f_small(sc & 15u), ml = dmin * u2f_small(sc >> 4);
+        acc = fmaf(dl * x.inv, s0 + s1, acc);
+        acc = fmaf(-ml, x.s16[g], acc);
+    }
+    return acc;
+}
+
+// ------------------------------------------------------------ Q3_K
+// u = q2 + 4*hbit in 0..7 packed at bits 4..6 of each byte; value = u - 4.
+__device__ __forceinline__ float dot_q3_k(const uint8_t *b, int p, const XPart &x) {
+    const float d = cvt16<true>(rd16(b + 108));
+    const uint32_t rot = (uint32_t)(4 - 2 * (p & 3)) & 31u;     // q2 field -> bits 4..5
+    const uint32_t hrot = (uint32_t)(6 - p) & 31u;              // hmask bit p -> bit 6
+    uint32_t w[8], h[8];
+    rd8w(b + 32 + 32 * (p >> 2), w);
+    rd8w(b, h);
+    float acc = 0.f;
+#pragma unroll
+    for (int g = 0; g < 2; g++) {
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t u = (__funnelshift_l(w[4 * g + k], w[4 * g + k], rot) & 0x30303030u) |
+                               (__funnelshift_l(h[4 * g + k], h[4 * g + k], hrot) & 0x40404040u);
+            const float *xv = x.v + 16 * g + 4 * k;
+            s0 = fmaf(fbits(u & 0x00000070u), xv[0], s0);
+            s1 = fmaf(fbits(u & 0x00007000u), xv[1], s1);
+            s0 = fmaf(fbits(u & 0x00700000u), xv[2], s0);
+            s1 = fmaf(fbits((u >> 8) & 0x00700000u), xv[3], s1);
+        }
+        const float dl = d * (float)q3k_scale(b + 96, 2 * p + g);
+        // sum(v x) = sum(u x) - 4 X
+        acc = fmaf(dl, fmaf(s0 + s1, x.inv, -4.0f * x.s16[g]), acc);
+    }
+    return acc;
+}
+
+// ------------------------------------------------------------ Q4_K
+// nibble (p&1) of 32 qs bytes; nibbles land at bits {0, 8, 16, 16}, the
+// scaled activations' {4, 12, 20, 20} minus 4, so products carry 2^-4.
+__device__ __forceinline__ float dot_q4_k(const uint8_t *b, int p, const XPart &x) {
+    const float d = cvt16<true>(rd16(b)), dmin = cvt16<true>(rd16(b + 2));
+    int s, m;
+    kscale_pair(b + 4, p, s, m);
+    const uint32_t sh = (uint32_t)(p & 1) * 4u;
+    uint32_t w[8];
+    rd8w(b + 16 + 32 * (p >> 1), w);
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const uint32_t t = w[k] >> sh;
+        const float *xv = x.v + 4 * k;
+        s0 = fmaf(fbits(t & 0x0000000Fu), xv[0], s0);
+        s1 = fmaf(fbits(t & 0x00000F00u), xv[1], s1);
+        s0 = fmaf(fbits(t & 0x000F0000u), xv[2], s0);
+        s1 = fmaf(fbits((t >> 8) & 0x000F0000u), xv[3], s1);
+    }
+    const float dl = d * u2f_small((uint32_t)s), ml = dmin * u2f_small((uint32_t)m);
+    return fmaf(dl * (x.inv * 16.0f), s0 + s1, -ml * (x.s16[0] + x.s16[1]));
+}
+
+// ------------------------------------------------------------ generic
+__device__ __forceinline__ float dot_generic(int t, const uint8_t *b, int p, const XPart &x, int n_valid) {
+    float y[32];
+    decode_part_exact<true>(t, b, p, y, n_valid);
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+        s0 = fmaf(i < n_valid ? y[i] : 0.f, x.v[i], s0);
+        s1 = fmaf(i + 1 < n_valid ? y[i + 1] : 0.f, x.v[i + 1], s1);
+    }
+    return s0 + s1;
+}
+
+// Dot of part p for a compile-time format: the fast decoders expect scaled
+// activations (load with SCALED = fast_format(T)), the others unscaled.
+template <int T>
+__device__ __forceinline__ float dot_part(const uint8_t *b, int p, const XPart &x, int n_valid) {
+    if constexpr (T == T_Q2_K) return dot_q2_k(b, p, x);
+    else if constexpr (T == T_Q3_K) return dot_q3_k(b, p, x);
+    else if constexpr (T == T_Q4_K) return dot_q4_k(b, p, x);
+    else return dot_generic(T, b, p, x, n_valid);
+}
+
+}  // namespace sepia

@@ -11,8 +11,7 @@
 //                      dequant (src/quants.c:79-248; gguf-py 0.19.0 for
 //                      Q2_K/Q3_K/IQ2_XXS/IQ1_S) -- explicit __fmul_rn /
 //                      __fadd_rn / __fsub_rn, never contracted to FMA.
-//   dot_part           sum_i w[i]*x[i] over the part in fp32 for the GEMV,
-//                      reassociated for speed (tolerance-level parity).
+// The GEMV dot products over a part live in quant_dot.cuh.
 //
 // Byte reads go through shared memory at whatever alignment the block has
 // (blocks of 110, 50, 66, ... bytes are only 2-byte aligned); see rd_words.
@@ -105,9 +104,19 @@ __device__ __forceinline__ int q3k_scale(const uint8_t *s, int i) {
 
 __device__ __forceinline__ float sgnf(uint32_t s, int j) { return ((s >> j) & 1) ? -1.0f : 1.0f; }
 
+// fp16 bits -> float: HW = false uses the integer restatement (NaN payloads
+// kept bit for bit, for the bitwise dequant gate); HW = true uses the
+// conversion instruction (identical for every finite value and infinity).
+template <bool HW>
+__device__ __forceinline__ float cvt16(uint32_t h) {
+    if constexpr (HW) return __half2float(__ushort_as_half((unsigned short)h));
+    else return f16_bits_to_f32(h);
+}
+
 // Decode part p of superblock `b` (bytes of the whole superblock) into y[32].
 // For F32/F16 `n_valid` limits the elements read (ragged last superblock).
-__device__ inline void decode_part_exact(int t, const uint8_t *b, int p, float *y, int n_valid = 32) {
+template <bool HW = false>
+__device__ __forceinline__ void decode_part_exact(int t, const uint8_t *b, int p, float *y, int n_valid = 32) {
     switch (t) {
     case T_F32: {
         const uint8_t *q = b + 128 * p;
@@ -116,17 +125,17 @@ __device__ inline void decode_part_exact(int t, const uint8_t *b, int p, float *
     }
     case T_F16: {
         const uint8_t *q = b + 64 * p;
-        for (int i = 0; i < n_valid; i++) y[i] = f16_bits_to_f32(rd16(q + 2 * i));
+        for (int i = 0; i < n_valid; i++) y[i] = cvt16<HW>(rd16(q + 2 * i));
         break;
     }
     case T_Q8_0: {
         const uint8_t *q = b + 34 * p;
-        const float d = f16_bits_to_f32(rd16(q));
+        const float d = cvt16<HW>(rd16(q));
         for (int i = 0; i < 32; i++) y[i] = __fmul_rn(d, (float)(int8_t)q[2 + i]);
         break;
     }
     case T_Q2_K: {
-        const float d = f16_bits_to_f32(rd16(b + 80)), dmin = f16_bits_to_f32(rd16(b + 82));
+        const float d = cvt16<HW>(rd16(b + 80)), dmin = cvt16<HW>(rd16(b + 82));
         const uint8_t *q = b + 16 + 32 * (p >> 2);
         const int sh = 2 * (p & 3);
         for (int g = 0; g < 2; g++) {
@@ -138,7 +147,7 @@ __device__ inline void decode_part_exact(int t, const uint8_t *b, int p, float *
         break;
     }
     case T_Q3_K: {
-        const float d = f16_bits_to_f32(rd16(b + 108));
+        const float d = cvt16<HW>(rd16(b + 108));
         const uint8_t *hm = b, *q = b + 32 + 32 * (p >> 2), *sc = b + 96;
         const int sh = 2 * (p & 3);
         for (int g = 0; g < 2; g++) {
@@ -151,7 +160,7 @@ __device__ inline void decode_part_exact(int t, const uint8_t *b, int p, float *
         break;
     }
     case T_Q4_K: case T_Q5_K: {
-        const float d = f16_bits_to_f32(rd16(b)), dmin = f16_bits_to_f32(rd16(b + 2));
+        const float d = cvt16<HW>(rd16(b)), dmin = cvt16<HW>(rd16(b + 2));
         int s, m;
         kscale_pair(b + 4, p, s, m);
         const float dl = __fmul_rn(d, (float)s), ml = __fmul_rn(dmin, (float)m);
@@ -169,7 +178,7 @@ __device__ inline void decode_part_exact(int t, const uint8_t *b, int p, float *
         break;
     }
     case T_Q6_K: {
-        const float d = f16_bits_to_f32(rd16(b + 208));
+        const float d = cvt16<HW>(rd16(b + 208));
         const int half = p >> 2, k = p & 3;
         const uint8_t *L = b + 64 * half + 32 * (k & 1), *Hh = b + 128 + 32 * half;
         const int8_t *sc = reinterpret_cast<const int8_t *>(b + 192 + 8 * half + 2 * k);
@@ -181,7 +190,7 @@ __device__ inline void decode_part_exact(int t, const uint8_t *b, int p, float *
         break;
     }
     case T_IQ2_XXS: {
-        const float d = f16_bits_to_f32(rd16(b));
+        const float d = cvt16<HW>(rd16(b));
         const uint32_t idx = rd32(b + 2 + 8 * p), sg = rd32(b + 6 + 8 * p);
         const float db = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(sg >> 28))), 0.25f);
         for (int l = 0; l < 4; l++) {
@@ -193,7 +202,7 @@ __device__ inline void decode_part_exact(int t, const uint8_t *b, int p, float *
         break;
     }
     case T_IQ2_XS: {
-        const float d = f16_bits_to_f32(rd16(b));
+        const float d = cvt16<HW>(rd16(b));
         const int sc = b[66 + p];
         const float db0 = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(sc & 15))), 0.25f);
         const float db1 = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(sc >> 4))), 0.25f);
@@ -208,7 +217,7 @@ __device__ inline void decode_part_exact(int t, const uint8_t *b, int p, float *
         break;
     }
     case T_IQ3_XXS: {
-        const float d = f16_bits_to_f32(rd16(b));
+        const float d = cvt16<HW>(rd16(b));
         const uint32_t a = rd32(b + 66 + 4 * p);
         const float db = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(a >> 28))), 0.5f);
         const uint8_t *qs = b + 2 + 8 * p;
@@ -223,7 +232,7 @@ __device__ inline void decode_part_exact(int t, const uint8_t *b, int p, float *
         break;
     }
     case T_IQ1_S: {
-        const float d = f16_bits_to_f32(rd16(b));
+        const float d = cvt16<HW>(rd16(b));
         const uint32_t h = rd16(b + 34 + 2 * p);
         const float dl = __fmul_rn(d, (float)(2 * ((h >> 12) & 7) + 1));
         const float delta = (h & 0x8000u) ? -0.125f : 0.125f;
@@ -236,7 +245,7 @@ __device__ inline void decode_part_exact(int t, const uint8_t *b, int p, float *
         break;
     }
     case T_IQ4_XS: {
-        const float d = f16_bits_to_f32(rd16(b));
+        const float d = cvt16<HW>(rd16(b));
         const uint32_t sh = rd16(b + 2);
         const int ls = ((b[4 + (p >> 1)] >> (4 * (p & 1))) & 15) | (((sh >> (2 * p)) & 3) << 4);
         const float dl = __fmul_rn(d, (float)(ls - 32));
@@ -252,157 +261,5 @@ __device__ inline void decode_part_exact(int t, const uint8_t *b, int p, float *
     }
 }
 
-// ==================================================================
-// Fast dot products for the GEMV (fp32, reassociated)
-// ==================================================================
-// Per-lane x context for one part: the 32 x values and their sums over the
-// two 16-element halves (used to fold the K-quant "min" terms and the
-// magic-number integer conversions below).
-struct XPart {
-    float v[32];
-    float s16[2];   // sum of v[0..15], v[16..31]
-};
-
-__device__ __forceinline__ void xpart_sums(XPart &x) {
-    float a = 0.f, b = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; i++) { a += x.v[i]; b += x.v[16 + i]; }
-    x.s16[0] = a;
-    x.s16[1] = b;
-}
-
-// Byte b (0..3) of word m moved to bits 16..23 of a float whose top byte is
-// 0x40: for a field of value v sitting at bits 5-6 of that byte this is the
-// float 2 + v/2 (exact). Single PRMT.
-template <int B>
-__device__ __forceinline__ float byte_to_f_hi(uint32_t m) {
-    // selector nibbles (out byte 3..0): 4 -> 0x40 (from c), B -> m byte B, 5 -> 0x00
-    constexpr uint32_t sel = 0x4055u | ((uint32_t)B << 8);
-    return __uint_as_float(__byte_perm(m, 0x40u, sel));
-}
-
-// sum over 16 weights whose 2-bit fields sit at bits 5-6 of the 16 bytes in
-// w[0..3] (after masking), against x[0..15]: returns sum f*x with f = 2+v/2.
-__device__ __forceinline__ float dot16_f2(const uint32_t (&m)[4], const float *x) {
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-        s0 = fmaf(byte_to_f_hi<0>(m[k]), x[4 * k + 0], s0);
-        s1 = fmaf(byte_to_f_hi<1>(m[k]), x[4 * k + 1], s1);
-        s0 = fmaf(byte_to_f_hi<2>(m[k]), x[4 * k + 2], s0);
-        s1 = fmaf(byte_to_f_hi<3>(m[k]), x[4 * k + 3], s1);
-    }
-    return s0 + s1;
-}
-
-// Q2_K part p: 32 consecutive qs bytes at shift s = 2(p&3), two 16-element
-// groups with 4-bit scale/min. y = sum_g dl_g*sum(v x) - ml_g*sum(x), and
-// sum(v x) = 2*sum(f x) - 4*sum(x) for the f = 2 + v/2 encoding.
-__device__ __forceinline__ float dot_q2_k(const uint8_t *b, int p, const XPart &x) {
-    const float d = f16_bits_to_f32(rd16(b + 80)), dmin = f16_bits_to_f32(rd16(b + 82));
-    const uint32_t rot = (uint32_t)(5 - 2 * (p & 3)) & 31u;   // field -> bits 5..6 of each byte
-    const uint8_t *q = b + 16 + 32 * (p >> 2);
-    uint32_t w[8];
-    rd_words<8>(q, w);
-    const uint32_t scw = lds_u16(b + 2 * p);
-    float acc = 0.f;
-#pragma unroll
-    for (int g = 0; g < 2; g++) {
-        uint32_t m[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) m[k] = __funnelshift_l(w[4 * g + k], w[4 * g + k], rot) & 0x60606060u;
-        const float S = dot16_f2(m, x.v + 16 * g);
-        const uint32_t s = (scw >> (8 * g)) & 255u;
-        const float dl = d * (float)(s & 15u), ml = dmin * (float)(s >> 4);
-        // dl*(2S - 4X) - ml*X
-        acc = fmaf(2.0f * dl, S, acc);
-        acc = fmaf(-(4.0f * dl + ml), x.s16[g], acc);
-    }
-    return acc;
-}
-
-// Q3_K part p: value = q2 - 4*(1-h) where q2 are the low 2 bits (shift
-// 2(p&3)) and h is bit p of hmask. u = q2 + 4h in 0..7 is packed at bits 4-6
-// of a byte -> float f = 2 + u/4; v = u - 4.
-template <int B>
-__device__ __forceinline__ float byte_to_f_u3(uint32_t m) {
-    constexpr uint32_t sel = 0x4055u | ((uint32_t)B << 8);
-    return __uint_as_float(__byte_perm(m, 0x40u, sel));
-}
-__device__ __forceinline__ float dot_q3_k(const uint8_t *b, int p, const XPart &x) {
-    const float d = f16_bits_to_f32(rd16(b + 108));
-    const uint32_t rot = (uint32_t)(4 - 2 * (p & 3)) & 31u;   // q2 field -> bits 4..5
-    const uint32_t hrot = (uint32_t)(6 - p) & 31u;              // hmask bit p -> bit 6
-    uint32_t w[8], h[8];
-    rd_words<8>(b + 32 + 32 * (p >> 2), w);
-    rd_words<8>(b, h);
-    float acc = 0.f;
-#pragma unroll
-    for (int g = 0; g < 2; g++) {
-        float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const uint32_t u = (__funnelshift_l(w[4 * g + k], w[4 * g + k], rot) & 0x30303030u) |
-                               (__funnelshift_l(h[4 * g + k], h[4 * g + k], hrot) & 0x40404040u);
-            s0 = fmaf(byte_to_f_u3<0>(u), x.v[16 * g + 4 * k + 0], s0);
-            s1 = fmaf(byte_to_f_u3<1>(u), x.v[16 * g + 4 * k + 1], s1);
-            s0 = fmaf(byte_to_f_u3<2>(u), x.v[16 * g + 4 * k + 2], s0);
-            s1 = fmaf(byte_to_f_u3<3>(u), x.v[16 * g + 4 * k + 3], s1);
-        }
-        // u at bits 4..6 of the byte = float bits 20..22: f = 2*(1 + u/8) = 2 + u/4
-        const float S = s0 + s1;
-        const float dl = d * (float)q3k_scale(b + 96, 2 * p + g);
-        // sum(u x) = 4(S - 2X); sum(v x) = sum(u x) - 4X = 4S - 12X
-        acc = fmaf(4.0f * dl, S, acc);
-        acc = fmaf(-12.0f * dl, x.s16[g], acc);
-    }
-    return acc;
-}
-
-// Q4_K part p: nibble (p&1) of 32 qs bytes, one 6-bit scale/min pair.
-// nibble placed at bits 3..6 of a byte = float bits 19..22 -> f = 2*(1 + v/16)
-// = 2 + v/8, so sum(v x) = 8(S - 2X).
-__device__ __forceinline__ float dot_q4_k(const uint8_t *b, int p, const XPart &x) {
-    const float d = f16_bits_to_f32(rd16(b)), dmin = f16_bits_to_f32(rd16(b + 2));
-    int s, m;
-    kscale_pair(b + 4, p, s, m);
-    const uint32_t rot = (p & 1) ? 31u : 3u;   // high nibble >> 1, low nibble << 3
-    uint32_t w[8];
-    rd_words<8>(b + 16 + 32 * (p >> 1), w);
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const uint32_t u = __funnelshift_l(w[k], w[k], rot) & 0x78787878u;
-        s0 = fmaf(byte_to_f_hi<0>(u), x.v[4 * k + 0], s0);
-        s1 = fmaf(byte_to_f_hi<1>(u), x.v[4 * k + 1], s1);
-        s0 = fmaf(byte_to_f_hi<2>(u), x.v[4 * k + 2], s0);
-        s1 = fmaf(byte_to_f_hi<3>(u), x.v[4 * k + 3], s1);
-    }
-    const float S = s0 + s1, X = x.s16[0] + x.s16[1];
-    const float dl = d * (float)s, ml = dmin * (float)m;
-    // dl*8*(S - 2X) - ml*X
-    return fmaf(8.0f * dl, S, -(16.0f * dl + ml) * X);
-}
-
-// Generic path: exact decode of the part into registers, then FMA.
-__device__ __forceinline__ float dot_generic(int t, const uint8_t *b, int p, const XPart &x, int n_valid) {
-    float y[32];
-    decode_part_exact(t, b, p, y, n_valid);
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-    for (int i = 0; i < 32; i += 2) {
-        s0 = fmaf(i < n_valid ? y[i] : 0.f, x.v[i], s0);
-        s1 = fmaf(i + 1 < n_valid ? y[i + 1] : 0.f, x.v[i + 1], s1);
-    }
-    return s0 + s1;
-}
-
-template <int T>
-__device__ __forceinline__ float dot_part(const uint8_t *b, int p, const XPart &x, int n_valid) {
-    if constexpr (T == T_Q2_K) return dot_q2_k(b, p, x);
-    else if constexpr (T == T_Q3_K) return dot_q3_k(b, p, x);
-    else if constexpr (T == T_Q4_K) return dot_q4_k(b, p, x);
-    else return dot_generic(T, b, p, x, n_valid);
-}
 
 }  // namespace sepia

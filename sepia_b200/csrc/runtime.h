@@ -23,8 +23,9 @@ int fail(const char *fmt, ...);
 int check(cudaError_t err, const char *what);
 // The library's own stream (non-blocking, created on first use).
 cudaStream_t lib_stream();
-// Stream argument of the raw entry points: NULL -> lib_stream().
-inline cudaStream_t as_stream(void *s) { return s ? (cudaStream_t)s : lib_stream(); }
+// Stream argument of the raw entry points: NULL is the legacy default stream
+// (stream 0), as everywhere in CUDA -- torch's current stream is usually 0.
+inline cudaStream_t as_stream(void *s) { return (cudaStream_t)s; }
 
 // Sets the dynamic shared-memory limit of `fn` to at least `bytes` (cached).
 int ensure_smem(const void *fn, int bytes);

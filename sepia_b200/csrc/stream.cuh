@@ -17,7 +17,7 @@
 // fetched from floor16(src) to ceil16(end) and lands at stage + (src & 15):
 // the shared-memory copy keeps the global address modulo 16.
 #pragma once
-#include "quant_formats.cuh"
+#include "quant_dot.cuh"
 
 namespace sepia {
 
@@ -58,7 +58,9 @@ __device__ __forceinline__ void consumer_sync(int nthreads) {
 }
 
 // Load the activation part a lane owns: x[sb*256 + 32p + i] for i < 32,
-// zero beyond in_dim; also the two 16-element sums.
+// zero beyond in_dim; also the two 16-element sums and, for the fast
+// formats (SCALED), the per-position pre-scaling of quant_dot.cuh.
+template <bool SCALED>
 __device__ __forceinline__ void load_xpart(XPart &xp, const float *x, int64_t in_dim, int sb, int p) {
     const int64_t base = (int64_t)sb * kQK + 32 * p;
     if (base + 32 <= in_dim && ((reinterpret_cast<uintptr_t>(x + base) & 15) == 0)) {
@@ -72,7 +74,7 @@ __device__ __forceinline__ void load_xpart(XPart &xp, const float *x, int64_t in
 #pragma unroll
         for (int i = 0; i < 32; i++) xp.v[i] = (base + i < in_dim) ? __ldg(x + base + i) : 0.0f;
     }
-    xpart_sums(xp);
+    xpart_finish<SCALED>(xp);
 }
 
 // Dot of one row's parts owned by this lane: superblocks sb_j, part p.

@@ -76,7 +76,7 @@ _PROTOS = {
     "sepia_gpu_matvec_q": (C.c_int, [C.c_int, vp, C.c_size_t, vp, vp, i64, i64]),
     "sepia_gpu_dequant_rows": (C.c_int, [C.c_int, vp, C.c_size_t, vp, i64]),
     "sepia_gpu_rel_project": (C.c_int, [vp, vp, vp, i64, i64, i64, i64]),
-    "sepia_gpu_banded_attn": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp] + [i64] * 8 + [C.c_float]),
+    "sepia_gpu_banded_attn": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp] + [i64] * 7 + [C.c_float]),
     "sepia_gpu_matvec_off": (C.c_int, [vp, C.c_size_t, vp, vp, i64, i64]),
     "sepia_gpu_rmsnorm_off": (C.c_int, [vp, C.c_size_t, vp, vp, i64, i64, C.c_float]),
     "sepia_gpu_sconv_off": (C.c_int, [vp, C.c_size_t, vp, vp, vp, i64, i64, i64]),
