@@ -15,12 +15,13 @@
  * Buffer model on a discrete GPU (the reference's Metal buffers are
  * unified memory; here they are mirrored):
  *   - alloc(len, 0) "Shared": device memory plus a pinned host mirror
- *     returned by host_ptr. sepia_gpu_begin() uploads every live Shared
- *     buffer's host mirror; sepia_gpu_end() downloads every Shared or
- *     wrapped buffer the GPU wrote during the batch. Host writes therefore
- *     belong before begin() and host reads after end(), which is exactly the
- *     reference's calling discipline (src/sepia_gpu.h:86-88 and every caller
- *     in src/sepia.c).
+ *     returned by host_ptr. The first op of a batch that names a Shared
+ *     buffer uploads its host mirror (so a buffer filled after begin(), as
+ *     src/sepia.c:4941 does, is seen); sepia_gpu_end() downloads every
+ *     Shared or wrapped buffer the GPU wrote during the batch. Host writes
+ *     therefore belong before the first op that uses the buffer and host
+ *     reads after end() -- the reference's calling discipline
+ *     (src/sepia_gpu.h:86-88 and every caller in src/sepia.c).
  *   - alloc(len, 1) "Private": device memory only, host_ptr NULL.
  *   - wrap_mmap(base, len): the bytes are copied into device memory once, at
  *     wrap time (the reference wraps the read-only resident.bin mapping);

@@ -36,7 +36,7 @@ struct AttnParams {
     const float *rel_logits;   // [T, H, E]
     const int64_t *kv_lo, *kv_hi;
     const float *tau;
-    float *part;               // [T, H, S, Dh + 2]
+    double *part;              // [T, H, S, Dh + 2]: m, l, acc[Dh] (fp64: no rounding before the combine)
     int64_t T, H, Hkv, Dh, E, q_pos_base, kv_dim;
     float inv_head_dim;
     int S;
@@ -82,11 +82,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
 
     // PV ownership: warp w owns heads g = w, w+4, ...; lane owns dims lane + 32j
     constexpr int kHPW = kAttnMaxG / 4;
-    float acc[kHPW][kAttnMaxDh / 32];
+    double acc[kHPW][kAttnMaxDh / 32];   // fp64: long kv chains stay at fp32 rounding
 #pragma unroll
     for (int a = 0; a < kHPW; a++)
 #pragma unroll
-        for (int j = 0; j < kAttnMaxDh / 32; j++) acc[a][j] = 0.0f;
+        for (int j = 0; j < kAttnMaxDh / 32; j++) acc[a][j] = 0.0;
     __syncthreads();
 
     for (int64_t base = c0; base < c1; base += kAttnKT) {
@@ -108,16 +108,20 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
                 const int64_t kv = base + r;
                 const int64_t dist = q_pos - kv;
                 for (int g = g0; g < G; g += gstep) {
-                    float d0 = 0.f, d1 = 0.f;
+                    // the reference's score arithmetic (src/sepia.c:1216-1220):
+                    // fp64 dot rounded to float, then content + bias in fp64,
+                    // rounded once -- a one-ulp score change moves exp() by
+                    // ~1e-6 relative, more than the whole error budget
+                    double d0 = 0.0, d1 = 0.0;
                     const float *qr = sq + g * ld, *kr = sk + r * ld;
                     for (int d = 0; d < Dh; d += 2) {
-                        d0 = fmaf(qr[d], kr[d], d0);
-                        d1 = fmaf(qr[d + 1], kr[d + 1], d1);
+                        d0 = fma((double)qr[d], (double)kr[d], d0);
+                        d1 = fma((double)qr[d + 1], (double)kr[d + 1], d1);
                     }
-                    float sc = (d0 + d1) * P.inv_head_dim;
+                    double sc = (double)(float)(d0 + d1) * (double)P.inv_head_dim;
                     if (dist < P.E && dist >= 0)
-                        sc += P.rel_logits[(t * P.H + (int64_t)hk * G + g) * P.E + dist] * tau;
-                    ss[g * kAttnKT + r] = sc;
+                        sc += (double)P.rel_logits[(t * P.H + (int64_t)hk * G + g) * P.E + dist] * (double)tau;
+                    ss[g * kAttnKT + r] = (float)sc;
                 }
             } else {
                 for (int g = g0; g < G; g += gstep) ss[g * kAttnKT + r] = -INFINITY;
@@ -133,22 +137,22 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
                 const float tmax = warp_max(fmaxf(v0, v1));
                 const float m_old = sml[2 * g];
                 const float m_new = fmaxf(m_old, tmax);
-                const float corr = (m_old == -INFINITY) ? 0.0f : expf(m_old - m_new);
-                const float p0 = (v0 == -INFINITY) ? 0.0f : expf(v0 - m_new);
-                const float p1 = (v1 == -INFINITY) ? 0.0f : expf(v1 - m_new);
+                const float corr = (m_old == -INFINITY) ? 0.0f : (float)exp((double)(m_old - m_new));
+                const float p0 = (v0 == -INFINITY) ? 0.0f : (float)exp((double)(v0 - m_new));
+                const float p1 = (v1 == -INFINITY) ? 0.0f : (float)exp((double)(v1 - m_new));
                 ss[g * kAttnKT + lane] = p0;
                 ss[g * kAttnKT + lane + 32] = p1;
                 const float psum = warp_sum(p0 + p1);
                 __syncwarp();
                 if (lane == 0) { sml[2 * g] = m_new; sml[2 * g + 1] = sml[2 * g + 1] * corr + psum; }
 #pragma unroll
-                for (int j = 0; j < kAttnMaxDh / 32; j++) acc[a][j] *= corr;
+                for (int j = 0; j < kAttnMaxDh / 32; j++) acc[a][j] *= (double)corr;
                 for (int r = 0; r < nt; r++) {
                     const float pr = ss[g * kAttnKT + r];
 #pragma unroll
                     for (int j = 0; j < kAttnMaxDh / 32; j++) {
                         const int d = lane + 32 * j;
-                        if (d < Dh) acc[a][j] = fmaf(pr, sv[r * ld + d], acc[a][j]);
+                        if (d < Dh) acc[a][j] = fma((double)pr, (double)sv[r * ld + d], acc[a][j]);
                     }
                 }
             }
@@ -161,7 +165,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
         const int g = warp + 4 * a;
         if (g < G) {
             const int64_t h = (int64_t)hk * G + g;
-            float *pp = P.part + ((t * P.H + h) * P.S + s) * (P.Dh + 2);
+            double *pp = P.part + ((t * P.H + h) * P.S + s) * (P.Dh + 2);
             if (lane == 0) { pp[0] = sml[2 * g]; pp[1] = sml[2 * g + 1]; }
 #pragma unroll
             for (int j = 0; j < kAttnMaxDh / 32; j++) {
@@ -173,24 +177,24 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
 }
 
 // out[t,h,:] = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M), splits in order.
-__global__ void k_attn_combine(const float *part, float *out, int64_t TH, int S, int64_t Dh) {
+__global__ void k_attn_combine(const double *part, float *out, int64_t TH, int S, int64_t Dh) {
     const int64_t th = blockIdx.x;
     if (th >= TH) return;
-    const float *pp = part + th * S * (Dh + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < S; s++) M = fmaxf(M, pp[s * (Dh + 2)]);
-    float L = 0.0f;
+    const double *pp = part + th * S * (Dh + 2);
+    double M = -INFINITY;
+    for (int s = 0; s < S; s++) M = fmax(M, pp[s * (Dh + 2)]);
+    double L = 0.0;
     for (int s = 0; s < S; s++) {
-        const float m = pp[s * (Dh + 2)];
-        if (m != -INFINITY) L += pp[s * (Dh + 2) + 1] * expf(m - M);
+        const double m = pp[s * (Dh + 2)];
+        if (m != -INFINITY) L += pp[s * (Dh + 2) + 1] * exp(m - M);
     }
     for (int64_t d = threadIdx.x; d < Dh; d += blockDim.x) {
-        float a = 0.0f;
+        double a = 0.0;
         for (int s = 0; s < S; s++) {
-            const float m = pp[s * (Dh + 2)];
-            if (m != -INFINITY) a += pp[s * (Dh + 2) + 2 + d] * expf(m - M);
+            const double m = pp[s * (Dh + 2)];
+            if (m != -INFINITY) a += pp[s * (Dh + 2) + 2 + d] * exp(m - M);
         }
-        out[th * Dh + d] = a / L;
+        out[th * Dh + d] = (float)(a / L);
     }
 }
 
@@ -215,13 +219,13 @@ int attn_splits(int64_t T, int64_t Hkv, int64_t max_n) {
 }
 
 size_t attn_part_bytes(int64_t T, int64_t H, int S, int64_t Dh) {
-    return (size_t)T * (size_t)H * (size_t)S * (size_t)(Dh + 2) * sizeof(float);
+    return (size_t)T * (size_t)H * (size_t)S * (size_t)(Dh + 2) * sizeof(double);
 }
 
 int launch_banded_attn(int kv_f16, const float *q, const void *k, const void *v, const float *rel_logits, float *out,
                        const int64_t *kv_lo_d, const int64_t *kv_hi_d, const float *tau_d, int64_t T, int64_t H,
                        int64_t Hkv, int64_t Dh, int64_t E, int64_t q_pos_base, int64_t kv_dim, float inv_head_dim,
-                       int S, float *part, cudaStream_t st) {
+                       int S, double *part, cudaStream_t st) {
     if (T <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || Dh <= 0 || E < 0 || kv_dim < Hkv * Dh)
         return fail("banded_attn: bad geometry T=%lld H=%lld Hkv=%lld Dh=%lld E=%lld kv_dim=%lld", (long long)T,
                     (long long)H, (long long)Hkv, (long long)Dh, (long long)E, (long long)kv_dim);
@@ -274,7 +278,7 @@ extern "C" int sepia_cuda_banded_attn(int kv_f16, const float *q, const void *k,
     if (!ws || ws_bytes < attn_part_bytes(T, H, S, Dh))
         return fail("banded_attn: workspace of %zu bytes < %zu needed", ws_bytes, attn_part_bytes(T, H, S, Dh));
     return launch_banded_attn(kv_f16, q, k, v, rel_logits, out, kv_lo, kv_hi, tau, T, H, Hkv, Dh, rel_extent,
-                              q_pos_base, kv_dim, inv_head_dim, S, (float *)ws, as_stream(stream));
+                              q_pos_base, kv_dim, inv_head_dim, S, (double *)ws, as_stream(stream));
 }
 
 extern "C" int sepia_cuda_rel_project(const float *r_vec, const float *rel_proj, float *rel_logits, int64_t T,

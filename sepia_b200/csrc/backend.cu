@@ -40,7 +40,7 @@ int launch_rel_project(const float *r_vec, const float *rel_proj, float *rel_log
 int launch_banded_attn(int kv_f16, const float *q, const void *k, const void *v, const float *rel_logits, float *out,
                        const int64_t *kv_lo_d, const int64_t *kv_hi_d, const float *tau_d, int64_t T, int64_t H,
                        int64_t Hkv, int64_t Dh, int64_t E, int64_t q_pos_base, int64_t kv_dim, float inv_head_dim,
-                       int S, float *part, cudaStream_t st);
+                       int S, double *part, cudaStream_t st);
 int attn_splits(int64_t T, int64_t Hkv, int64_t max_n);
 size_t attn_part_bytes(int64_t T, int64_t H, int S, int64_t Dh);
 }  // namespace sepia
@@ -55,6 +55,7 @@ struct SepiaGpuBuf {
     size_t len = 0;          // device bytes
     BufKind kind = kShared;
     bool dev_dirty = false;  // written by the GPU in the open batch
+    bool synced = false;     // Shared: host mirror uploaded in the open batch
 };
 
 namespace {
@@ -134,16 +135,27 @@ T *dptr(SepiaGpuBuf *b, size_t off = 0) {
     return reinterpret_cast<T *>(static_cast<char *>(b->dev) + off);
 }
 
+// Bounds-checks a buffer argument of an op and, for a Shared buffer the
+// batch has not touched yet, enqueues the upload of its host mirror first:
+// the reference (unified memory) may fill a Shared buffer after
+// sepia_gpu_begin(), right before the op that reads it (src/sepia.c:4941).
 bool fits(SepiaGpuBuf *b, size_t off, size_t bytes, const char *op, const char *what) {
     if (!b || !b->dev) { fail("%s: %s buffer is NULL", op, what); return false; }
     if (off > b->len || bytes > b->len - off) {
         fail("%s: %s needs %zu bytes at offset %zu but the buffer holds %zu", op, what, bytes, off, b->len);
         return false;
     }
+    if (b->kind == kShared && g.batch_open && !b->synced) {
+        if (!check(cudaMemcpyAsync(b->dev, b->host, b->len, cudaMemcpyHostToDevice, g.stream), "upload Shared buffer"))
+            return false;
+        b->synced = true;
+    }
     return true;
 }
 
-void mark(SepiaGpuBuf *b) { if (b) b->dev_dirty = true; }
+void mark(SepiaGpuBuf *b) {
+    if (b) { b->dev_dirty = true; b->synced = true; }
+}
 
 double now_s() {
     struct timespec ts;
@@ -295,11 +307,11 @@ extern "C" int sepia_gpu_selftest_touch(SepiaGpuBuf *b, size_t n_floats) {
 extern "C" int sepia_gpu_begin(void) {
     if (!g.ready) return fail("begin: GPU not initialized");
     if (g.batch_open) return fail("begin: a batch is already active");
+    // Shared buffers are uploaded lazily, by the first op of the batch that
+    // names them (see fits()).
     for (SepiaGpuBuf *b : g.bufs) {
         b->dev_dirty = false;
-        if (b->kind == kShared &&
-            !check(cudaMemcpyAsync(b->dev, b->host, b->len, cudaMemcpyHostToDevice, g.stream), "begin: upload"))
-            return 0;
+        b->synced = false;
     }
     g.batch_open = true;
     return 1;
@@ -319,6 +331,7 @@ extern "C" int sepia_gpu_end(void) {
         if (b->dev_dirty && b->host && b->kind != kPrivate)
             ok &= check(cudaMemcpyAsync(b->host, b->dev, b->len, cudaMemcpyDeviceToHost, g.stream), "end: download");
         b->dev_dirty = false;
+        b->synced = false;
     }
     ok &= wait_stream("end");
     g.arena.reset();
@@ -481,7 +494,7 @@ extern "C" int sepia_gpu_banded_attn(SepiaGpuBuf *q, SepiaGpuBuf *k, SepiaGpuBuf
     memcpy(hs + 2 * nb64, tau, nb32);
     if (!check(cudaMemcpyAsync(ds, hs, 2 * nb64 + nb32, cudaMemcpyHostToDevice, g.stream), "banded_attn upload")) return 0;
     const int S = attn_splits(T, Hkv, max_n);
-    float *part = (float *)g.arena.take(attn_part_bytes(T, H, S, Dh));
+    double *part = (double *)g.arena.take(attn_part_bytes(T, H, S, Dh));
     if (!part) return fail("banded_attn: out of scratch memory");
     if (!launch_banded_attn(0, dptr(q), dptr(k), dptr(v), rel_extent > 0 ? dptr(rel_logits) : nullptr, dptr(attn_out),
                             (const int64_t *)ds, (const int64_t *)(ds + nb64), (const float *)(ds + 2 * nb64), T, H, Hkv,

@@ -79,8 +79,8 @@ __device__ __forceinline__ float warp_max(float v) {
 // Reduce-scatter of N per-lane partial sums across the warp (N a power of
 // two <= 32). On return v[0] in lane L holds the full warp sum of row
 // rs_row<N>(L). Costs N-1 + log2(32/N) shuffles instead of N*5.
-template <int N>
-__device__ __forceinline__ void warp_reduce_scatter(float (&v)[N], int lane) {
+template <int N, typename T>
+__device__ __forceinline__ void warp_reduce_scatter(T (&v)[N], int lane) {
     int n = N;
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) {
@@ -89,9 +89,9 @@ __device__ __forceinline__ void warp_reduce_scatter(float (&v)[N], int lane) {
 #pragma unroll
             for (int i = 0; i < N / 2; i++) {
                 if (i < n / 2) {
-                    const float lo = v[i], hi = v[i + n / 2];
-                    const float send = upper ? lo : hi;
-                    const float keep = upper ? hi : lo;
+                    const T lo = v[i], hi = v[i + n / 2];
+                    const T send = upper ? lo : hi;
+                    const T keep = upper ? hi : lo;
                     v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
                 }
             }

@@ -303,8 +303,8 @@ __global__ void __launch_bounds__(17 * 32, 1) k_gateup(const GuParams P) {
     const MoeDev &L = P.L;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kGuStagesMax;
-    float *red = reinterpret_cast<float *>(smem + 256);   // [2][nwc][kTRG]
-    uint8_t *stage0 = smem + 256 + ((2 * 16 * kTRG * 4 + 127) & ~127);
+    double *red = reinterpret_cast<double *>(smem + 256);   // [2][nwc][kTRG]
+    uint8_t *stage0 = smem + 256 + ((2 * 16 * kTRG * 8 + 127) & ~127);
 
     int slots[kMaxSlots];
     const int n_act = active_slots(L, P.idx, slots);
@@ -374,16 +374,20 @@ __global__ void __launch_bounds__(17 * 32, 1) k_gateup(const GuParams P) {
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
-        warp_reduce_scatter<kTRG>(acc, lane);
-        if ((lane & 3) == 0) red[(grp * P.nwc + cw) * kTRG + my_row] = acc[0];
+        double ad[kTRG];
+#pragma unroll
+        for (int i = 0; i < kTRG; i++) ad[i] = (double)acc[i];
+        warp_reduce_scatter<kTRG>(ad, lane);
+        if ((lane & 3) == 0) red[(grp * P.nwc + cw) * kTRG + my_row] = ad[0];
         consumer_sync(n_cons * 32);
         const int t = threadIdx.x;
         if (t < nr) {
-            float gsum = 0.0f, usum = 0.0f;
+            double gd = 0.0, ud = 0.0;
             for (int c = 0; c < P.nwc; c++) {
-                gsum += red[c * kTRG + t];
-                usum += red[(P.nwc + c) * kTRG + t];
+                gd += red[c * kTRG + t];
+                ud += red[(P.nwc + c) * kTRG + t];
             }
+            const float gsum = (float)gd, usum = (float)ud;
             const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, (float)exp(-(double)gsum)));
             float hv = __fmul_rn(__fmul_rn(gsum, sig), usum);
             if (slot >= L.topk) hv = __fmul_rn(hv, P.weights[slot]);   // shared: gamma inside h
@@ -420,8 +424,8 @@ __global__ void __launch_bounds__(17 * 32, 1) k_down(const DnParams P) {
     const MoeDev &L = P.L;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kDnStagesMax;
-    float *red = reinterpret_cast<float *>(smem + 256);   // [kMaxSlots][nwc][kTRD]
-    uint8_t *stage0 = smem + 256 + ((kMaxSlots * 16 * kTRD * 4 + 127) & ~127);
+    double *red = reinterpret_cast<double *>(smem + 256);   // [kMaxSlots][nwc][kTRD]
+    uint8_t *stage0 = smem + 256 + ((kMaxSlots * 16 * kTRD * 8 + 127) & ~127);
 
     int slots[kMaxSlots];
     const int n_act = active_slots(L, P.idx, slots);
@@ -511,8 +515,11 @@ __global__ void __launch_bounds__(17 * 32, 1) k_down(const DnParams P) {
         for (int q = 0; q < SPW; q++) {
             const int a = sg + q * kGroups;
             if (a < n_act) {
-                warp_reduce_scatter<kTRD>(acc[q], lane);
-                if ((lane & 7) == 0) red[(a * P.nwc + cw) * kTRD + my_row] = acc[q][0];
+                double ad[kTRD];
+#pragma unroll
+                for (int i = 0; i < kTRD; i++) ad[i] = (double)acc[q][i];
+                warp_reduce_scatter<kTRD>(ad, lane);
+                if ((lane & 7) == 0) red[(a * P.nwc + cw) * kTRD + my_row] = ad[0];
             }
         }
         consumer_sync(n_cons * 32);
@@ -524,8 +531,9 @@ __global__ void __launch_bounds__(17 * 32, 1) k_down(const DnParams P) {
             for (int s = 0; s < n_slots; s++) {
                 float term = 0.0f;
                 if (a < n_act && slots[a] == s) {
-                    float e = 0.0f;
-                    for (int c = 0; c < P.nwc; c++) e += red[(a * P.nwc + c) * kTRD + t];
+                    double ed = 0.0;
+                    for (int c = 0; c < P.nwc; c++) ed += red[(a * P.nwc + c) * kTRD + t];
+                    const float e = (float)ed;
                     term = (s < L.topk) ? __fmul_rn(e, P.weights[s]) : e;
                     a++;
                     if (!P.slots_out) o = __fadd_rn(o, term);
@@ -657,7 +665,7 @@ int launch_gateup(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaS
     const uint32_t ss_u = L.n_shared ? slot_bytes_for((uint64_t)G.tr_shared * L.rb_sh_up) : 0;
     G.up_off = std::max(sr_g, ss_g);
     G.slot_bytes = G.up_off + std::max(sr_u, ss_u);
-    const int head_g = 256 + ((2 * 16 * kTRG * 4 + 127) & ~127);
+    const int head_g = 256 + ((2 * 16 * kTRG * 8 + 127) & ~127);
     G.stages = kGuStagesMax;
     while (G.stages > 2 && head_g + (int64_t)G.stages * G.slot_bytes > di.smem_optin) G.stages--;
     const int64_t smem_g = head_g + (int64_t)G.stages * G.slot_bytes;
@@ -685,7 +693,7 @@ int launch_down(const MoeDev &L, const SepiaMoeWork *ws, float *out, float *slot
     for (int s = 0; s < n_slots; s++)
         sbytes += slot_bytes_for((uint64_t)kTRD * (s < L.topk ? L.rb_down : L.rb_sh_down));
     D.slot_bytes = (uint32_t)sbytes;
-    const int head_d = 256 + ((kMaxSlots * 16 * kTRD * 4 + 127) & ~127);
+    const int head_d = 256 + ((kMaxSlots * 16 * kTRD * 8 + 127) & ~127);
     D.stages = kDnStagesMax;
     while (D.stages > 2 && head_d + (int64_t)D.stages * D.slot_bytes > di.smem_optin) D.stages--;
     const int64_t smem_d = head_d + (int64_t)D.stages * D.slot_bytes;

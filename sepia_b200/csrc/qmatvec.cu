@@ -9,8 +9,10 @@
 #include "../../include/sepia_cuda.h"
 #include "runtime.h"
 #include "stream.cuh"
+#include "mma_gemv.cuh"
 
 #include <algorithm>
+#include <stdlib.h>
 
 namespace sepia {
 
@@ -40,8 +42,8 @@ __global__ void __launch_bounds__(17 * 32) k_matvec(const MvParams P) {
     const int TR = TRW * P.G;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kMvStagesMax;
-    float *red = reinterpret_cast<float *>(smem + 128);                    // [G][nwc][TRW]
-    uint8_t *stage0 = smem + 128 + ((n_cons * TRW * 4 + 127) & ~127);
+    double *red = reinterpret_cast<double *>(smem + 128);                  // [G][nwc][TRW]
+    uint8_t *stage0 = smem + 128 + ((n_cons * TRW * 8 + 127) & ~127);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < P.stages; s++) {
@@ -110,19 +112,173 @@ __global__ void __launch_bounds__(17 * 32) k_matvec(const MvParams P) {
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[slot]);
             }
-            warp_reduce_scatter<TRW>(acc, lane);
-            if ((lane & wlane) == 0) red[(g * P.nwc + cw) * TRW + my_row] = acc[0];
+            // partials are reduced in fp64 so the row sum rounds once, like
+            // the reference's double-accumulated dot
+            double ad[TRW];
+#pragma unroll
+            for (int i = 0; i < TRW; i++) ad[i] = (double)acc[i];
+            warp_reduce_scatter<TRW>(ad, lane);
+            if ((lane & wlane) == 0) red[(g * P.nwc + cw) * TRW + my_row] = ad[0];
             consumer_sync(n_cons * 32);
             const int t = threadIdx.x;
             if (t < nr) {
                 const int gg = t / TRW, ii = t % TRW;
-                float s = 0.0f;
+                double s = 0.0;
                 for (int c = 0; c < P.nwc; c++) s += red[(gg * P.nwc + c) * TRW + ii];
-                P.y[(int64_t)v * P.out_dim + r0 + t] = s;
+                P.y[(int64_t)v * P.out_dim + r0 + t] = (float)s;
             }
             consumer_sync(n_cons * 32);
         }
     }
+}
+
+// ------------------------------------------------------------------ tensor-core path
+// Q2_K rows on the integer tensor cores (mma_gemv.cuh). Units are 16-row
+// tiles. Warps: n_cons consumers (consumer c owns superblocks
+// [c*sbw, (c+1)*sbw) of every tile), one producer (bulk copies), one
+// reducer. Per stage slot three mbarriers: full (copy landed), ready (all
+// consumers deposited their fp64 row partials), empty (reducer summed them
+// in consumer order and stored the rows; the slot may be refilled).
+// Consumers never wait on each other.
+struct MvMmaParams {
+    const uint8_t *w;
+    int64_t row_bytes;
+    const float *x;
+    float *y;
+    int64_t out_dim;
+    int nsb, n_cons, sbw, stages;
+    uint32_t slot_bytes, red_off, xl_off, stage_off;
+    int64_t num_units;
+    int *err;
+};
+
+constexpr int kMmaRows = 16;
+constexpr int kMmaStagesMax = 6;
+
+__global__ void __launch_bounds__(18 * 32, 1) k_matvec_mma_q2k(const MvMmaParams P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_cons = P.n_cons, prod = n_cons, redw = n_cons + 1;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *ready = full + kMmaStagesMax;
+    uint64_t *empty = ready + kMmaStagesMax;
+    double *red = reinterpret_cast<double *>(smem + P.red_off);      // [stages][n_cons][16]
+    const XLimbs X = xlimbs_carve(smem + P.xl_off, P.nsb);
+    uint8_t *stage0 = smem + P.stage_off;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P.stages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&ready[s], n_cons);
+            mbar_init(&empty[s], 1);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (warp == prod && lane == 0) {   // start streaming before building the tables
+        int64_t k = 0;
+        for (int64_t u = blockIdx.x; k < P.stages && u < P.num_units; k++, u += gridDim.x) {
+            const int64_t r0 = u * kMmaRows;
+            const ByteRange r{P.w + r0 * P.row_bytes, (uint32_t)(imin64(kMmaRows, P.out_dim - r0) * P.row_bytes)};
+            mbar_arrive_expect_tx(&full[k], range_copy_bytes(r));
+            range_issue(stage0 + (size_t)k * P.slot_bytes, r, &full[k]);
+        }
+    }
+    xlimbs_build(X, P.x, P.nsb, warp, blockDim.x >> 5, lane);
+
+    if (warp == prod) {
+        if (lane == 0) {
+            int64_t k = P.stages, issued = 0;
+            for (int64_t u = blockIdx.x; u < P.num_units && issued < P.stages; u += gridDim.x) issued++;
+            for (int64_t u = blockIdx.x + (int64_t)P.stages * gridDim.x; u < P.num_units; u += gridDim.x, k++) {
+                const int slot = (int)(k % P.stages);
+                if (!mbar_wait(&empty[slot], (uint32_t)(((k / P.stages) - 1) & 1), P.err)) break;
+                const int64_t r0 = u * kMmaRows;
+                const ByteRange r{P.w + r0 * P.row_bytes, (uint32_t)(imin64(kMmaRows, P.out_dim - r0) * P.row_bytes)};
+                mbar_arrive_expect_tx(&full[slot], range_copy_bytes(r));
+                range_issue(stage0 + (size_t)slot * P.slot_bytes, r, &full[slot]);
+                issued = k + 1;
+            }
+            for (int64_t j = (issued > P.stages ? issued - P.stages : 0); j < issued; j++)
+                mbar_wait(&full[j % P.stages], (uint32_t)((j / P.stages) & 1), nullptr);
+        }
+        return;
+    }
+    if (warp == redw) {
+        int64_t k = 0;
+        for (int64_t u = blockIdx.x; u < P.num_units; u += gridDim.x, k++) {
+            const int slot = (int)(k % P.stages);
+            if (!mbar_wait(&ready[slot], (uint32_t)((k / P.stages) & 1), P.err)) break;
+            const int64_t r0 = u * kMmaRows;
+            const int64_t nr = imin64(kMmaRows, P.out_dim - r0);
+            if (lane < nr) {
+                const double *rs = red + (size_t)slot * n_cons * kMmaRows + lane;
+                double s = 0.0;
+                for (int c = 0; c < n_cons; c++) s += rs[c * kMmaRows];
+                P.y[r0 + lane] = (float)s;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        return;
+    }
+
+    const int cw = warp;
+    const int sb0 = cw * P.sbw, sb1 = min(P.nsb, sb0 + P.sbw);
+    const int gid = lane >> 2, tig = lane & 3;
+    int64_t k = 0;
+    for (int64_t u = blockIdx.x; u < P.num_units; u += gridDim.x, k++) {
+        const int slot = (int)(k % P.stages);
+        if (!mbar_wait(&full[slot], (uint32_t)((k / P.stages) & 1), P.err)) break;
+        const int64_t r0 = u * kMmaRows;
+        const uint8_t *tile = range_data(stage0 + (size_t)slot * P.slot_bytes, ByteRange{P.w + r0 * P.row_bytes, 0});
+        double yg = 0.0, yg8 = 0.0;
+        tile16_q2k(tile, P.row_bytes, sb0, sb1, X, lane, yg, yg8);
+        tile16_finish(yg, yg8);
+        if (tig == 0) {
+            double *rs = red + ((size_t)slot * n_cons + cw) * kMmaRows;
+            rs[gid] = yg;
+            rs[gid + 8] = yg8;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[slot]);   // release: the partials above are visible to the reducer
+    }
+}
+
+static int launch_matvec_mma_q2k(const void *w, const float *x, float *y, int64_t out_dim, int64_t in_dim,
+                                 int64_t rb, cudaStream_t st) {
+    DevInfo &di = dev_info();
+    MvMmaParams P;
+    P.w = reinterpret_cast<const uint8_t *>(w);
+    P.row_bytes = rb;
+    P.x = x; P.y = y; P.out_dim = out_dim;
+    P.nsb = (int)(in_dim / kQK);
+    P.n_cons = std::min(16, P.nsb);
+    P.sbw = (P.nsb + P.n_cons - 1) / P.n_cons;
+    P.n_cons = (P.nsb + P.sbw - 1) / P.sbw;
+    P.slot_bytes = slot_bytes_for((uint64_t)kMmaRows * rb);
+    P.stages = kMmaStagesMax;
+    int64_t smem = 0;
+    for (;;) {
+        P.red_off = 3 * kMmaStagesMax * 8 + 16;
+        P.red_off = (P.red_off + 127) & ~127u;
+        P.xl_off = P.red_off + ((P.stages * P.n_cons * kMmaRows * 8 + 127) & ~127);
+        P.stage_off = P.xl_off + ((xlimbs_bytes(P.nsb) + 127) & ~127);
+        smem = P.stage_off + (int64_t)P.stages * P.slot_bytes;
+        if (P.stages <= 2 || smem <= (int64_t)di.smem_optin) break;
+        P.stages--;
+    }
+    if (smem > di.smem_optin) return fail("matvec_q: tensor-core tile needs %lld B of shared memory", (long long)smem);
+    if (!ensure_smem((const void *)k_matvec_mma_q2k, (int)smem)) return 0;
+    P.num_units = (out_dim + kMmaRows - 1) / kMmaRows;
+    P.err = di.err;
+    const int threads = (P.n_cons + 2) * 32;
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_matvec_mma_q2k, threads, (size_t)smem);
+    if (per_sm < 1) per_sm = 1;
+    const int64_t grid = std::min<int64_t>(P.num_units, (int64_t)di.sm_count * per_sm);
+    k_matvec_mma_q2k<<<(unsigned)grid, threads, (size_t)smem, st>>>(P);
+    return check(cudaGetLastError(), "matvec_q (tensor cores) launch");
 }
 
 // Exact dequantisation: one thread per 32-element part.
@@ -174,21 +330,25 @@ int launch_matvec_q(int t, const void *w, const float *x, float *y, int64_t out_
     const int64_t rb = host_row_bytes(t, in_dim);
     if (rb <= 0) return fail("matvec_q: unsupported ggml type %d or in_dim %lld not block-aligned", t, (long long)in_dim);
     if (!w || !x || !y) return fail("matvec_q: null pointer");
+    // Q2_K with 4-byte aligned rows runs on the integer tensor cores
+    if (t == T_Q2_K && n_vec == 1 && in_dim <= 16384 && ((reinterpret_cast<uintptr_t>(w) & 3) == 0) &&
+        ((reinterpret_cast<uintptr_t>(x) & 15) == 0))
+        return launch_matvec_mma_q2k(w, x, y, out_dim, in_dim, rb, st);
     DevInfo &di = dev_info();
     const int nsb = (int)((in_dim + kQK - 1) / kQK);
     int c = 1, nwc = (nsb + 3) / 4;
     if (nwc > 16) { c = 2; nwc = (nsb + 7) / 8; }
     if (nwc > 16) return fail("matvec_q: in_dim %lld too large (max 32768)", (long long)in_dim);
     int G = 1;
-    while (nwc * G * 2 <= 8) G *= 2;          // at least 8 consumer warps when rows are short
+    while (nwc * G * 2 <= 16) G *= 2;         // up to 16 consumer warps: latency hiding
     int trw = 8;
-    if ((int64_t)trw * G * rb > 48 * 1024) trw = 2;
-    while (G > 1 && (int64_t)trw * G * rb > 48 * 1024) G /= 2;
+    if ((int64_t)trw * G * rb > 80 * 1024) trw = 2;
+    while (G > 1 && (int64_t)trw * G * rb > 80 * 1024) G /= 2;
     if ((int64_t)trw * G * rb > 160 * 1024) return fail("matvec_q: rows of %lld bytes too large", (long long)rb);
     const int TR = trw * G;
     const uint32_t slot = slot_bytes_for((uint64_t)TR * rb);
     const int n_cons = nwc * G;
-    const int head = 128 + ((n_cons * trw * 4 + 127) & ~127);
+    const int head = 128 + ((n_cons * trw * 8 + 127) & ~127);
     int stages = kMvStagesMax;
     while (stages > 2 && head + (int64_t)stages * slot > (int64_t)di.smem_optin) stages--;
     const int64_t smem = head + (int64_t)stages * slot;

@@ -168,13 +168,15 @@ __device__ __forceinline__ float dot_q4_k(const uint8_t *b, int p, const XPart &
 __device__ __forceinline__ float dot_generic(int t, const uint8_t *b, int p, const XPart &x, int n_valid) {
     float y[32];
     decode_part_exact<true>(t, b, p, y, n_valid);
-    float s0 = 0.f, s1 = 0.f;
+    // fp64 accumulation: the part's sum rounds once (the reference
+    // double-accumulates its dot, src/sepia.c:731-735)
+    double s0 = 0.0, s1 = 0.0;
 #pragma unroll
     for (int i = 0; i < 32; i += 2) {
-        s0 = fmaf(i < n_valid ? y[i] : 0.f, x.v[i], s0);
-        s1 = fmaf(i + 1 < n_valid ? y[i + 1] : 0.f, x.v[i + 1], s1);
+        s0 = fma(i < n_valid ? (double)y[i] : 0.0, (double)x.v[i], s0);
+        s1 = fma(i + 1 < n_valid ? (double)y[i + 1] : 0.0, (double)x.v[i + 1], s1);
     }
-    return s0 + s1;
+    return (float)(s0 + s1);
 }
 
 // Dot of part p for a compile-time format: the fast decoders expect scaled

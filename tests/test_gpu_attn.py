@@ -5,6 +5,7 @@ T=1 decode, prefill chunks, band edge mid-chunk, sliding windows, tau != 1 at
 a large position, GQA; plus BASELINE configuration 4 (H=64, Hkv=8, Dh=128,
 fp16 K/V, windows 4096 / global, rel_extent 256) at reduced context."""
 import ctypes as C
+import zlib
 
 import numpy as np
 import pytest
@@ -64,7 +65,7 @@ def run_oracle(oracle, c):
 @pytest.mark.parametrize("name", list(CASES))
 @pytest.mark.parametrize("f16", [False, True])
 def test_banded_attn_cases(lib, oracle, name, f16):
-    rng = np.random.default_rng(abs(hash(name)) % 1000)
+    rng = np.random.default_rng(zlib.crc32(name.encode()) % 1000)
     c = make_case(rng, *CASES[name], f16=f16)
     assert oracle.rel_err(run_gpu(c, f16), run_oracle(oracle, c)) <= TOL
 
