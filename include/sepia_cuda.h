@@ -135,6 +135,26 @@ int sepia_cuda_banded_attn(int kv_f16, const float *q, const void *k, const void
                            int64_t q_pos_base, int64_t kv_dim, float inv_head_dim, int64_t max_kv,
                            void *ws, size_t ws_bytes, void *stream);
 
+/* Allocation-free banded attention. No counterpart in the reference (its
+ * Metal backend allocates per call): for callers that cannot allocate device
+ * memory -- a host whose device heap belongs to another allocator, a plugin
+ * host that only passes its own input/output buffers, or a loop that must not
+ * call cudaMalloc/cudaFree because they can synchronize the device. Same
+ * arguments and result as sepia_cuda_banded_attn minus the workspace: the
+ * split partials go to a fixed 8 MiB array inside the library
+ * (sepia_cuda_banded_attn_noalloc_max_bytes), held on every GPU that loads
+ * the library until exit. Shapes whose partials exceed it return 0 with a
+ * "needs N bytes" error. The first call on each device resolves the array's
+ * address; make it before any stream capture begins. All calls on a device
+ * share the array: calls whose kernels overlap on the GPU (unordered
+ * streams) race; calls on one stream are safe. */
+size_t sepia_cuda_banded_attn_noalloc_max_bytes(void);
+int sepia_cuda_banded_attn_noalloc(int kv_f16, const float *q, const void *k, const void *v,
+                                   const float *rel_logits, float *out, const int64_t *kv_lo,
+                                   const int64_t *kv_hi, const float *tau, int64_t T, int64_t H, int64_t Hkv,
+                                   int64_t Dh, int64_t rel_extent, int64_t q_pos_base, int64_t kv_dim,
+                                   float inv_head_dim, int64_t max_kv, void *stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

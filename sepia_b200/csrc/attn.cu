@@ -21,6 +21,7 @@
 
 #include <cuda_fp16.h>
 #include <algorithm>
+#include <mutex>
 
 namespace sepia {
 
@@ -279,6 +280,75 @@ extern "C" int sepia_cuda_banded_attn(int kv_f16, const float *q, const void *k,
         return fail("banded_attn: workspace of %zu bytes < %zu needed", ws_bytes, attn_part_bytes(T, H, S, Dh));
     return launch_banded_attn(kv_f16, q, k, v, rel_logits, out, kv_lo, kv_hi, tau, T, H, Hkv, Dh, rel_extent,
                               q_pos_base, kv_dim, inv_head_dim, S, (double *)ws, as_stream(stream));
+}
+
+// ------------------------------------------------ allocation-free variant
+// Some callers cannot allocate device memory at all: hosts whose device heap
+// is owned by another allocator that reserved it up front, plugin hosts that
+// only hand the library their own input/output buffers, and latency-critical
+// loops that must not call cudaMalloc/cudaFree because those can synchronize
+// the whole device. For them the split partials live in a fixed array
+// compiled into the library instead of a caller workspace.
+//
+// The first call on each device looks up the array's device address (one
+// cudaGetDevice + cudaGetSymbolAddress, with that device current); make that
+// first call before any stream capture begins. The array is a module global, so every GPU that loads the
+// library holds its kNoAllocScratchBytes from module load until the process
+// exits.
+//
+// Nothing in it must start at zero: every (token, head, split) record is
+// fully written by k_attn_split before k_attn_combine reads it. All calls on
+// one device share the one array, so two calls whose kernels overlap on the
+// GPU (different streams with no ordering between them) race and corrupt
+// each other's result; calls on one stream are ordered and safe.
+constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;   // 8 MiB of fp64 partials
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) double g_attn_noalloc_part[kNoAllocScratchBytes / sizeof(double)];
+
+// Device address of g_attn_noalloc_part on the current device. In host code
+// the symbol is only a host-side handle, never a device address, so the
+// address is looked up once per device (with that device current) through
+// cudaGetSymbolAddress and cached.
+static double *noalloc_part_ptr() {
+    static std::mutex mu;
+    static double *ptrs[kNoAllocMaxDevices] = {};
+    int dev = -1;
+    if (!check(cudaGetDevice(&dev), "banded_attn_noalloc: cudaGetDevice")) return nullptr;
+    if (dev < 0 || dev >= kNoAllocMaxDevices) {
+        fail("banded_attn_noalloc: device %d out of range (max %d)", dev, kNoAllocMaxDevices);
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptrs[dev]) {
+        void *p = nullptr;
+        if (!check(cudaGetSymbolAddress(&p, g_attn_noalloc_part), "banded_attn_noalloc: cudaGetSymbolAddress"))
+            return nullptr;
+        ptrs[dev] = (double *)p;
+    }
+    return ptrs[dev];
+}
+
+extern "C" size_t sepia_cuda_banded_attn_noalloc_max_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int sepia_cuda_banded_attn_noalloc(int kv_f16, const float *q, const void *k, const void *v,
+                                              const float *rel_logits, float *out, const int64_t *kv_lo,
+                                              const int64_t *kv_hi, const float *tau, int64_t T, int64_t H,
+                                              int64_t Hkv, int64_t Dh, int64_t rel_extent, int64_t q_pos_base,
+                                              int64_t kv_dim, float inv_head_dim, int64_t max_kv, void *stream) {
+    if (T <= 0 || H <= 0 || Hkv <= 0 || Dh <= 0)
+        return fail("banded_attn_noalloc: bad geometry T=%lld H=%lld Hkv=%lld Dh=%lld", (long long)T, (long long)H,
+                    (long long)Hkv, (long long)Dh);
+    const int S = attn_splits(T, Hkv, max_kv > 0 ? max_kv : 1);
+    const size_t need = attn_part_bytes(T, H, S, Dh);
+    if (need > kNoAllocScratchBytes)
+        return fail("banded_attn_noalloc: T=%lld H=%lld Dh=%lld needs %zu bytes of partials, above the fixed "
+                    "%zu-byte scratch; use sepia_cuda_banded_attn with a caller workspace",
+                    (long long)T, (long long)H, (long long)Dh, need, kNoAllocScratchBytes);
+    double *part = noalloc_part_ptr();
+    if (!part) return 0;
+    return launch_banded_attn(kv_f16, q, k, v, rel_logits, out, kv_lo, kv_hi, tau, T, H, Hkv, Dh, rel_extent,
+                              q_pos_base, kv_dim, inv_head_dim, S, part, as_stream(stream));
 }
 
 extern "C" int sepia_cuda_rel_project(const float *r_vec, const float *rel_proj, float *rel_logits, int64_t T,

@@ -112,6 +112,9 @@ _PROTOS = {
     "sepia_cuda_banded_attn_ws_bytes": (C.c_size_t, [i64, i64, i64, i64, i64]),
     "sepia_cuda_banded_attn": (C.c_int, [C.c_int, vp, vp, vp, vp, vp, vp, vp, vp] + [i64] * 7 + [C.c_float, i64, vp,
                                                                                                   C.c_size_t, vp]),
+    "sepia_cuda_banded_attn_noalloc_max_bytes": (C.c_size_t, []),
+    "sepia_cuda_banded_attn_noalloc": (C.c_int, [C.c_int, vp, vp, vp, vp, vp, vp, vp, vp] + [i64] * 7
+                                       + [C.c_float, i64, vp]),
 }
 
 
