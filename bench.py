@@ -42,6 +42,7 @@ def parse():
     ap.add_argument("--impl", default="sepia", choices=["sepia", "reference"])
     ap.add_argument("--layers", type=int, default=4, help="distinct layer instances rotated per step")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="eager launches instead of one CUDA graph per layer")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--parity", action="store_true", help="check one step against the CPU oracle")
     return ap.parse_args()
@@ -233,6 +234,26 @@ def main():
     def step(i):
         layers[i % len(layers)].forward(X[i % 64], out, group=group)
 
+    # Decode runs a layer as one CUDA graph (router, gate/up, down, combine
+    # replayed without host launch gaps). One graph per layer instance, each
+    # with its own resident input; eager launches for the sharded path.
+    graphs = []
+    if world == 1 and not args.no_graph:
+        xin = X[:len(layers)].clone()
+        outs = torch.empty(len(layers), shape.hidden, dtype=torch.float32, device="cuda")
+        for l, D in enumerate(layers):      # warm: kernel attributes set before capture
+            D.forward(xin[l], outs[l])
+        torch.cuda.synchronize()
+        for l, D in enumerate(layers):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                D.forward(xin[l], outs[l])
+            graphs.append(g)
+        torch.cuda.synchronize()
+
+        def step(i):  # noqa: F811
+            graphs[i % len(graphs)].replay()
+
     if args.parity and rank == 0 and world == 1:
         parity_check(layers[0], X[0])
 
@@ -326,6 +347,9 @@ def per_kernel_times(layers, X, args, world, group):
     n = max(20, min(args.steps, 200))
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n)]
     out = torch.empty(layers[0].shape.hidden, device="cuda")
+    # hold the device back while the host enqueues every launch, so that the
+    # events bracket device time only (no host launch gaps)
+    torch.cuda._sleep(100_000_000)
     for i in range(n):
         D = layers[i % len(layers)]
         x = X[i % 64]

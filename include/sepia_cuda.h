@@ -92,6 +92,7 @@ typedef struct {
     float *h;               /* [topk + n_shared, ff] SwiGLU activations */
     float *slots;           /* [topk + n_shared, hidden] per-slot terms (sharded mode) */
     unsigned int *counter;  /* router completion counter; zero before first use */
+    double *router_part;    /* [n_routed + n_shared, ceil(hidden/1024)] router chunk partials */
 } SepiaMoeWork;
 
 size_t sepia_cuda_moe_work_bytes(const SepiaMoeLayer *L);

@@ -29,6 +29,10 @@ namespace sepia {
 
 constexpr int kMaxSlots = 16;      // topk + n_shared
 constexpr int kRouterWarps = 8;
+constexpr int kRouterChunk = 1024;       // router row elements per warp
+constexpr int kRouterMaxExperts = 1024;  // n_routed + n_shared
+constexpr int kRouterMaxChunks = 16;     // hidden <= 16384
+__host__ __device__ inline int router_chunks(int64_t hidden) { return (int)((hidden + kRouterChunk - 1) / kRouterChunk); }
 constexpr int kGuStagesMax = 8;
 constexpr int kDnStagesMax = 8;
 constexpr int kTRG = 8;            // max rows per gate/up unit
@@ -80,44 +84,51 @@ __device__ __forceinline__ float logsigmoid_ref(float x) {
     return x - log1pf((float)exp((double)x));
 }
 
+// Router GEMV: the [n_total, hidden] f32 matrix is cut into chunks of
+// kRouterChunk consecutive elements of one row; one warp per chunk, every
+// lane issuing all of its 16-byte loads before the first FMA, so the whole
+// matrix is in flight at once (a decode router is too small to reach HBM
+// bandwidth any other way). Chunk partials are fp64 and are summed per row
+// in chunk order by the last CTA, so the result does not depend on
+// scheduling. That CTA then runs the selection (one warp: the serial parts
+// are short and __syncthreads rounds would dominate).
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router(const MoeDev L, const float *x, float *logits,
                                                                int32_t *topk_idx, float *weights,
-                                                               unsigned int *counter) {
-    // one CTA per logit row; the 8 warps split the row into contiguous
-    // chunks and their fp64 partials are summed in warp order (deterministic)
+                                                               unsigned int *counter, double *part) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x;
-    __shared__ double s_part[kRouterWarps];
-    {
-        const float *w = L.router_w + (int64_t)row * L.hidden;
+    const int n_total = L.n_routed + L.n_shared;
+    const int cpr = router_chunks(L.hidden);
+    const int64_t chunk = (int64_t)blockIdx.x * kRouterWarps + warp;
+    if (chunk < (int64_t)n_total * cpr) {
+        const int row = (int)(chunk / cpr), c = (int)(chunk % cpr);
+        const int64_t c0 = (int64_t)c * kRouterChunk;
+        const int64_t n = imin64(kRouterChunk, L.hidden - c0);
+        const float *w = L.router_w + (int64_t)row * L.hidden + c0;
+        const float *xc = x + c0;
         double acc = 0.0;
-        const bool vec = ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15) == 0 &&
-                         (L.hidden % (4 * kRouterWarps)) == 0;
-        if (vec) {
-            const int64_t per = L.hidden / 4 / kRouterWarps;
-            const float4 *w4 = reinterpret_cast<const float4 *>(w) + warp * per;
-            const float4 *x4 = reinterpret_cast<const float4 *>(x) + warp * per;
-#pragma unroll 4
-            for (int64_t i = lane; i < per; i += 32) {
-                const float4 a4 = __ldg(w4 + i), b4 = __ldg(x4 + i);
-                acc = fma((double)a4.x, (double)b4.x, acc);
-                acc = fma((double)a4.y, (double)b4.y, acc);
-                acc = fma((double)a4.z, (double)b4.z, acc);
-                acc = fma((double)a4.w, (double)b4.w, acc);
+        if (n == kRouterChunk && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(xc)) & 15) == 0) {
+            constexpr int kV = kRouterChunk / 128;      // float4 per lane
+            float4 wv[kV], xv[kV];
+#pragma unroll
+            for (int i = 0; i < kV; i++) wv[i] = __ldcs(reinterpret_cast<const float4 *>(w) + lane + 32 * i);
+#pragma unroll
+            for (int i = 0; i < kV; i++) xv[i] = __ldg(reinterpret_cast<const float4 *>(xc) + lane + 32 * i);
+            double a2[2] = {0.0, 0.0};
+#pragma unroll
+            for (int i = 0; i < kV; i++) {
+                a2[i & 1] = fma((double)wv[i].x, (double)xv[i].x, a2[i & 1]);
+                a2[i & 1] = fma((double)wv[i].y, (double)xv[i].y, a2[i & 1]);
+                a2[i & 1] = fma((double)wv[i].z, (double)xv[i].z, a2[i & 1]);
+                a2[i & 1] = fma((double)wv[i].w, (double)xv[i].w, a2[i & 1]);
             }
+            acc = a2[0] + a2[1];
         } else {
-            for (int64_t i = threadIdx.x; i < L.hidden; i += blockDim.x) acc = fma((double)w[i], (double)x[i], acc);
+            for (int64_t i = lane; i < n; i += 32) acc = fma((double)w[i], (double)xc[i], acc);
         }
         acc = warp_sum_d(acc);
-        if (lane == 0) s_part[warp] = acc;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            double t = 0.0;
-            for (int i = 0; i < kRouterWarps; i++) t += s_part[i];
-            logits[row] = (float)t;
-        }
+        if (lane == 0) part[chunk] = acc;
     }
-    // ---- last CTA performs the selection ----
+    // ---- last CTA: logits, then the selection ----
     __shared__ unsigned int s_last;
     __threadfence();
     __syncthreads();
@@ -126,59 +137,60 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(const MoeDev L, co
     if (!s_last) return;
     __threadfence();
 
-    __shared__ float s_score[1024];
-    __shared__ float s_bv[kRouterWarps];
-    __shared__ int s_bi[kRouterWarps];
-    __shared__ int s_sel[kMaxSlots];
-    const volatile float *lg = logits;
-    for (int i = threadIdx.x; i < L.n_routed; i += blockDim.x)
-        s_score[i] = __fadd_rn(sigmoid_ref(lg[i]), L.router_bias[i]);
-    __syncthreads();
-    for (int j = 0; j < L.topk; j++) {
-        // block argmax: first index of the maximum among unused entries
-        float bv = 0.0f;
-        int bi = -1;
-        for (int i = threadIdx.x; i < L.n_routed; i += blockDim.x) {
-            bool used = false;
-            for (int q = 0; q < j; q++) used |= (s_sel[q] == i);
-            if (used) continue;
-            const float v = s_score[i];
-            if (bi < 0 || v > bv) { bv = v; bi = i; }
-        }
+    __shared__ float s_logit[kRouterMaxExperts];
+    __shared__ float s_score[kRouterMaxExperts];
+    // row sums in chunk order; a thread's loads are independent (L2: other
+    // CTAs wrote them), so they are all in flight together
+    for (int r = threadIdx.x; r < n_total; r += blockDim.x) {
+        double v[kRouterMaxChunks];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
-        }
-        if (lane == 0) { s_bv[warp] = bv; s_bi[warp] = bi; }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float v = s_bv[0];
-            int b = s_bi[0];
-            for (int w2 = 1; w2 < kRouterWarps; w2++) {
-                const int oi = s_bi[w2];
-                if (oi >= 0 && (b < 0 || s_bv[w2] > v || (s_bv[w2] == v && oi < b))) { v = s_bv[w2]; b = oi; }
-            }
-            s_sel[j] = b;
-        }
-        __syncthreads();
+        for (int c = 0; c < kRouterMaxChunks; c++) v[c] = (c < cpr) ? __ldcg(part + (int64_t)r * cpr + c) : 0.0;
+        double t = 0.0;
+#pragma unroll
+        for (int c = 0; c < kRouterMaxChunks; c++)
+            if (c < cpr) t += v[c];
+        s_logit[r] = (float)t;
+        logits[r] = (float)t;
     }
-    if (threadIdx.x == 0) {
-        const int n_sel = L.topk + L.n_shared;
-        float lp[kMaxSlots];
-        for (int j = 0; j < n_sel; j++) {
-            const float l = (j < L.topk) ? lg[s_sel[j]] : lg[L.n_routed + (j - L.topk)];
-            lp[j] = logsigmoid_ref(l);
+    __syncthreads();
+    for (int i = threadIdx.x; i < L.n_routed; i += blockDim.x)
+        s_score[i] = __fadd_rn(sigmoid_ref(s_logit[i]), L.router_bias[i]);
+    __syncthreads();
+    // top-k by rank: entry i is the (rank_i)-th pick of the reference's
+    // repeated strict-'>' scan from index 0, where rank_i counts the entries
+    // that beat it (higher score, or equal score at a lower index). One pass,
+    // every thread ranking its own entries against all others.
+    __shared__ int s_sel[kMaxSlots];
+    for (int i = threadIdx.x; i < L.n_routed; i += blockDim.x) {
+        const float v = s_score[i];
+        int rank = 0;
+        for (int j = 0; j < L.n_routed; j++) {
+            const float u = s_score[j];
+            rank += (u > v || (u == v && j < i)) ? 1 : 0;
         }
-        float lmax = lp[0];
-        for (int j = 1; j < n_sel; j++) lmax = fmaxf(lmax, lp[j]);
-        double se = 0.0;
-        for (int j = 0; j < n_sel; j++) se += exp((double)(lp[j] - lmax));
-        const double lse = (double)lmax + log(se);
-        const double sc = (double)L.route_scale * (double)L.global_scale;
-        for (int j = 0; j < n_sel; j++) weights[j] = (float)(exp((double)lp[j] - lse) * sc);
-        for (int j = 0; j < L.topk; j++) topk_idx[j] = s_sel[j];
+        if (rank < L.topk) s_sel[rank] = i;
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    // weights: softmax over the k selected raw logits and the shared-sink
+    // logits in log-sigmoid space (src/sepia.c:1349-1374); lane j owns slot j
+    const int n_sel = L.topk + L.n_shared;
+    float lp = -INFINITY;
+    if (lane < n_sel) {
+        const float l = (lane < L.topk) ? s_logit[s_sel[lane]] : s_logit[L.n_routed + (lane - L.topk)];
+        lp = logsigmoid_ref(l);
+    }
+    float lmax = lp;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    const double e = (lane < n_sel) ? exp((double)(lp - lmax)) : 0.0;
+    double se = 0.0;
+    for (int j = 0; j < n_sel; j++) se += __shfl_sync(0xffffffffu, e, j);   // slot order
+    const double lse = (double)lmax + log(se);
+    const double scl = (double)L.route_scale * (double)L.global_scale;
+    if (lane < n_sel) weights[lane] = (float)(exp((double)lp - lse) * scl);
+    if (lane < L.topk) topk_idx[lane] = s_sel[lane];
+    if (lane == 0) {
         *counter = 0u;   // ready for the next launch
         __threadfence();
     }
@@ -646,8 +658,14 @@ static int pick_tr(int64_t rb_pair, int64_t budget) {
 
 int launch_router(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaStream_t st) {
     const int n_total = L.n_routed + L.n_shared;
-    const int grid = n_total;
-    k_router<<<grid, kRouterWarps * 32, 0, st>>>(L, x, ws->logits, ws->topk_idx, ws->weights, ws->counter);
+    if (n_total > kRouterMaxExperts) return fail("moe: %d experts exceed the router's %d", n_total, kRouterMaxExperts);
+    if (router_chunks(L.hidden) > kRouterMaxChunks)
+        return fail("moe: hidden %lld exceeds the router's %d", (long long)L.hidden, kRouterMaxChunks * kRouterChunk);
+    if (!ws->router_part) return fail("moe: work area has no router partials (carve it with moe_work_carve)");
+    const int64_t chunks = (int64_t)n_total * router_chunks(L.hidden);
+    const unsigned grid = (unsigned)((chunks + kRouterWarps - 1) / kRouterWarps);
+    k_router<<<grid, kRouterWarps * 32, 0, st>>>(L, x, ws->logits, ws->topk_idx, ws->weights, ws->counter,
+                                                  ws->router_part);
     return check(cudaGetLastError(), "moe router launch");
 }
 
@@ -727,6 +745,7 @@ extern "C" size_t sepia_cuda_moe_work_bytes(const SepiaMoeLayer *L) {
     add(n_slots * (size_t)L->ff * 4); // h
     add(n_slots * (size_t)L->hidden * 4);  // slots
     add(256);                         // counter
+    add(n_total * (size_t)router_chunks(L->hidden) * 8);  // router_part
     return b;
 }
 
@@ -744,6 +763,7 @@ extern "C" int sepia_cuda_moe_work_carve(const SepiaMoeLayer *L, void *base, siz
     ws->h = (float *)take(n_slots * (size_t)L->ff * 4);
     ws->slots = (float *)take(n_slots * (size_t)L->hidden * 4);
     ws->counter = (unsigned int *)take(256);
+    ws->router_part = (double *)take(n_total * (size_t)router_chunks(L->hidden) * 8);
     return 1;
 }
 
