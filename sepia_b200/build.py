@@ -66,7 +66,7 @@ def build(verbose: bool = False, ptxas_v: bool = False, force: bool = False) -> 
             if r.returncode != 0:
                 raise RuntimeError(f"nvcc failed on {src.name}")
     objs = [str(BUILD / (s.stem + ".o")) for s in sources()]
-    if force or jobs or not OUT.exists():
+    if force or jobs or not OUT.exists() or any(Path(o).stat().st_mtime > OUT.stat().st_mtime for o in objs):
         tmp = OUT.with_suffix(".so.tmp")
         cmd = [cc, *ARCH, "-shared", "-o", str(tmp), *objs, "-lcudart"]
         r = subprocess.run(cmd, capture_output=True, text=True)

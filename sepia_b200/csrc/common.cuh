@@ -20,6 +20,9 @@ constexpr int kQK = 256;                 // superblock width of every K/IQ forma
 // (~1-2 s at B200 clocks), records the failure in the device error word
 // and returns.
 constexpr long long kWaitCycles = 4000000000LL;
+// try_wait may suspend the waiting thread up to this long (ns) instead of
+// returning at once: waiting warps stop taking issue slots
+constexpr int kWaitSuspendNs = 1000000;
 
 // Device-side error word: 0 = ok. Kernels set a nonzero code instead of
 // trapping; the host reads it at sepia_gpu_end() / sepia_cuda_check().
@@ -144,10 +147,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(kWaitSuspendNs)
         : "memory");
     return ok != 0;
 }

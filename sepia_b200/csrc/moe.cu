@@ -22,6 +22,7 @@
 #include "../../include/sepia_cuda.h"
 #include "runtime.h"
 #include "stream.cuh"
+#include "qengine.cuh"
 
 #include <algorithm>
 
@@ -92,14 +93,22 @@ __device__ __forceinline__ float logsigmoid_ref(float x) {
 // in chunk order by the last CTA, so the result does not depend on
 // scheduling. That CTA then runs the selection (one warp: the serial parts
 // are short and __syncthreads rounds would dominate).
+// Warps past the last chunk build the tensor-core activation table of x
+// (one superblock each) for the gate/up projections, when xtab is given.
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router(const MoeDev L, const float *x, float *logits,
                                                                int32_t *topk_idx, float *weights,
-                                                               unsigned int *counter, double *part) {
+                                                               unsigned int *counter, double *part, uint8_t *xtab) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_total = L.n_routed + L.n_shared;
     const int cpr = router_chunks(L.hidden);
     const int64_t chunk = (int64_t)blockIdx.x * kRouterWarps + warp;
-    if (chunk < (int64_t)n_total * cpr) {
+    const int64_t n_chunks = (int64_t)n_total * cpr;
+    griddep_launch();
+    if (chunk >= n_chunks) {
+        griddep_wait();
+        const int sb = (int)(chunk - n_chunks);
+        if (xtab && sb < (int)(L.hidden / kQK)) xtab_build(xtab, x, sb + 1, sb, 1 << 30, lane);
+    } else {
         const int row = (int)(chunk / cpr), c = (int)(chunk % cpr);
         const int64_t c0 = (int64_t)c * kRouterChunk;
         const int64_t n = imin64(kRouterChunk, L.hidden - c0);
@@ -109,8 +118,11 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(const MoeDev L, co
         if (n == kRouterChunk && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(xc)) & 15) == 0) {
             constexpr int kV = kRouterChunk / 128;      // float4 per lane
             float4 wv[kV], xv[kV];
+            // the weights do not depend on the previous kernel: load them
+            // before waiting for it (x does)
 #pragma unroll
             for (int i = 0; i < kV; i++) wv[i] = __ldcs(reinterpret_cast<const float4 *>(w) + lane + 32 * i);
+            griddep_wait();
 #pragma unroll
             for (int i = 0; i < kV; i++) xv[i] = __ldg(reinterpret_cast<const float4 *>(xc) + lane + 32 * i);
             double a2[2] = {0.0, 0.0};
@@ -123,6 +135,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(const MoeDev L, co
             }
             acc = a2[0] + a2[1];
         } else {
+            griddep_wait();
             for (int64_t i = lane; i < n; i += 32) acc = fma((double)w[i], (double)xc[i], acc);
         }
         acc = warp_sum_d(acc);
@@ -561,10 +574,166 @@ __global__ void __launch_bounds__(17 * 32, 1) k_down(const DnParams P) {
 // out[r] = sum over slots in order (after an all-reduce of the slot terms).
 __global__ void k_combine(const float *slots, int n_slots, int64_t hidden, float *out) {
     const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    griddep_wait();
+    griddep_launch();
     if (r >= hidden) return;
     float o = 0.0f;
     for (int s = 0; s < n_slots; s++) o = __fadd_rn(o, slots[(int64_t)s * hidden + r]);
     out[r] = o;
+}
+
+// ============================================================== tensor-core path
+// Gate/up and down of every selected expert on the engine of qengine.cuh,
+// chained router -> gate/up -> down by programmatic dependent launch: each
+// kernel starts streaming weights that do not depend on its predecessor
+// (shared experts for gate/up, every down matrix) while the predecessor
+// finishes.
+
+// Per-slot row sources of one launch, kept in the engine's shared job
+// scratch: matrix bases (gate/up, or down), row bytes, format and splits;
+// nsplit = 0 for slots this rank does not own.
+struct MoeSlot {
+    const uint8_t *a, *b;
+    int64_t rb;
+    int type, sbs, nsplit, pad;
+};
+static_assert(kMaxSlots * sizeof(MoeSlot) <= (size_t)kQeJobSmem, "slot table exceeds the job scratch");
+
+// Units: (slot, 8-row block of ff): MMA rows 0-7 are the gate rows, 8-15 the
+// matching up rows. Shared slots come first: they do not depend on the router.
+struct GuJob {
+    MoeDev L;
+    const int32_t *idx;
+    const float *weights;
+    float *h;
+    const uint8_t *xtab;
+    int nsb_h, tpu, n_slots;
+    int sbs_r, nsplit_r, sbs_s, nsplit_s;
+    __device__ void init() {}
+    __device__ void setup(uint8_t *jsm, int tid, bool after_dep) {
+        MoeSlot *S = reinterpret_cast<MoeSlot *>(jsm);
+        if (!after_dep && tid < L.n_shared) {
+            MoeSlot &m = S[L.topk + tid];
+            m.a = L.sh_gate + (int64_t)tid * L.sh_gate_stride;
+            m.b = L.sh_up + (int64_t)tid * L.sh_up_stride;
+            m.rb = L.rb_sh_gate; m.type = L.sh_gate_type; m.sbs = sbs_s;
+            m.nsplit = (tid % L.world == L.rank) ? nsplit_s : 0;
+        }
+        if (after_dep && tid < L.topk) {
+            MoeSlot &m = S[tid];
+            const int e = idx[tid];
+            const bool own = e >= 0 && e < L.n_routed && e % L.world == L.rank;
+            const int64_t le = own ? local_expert(L, e) : 0;
+            m.a = L.gate + le * L.gate_stride;
+            m.b = L.up + le * L.up_stride;
+            m.rb = L.rb_gate; m.type = L.gate_type; m.sbs = sbs_r;
+            m.nsplit = own ? nsplit_r : 0;
+        }
+    }
+    __device__ int64_t n_units() const { return (int64_t)n_slots * tpu; }
+    __device__ int slot_of(int a) const { return a < L.n_shared ? L.topk + a : a - L.n_shared; }
+    __device__ bool needs_dep(int64_t u) const { return slot_of((int)u / tpu) < L.topk; }
+    __device__ void unit(const uint8_t *jsm, int64_t u, QUnit &U) const {
+        const int a = (int)u / tpu, r = (int)u - a * tpu;
+        const MoeSlot &m = reinterpret_cast<const MoeSlot *>(jsm)[slot_of(a)];
+        U.type = m.type; U.rb = m.rb; U.sbs = m.sbs; U.nsplit = m.nsplit;
+        U.nsb = nsb_h;
+        U.tab = 0;
+        U.nlo = U.nhi = 8;
+        U.lo = m.a + (int64_t)r * 8 * m.rb;
+        U.hi = m.b + (int64_t)r * 8 * m.rb;
+    }
+    __device__ int n_tab() const { return 1; }
+    __device__ const uint8_t *tab_global() const { return xtab; }
+    __device__ const float *tab_src(int) const { return nullptr; }
+    // lanes 0-7: h = silu(g) * u in the reference's float arithmetic
+    // (src/sepia.c:1405-1410; shared experts: * gamma, src/sepia.c:1432-1444)
+    __device__ void finish(const uint8_t *, int64_t u, const QUnit &, double v, int lane) const {
+        const int a = (int)u / tpu, r = (int)u - a * tpu;
+        const int s = slot_of(a);
+        const float uv = (float)__shfl_sync(0xffffffffu, v, (lane + 8) & 31);
+        if (lane < 8) {
+            const float gv = (float)v;
+            const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, (float)exp(-(double)gv)));
+            float hv = __fmul_rn(__fmul_rn(gv, sig), uv);
+            if (s >= L.topk) hv = __fmul_rn(hv, weights[s]);
+            h[(int64_t)s * L.ff + (int64_t)r * 8 + lane] = hv;
+        }
+    }
+};
+
+// Units: (16-row tile of hidden, slot), slot-minor. The reducer writes each
+// slot's term (routed: E_j * w_j; shared: S_s, gamma already inside h);
+// k_combine sums them in slot order.
+struct DnJob {
+    MoeDev L;
+    const int32_t *idx;
+    const float *weights;
+    const uint8_t *htab;
+    float *slots_out;
+    int nsb_f, n_slots, n_tiles;
+    int sbs_r, nsplit_r, sbs_s, nsplit_s;
+    __device__ void init() {}
+    // the router finished before the gate/up kernel let its successors
+    // launch, so the expert ids are final already
+    __device__ void setup(uint8_t *jsm, int tid, bool after_dep) {
+        if (after_dep || tid >= n_slots) return;
+        MoeSlot &m = reinterpret_cast<MoeSlot *>(jsm)[tid];
+        if (tid >= L.topk) {
+            const int e = tid - L.topk;
+            m.a = L.sh_down + (int64_t)e * L.sh_down_stride;
+            m.rb = L.rb_sh_down; m.type = L.sh_down_type; m.sbs = sbs_s;
+            m.nsplit = (e % L.world == L.rank) ? nsplit_s : 0;
+        } else {
+            const int e = idx[tid];
+            const bool own = e >= 0 && e < L.n_routed && e % L.world == L.rank;
+            m.a = L.down + (own ? local_expert(L, e) : 0) * L.down_stride;
+            m.rb = L.rb_down; m.type = L.down_type; m.sbs = sbs_r;
+            m.nsplit = own ? nsplit_r : 0;
+        }
+        m.b = m.a;
+    }
+    __device__ int64_t n_units() const { return (int64_t)n_slots * n_tiles; }
+    __device__ bool needs_dep(int64_t) const { return false; }
+    __device__ void unit(const uint8_t *jsm, int64_t u, QUnit &U) const {
+        const int t = (int)u / n_slots, s = (int)u - t * n_slots;
+        const MoeSlot &m = reinterpret_cast<const MoeSlot *>(jsm)[s];
+        const int64_t r0 = (int64_t)t * 16;
+        const int nr = (int)imin64(16, L.hidden - r0);
+        U.type = m.type; U.rb = m.rb; U.sbs = m.sbs; U.nsplit = m.nsplit;
+        U.nsb = nsb_f;
+        U.tab = s;
+        U.nlo = min(8, nr);
+        U.nhi = max(0, nr - 8);
+        U.lo = m.a + r0 * m.rb;
+        U.hi = U.lo + 8 * m.rb;
+    }
+    __device__ int n_tab() const { return n_slots; }
+    __device__ const uint8_t *tab_global() const { return htab; }
+    __device__ const float *tab_src(int) const { return nullptr; }
+    __device__ void finish(const uint8_t *, int64_t u, const QUnit &, double v, int lane) const {
+        const int t = (int)u / n_slots, s = (int)u - t * n_slots;
+        const int64_t r0 = (int64_t)t * 16;
+        if (lane < 16 && r0 + lane < L.hidden) {
+            const float e = (float)v;
+            slots_out[(int64_t)s * L.hidden + r0 + lane] = (s < L.topk) ? __fmul_rn(e, weights[s]) : e;
+        }
+    }
+};
+
+template <typename Kern, typename... Args>
+static cudaError_t launch_pdl(Kern kern, unsigned grid, unsigned block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
 // ============================================================== host side
@@ -656,6 +825,109 @@ static int pick_tr(int64_t rb_pair, int64_t budget) {
     return tr;
 }
 
+// Tensor-core engine eligibility: K-quant formats it decodes, whole
+// superblocks, rows at 4-byte aligned addresses that agree mod 4 between
+// the gate and up matrices, and the tables in the work area.
+static bool rows_ok(const void *base, int64_t stride, int64_t rb) {
+    return ((reinterpret_cast<uintptr_t>(base) | (uintptr_t)stride | (uintptr_t)rb) & 3) == 0;
+}
+static bool engine_gateup_ok(const MoeDev &L, const SepiaMoeWork *ws) {
+    if (!ws->xtab || !ws->htab) return false;
+    if (L.hidden % kQK || L.ff % kQK || L.hidden / kQK > 64 || L.ff / kQK > 16) return false;
+    if (!mma_format(L.gate_type) || L.up_type != L.gate_type) return false;
+    if (!rows_ok(L.gate, L.gate_stride, L.rb_gate) || !rows_ok(L.up, L.up_stride, L.rb_up) ||
+        ((reinterpret_cast<uintptr_t>(L.gate) ^ reinterpret_cast<uintptr_t>(L.up)) & 3))
+        return false;
+    if (L.n_shared > 0) {
+        if (!mma_format(L.sh_gate_type) || L.sh_up_type != L.sh_gate_type) return false;
+        if (!rows_ok(L.sh_gate, L.sh_gate_stride, L.rb_sh_gate) || !rows_ok(L.sh_up, L.sh_up_stride, L.rb_sh_up) ||
+            ((reinterpret_cast<uintptr_t>(L.sh_gate) ^ reinterpret_cast<uintptr_t>(L.sh_up)) & 3))
+            return false;
+    }
+    return true;
+}
+static bool engine_down_ok(const MoeDev &L, const SepiaMoeWork *ws) {
+    if (!ws->htab || L.ff % kQK || L.ff / kQK > 16) return false;
+    if (!mma_format(L.down_type) || !rows_ok(L.down, L.down_stride, L.rb_down)) return false;
+    if (L.n_shared > 0 && (!mma_format(L.sh_down_type) || !rows_ok(L.sh_down, L.sh_down_stride, L.rb_sh_down)))
+        return false;
+    return true;
+}
+
+constexpr uint32_t kMoeRowBudget = 2400;    // bytes of one row per item
+
+static int launch_gateup_engine(const MoeDev &L, const SepiaMoeWork *ws, cudaStream_t st) {
+    DevInfo &di = dev_info();
+    GuJob J;
+    J.L = L; J.idx = ws->topk_idx; J.weights = ws->weights; J.h = ws->h;
+    J.xtab = ws->xtab;
+    J.nsb_h = (int)(L.hidden / kQK); J.tpu = (int)(L.ff / 8);
+    J.n_slots = L.topk + L.n_shared;
+    J.sbs_r = qe_sbs(L.gate_type, J.nsb_h, kMoeRowBudget, J.nsplit_r);
+    J.sbs_s = J.sbs_r; J.nsplit_s = J.nsplit_r;
+    if (L.n_shared) J.sbs_s = qe_sbs(L.sh_gate_type, J.nsb_h, kMoeRowBudget, J.nsplit_s);
+    if (!J.sbs_r || !J.sbs_s) return fail("moe: no tensor-core split for the gate/up rows");
+    const uint32_t row_max = std::max((uint32_t)J.sbs_r * qe_sb_bytes(L.gate_type),
+                                      L.n_shared ? (uint32_t)J.sbs_s * qe_sb_bytes(L.sh_gate_type) : 0u);
+    int cg, G;
+    qe_groups(std::max(J.sbs_r, J.sbs_s), cg, G);
+    QeLayout P;
+    int64_t smem = 0;
+    if (!qe_layout(P, G, cg, row_max, 1, J.nsb_h, di.smem_optin, smem))
+        return fail("moe: gate/up tile needs %lld B of shared memory", (long long)smem);
+    P.err = di.err;
+    const void *fn = (const void *)k_qengine<GuJob>;
+    if (!ensure_smem(fn, (int)smem)) return 0;
+    const int64_t units = (int64_t)J.n_slots * J.tpu;
+    const unsigned grid = (unsigned)std::min<int64_t>(units, di.sm_count);
+    return check(launch_pdl(k_qengine<GuJob>, grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, J, P),
+                 "moe gate/up (tensor cores) launch");
+}
+
+static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *out, float *slots_out,
+                              cudaStream_t st) {
+    DevInfo &di = dev_info();
+    DnJob J;
+    J.L = L; J.idx = ws->topk_idx; J.weights = ws->weights; J.htab = ws->htab;
+    J.slots_out = slots_out ? slots_out : ws->slots;
+    J.nsb_f = (int)(L.ff / kQK);
+    J.n_slots = L.topk + L.n_shared;
+    J.n_tiles = (int)((L.hidden + 15) / 16);
+    J.sbs_r = qe_sbs(L.down_type, J.nsb_f, kMoeRowBudget, J.nsplit_r);
+    J.sbs_s = J.sbs_r; J.nsplit_s = J.nsplit_r;
+    if (L.n_shared) J.sbs_s = qe_sbs(L.sh_down_type, J.nsb_f, kMoeRowBudget, J.nsplit_s);
+    if (!J.sbs_r || !J.sbs_s) return fail("moe: no tensor-core split for the down rows");
+    const uint32_t row_max = std::max((uint32_t)J.sbs_r * qe_sb_bytes(L.down_type),
+                                      L.n_shared ? (uint32_t)J.sbs_s * qe_sb_bytes(L.sh_down_type) : 0u);
+    int cg, G;
+    qe_groups(std::max(J.sbs_r, J.sbs_s), cg, G);
+    QeLayout P;
+    int64_t smem = 0;
+    if (!qe_layout(P, G, cg, row_max, J.n_slots, J.nsb_f, di.smem_optin, smem))
+        return fail("moe: down tile needs %lld B of shared memory", (long long)smem);
+    P.err = di.err;
+    const void *fn = (const void *)k_qengine<DnJob>;
+    if (!ensure_smem(fn, (int)smem)) return 0;
+    if (slots_out &&
+        !check(cudaMemsetAsync(slots_out, 0, (size_t)J.n_slots * L.hidden * sizeof(float), st), "moe slot clear"))
+        return 0;
+    // tables of every slot's h, then the down projections, then the combine
+    const int tab_warps = J.n_slots * J.nsb_f;
+    if (!check(launch_pdl(k_xtab, (unsigned)((tab_warps + 7) / 8), 256, 0, st, (const float *)ws->h, (int64_t)L.ff,
+                          J.n_slots, J.nsb_f, ws->htab),
+               "moe h tables launch"))
+        return 0;
+    const int64_t units = (int64_t)J.n_slots * J.n_tiles;
+    const unsigned grid = (unsigned)std::min<int64_t>(units, di.sm_count);
+    if (!check(launch_pdl(k_qengine<DnJob>, grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, J, P),
+               "moe down (tensor cores) launch"))
+        return 0;
+    if (slots_out) return 1;
+    return check(launch_pdl(k_combine, (unsigned)((L.hidden + 255) / 256), 256, 0, st, (const float *)J.slots_out,
+                            J.n_slots, L.hidden, out),
+                 "moe combine launch");
+}
+
 int launch_router(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaStream_t st) {
     const int n_total = L.n_routed + L.n_shared;
     if (n_total > kRouterMaxExperts) return fail("moe: %d experts exceed the router's %d", n_total, kRouterMaxExperts);
@@ -663,13 +935,16 @@ int launch_router(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaS
         return fail("moe: hidden %lld exceeds the router's %d", (long long)L.hidden, kRouterMaxChunks * kRouterChunk);
     if (!ws->router_part) return fail("moe: work area has no router partials (carve it with moe_work_carve)");
     const int64_t chunks = (int64_t)n_total * router_chunks(L.hidden);
-    const unsigned grid = (unsigned)((chunks + kRouterWarps - 1) / kRouterWarps);
-    k_router<<<grid, kRouterWarps * 32, 0, st>>>(L, x, ws->logits, ws->topk_idx, ws->weights, ws->counter,
-                                                  ws->router_part);
-    return check(cudaGetLastError(), "moe router launch");
+    uint8_t *xtab = engine_gateup_ok(L, ws) ? ws->xtab : nullptr;
+    const int64_t warps = chunks + (xtab ? L.hidden / kQK : 0);
+    const unsigned grid = (unsigned)((warps + kRouterWarps - 1) / kRouterWarps);
+    return check(launch_pdl(k_router, grid, kRouterWarps * 32, 0, st, L, x, ws->logits, ws->topk_idx, ws->weights,
+                            ws->counter, ws->router_part, xtab),
+                 "moe router launch");
 }
 
 int launch_gateup(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaStream_t st) {
+    if (engine_gateup_ok(L, ws)) return launch_gateup_engine(L, ws, st);
     DevInfo &di = dev_info();
     GuParams G;
     G.L = L; G.x = x; G.idx = ws->topk_idx; G.weights = ws->weights; G.h = ws->h;
@@ -697,7 +972,9 @@ int launch_gateup(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaS
     return check(cudaGetLastError(), "moe gate/up launch");
 }
 
+// The down engine reads the h tables that only the gate/up engine builds.
 int launch_down(const MoeDev &L, const SepiaMoeWork *ws, float *out, float *slots_out, cudaStream_t st) {
+    if (engine_gateup_ok(L, ws) && engine_down_ok(L, ws)) return launch_down_engine(L, ws, out, slots_out, st);
     DevInfo &di = dev_info();
     const int n_slots = L.topk + L.n_shared;
     DnParams D;
@@ -726,6 +1003,7 @@ int launch_down(const MoeDev &L, const SepiaMoeWork *ws, float *out, float *slot
 
 int launch_experts(const MoeDev &L, const float *x, const SepiaMoeWork *ws, float *out, float *slots_out,
                    cudaStream_t st) {
+    // the down engine reads the h tables that only the gate/up engine builds
     return launch_gateup(L, x, ws, st) && launch_down(L, ws, out, slots_out, st);
 }
 
@@ -746,8 +1024,11 @@ extern "C" size_t sepia_cuda_moe_work_bytes(const SepiaMoeLayer *L) {
     add(n_slots * (size_t)L->hidden * 4);  // slots
     add(256);                         // counter
     add(n_total * (size_t)router_chunks(L->hidden) * 8);  // router_part
+    add((size_t)(L->hidden / kQK) * kTabSB);                        // xtab
+    add(n_slots * (size_t)(L->ff / kQK) * kTabSB);                  // htab
     return b;
 }
+
 
 extern "C" int sepia_cuda_moe_work_carve(const SepiaMoeLayer *L, void *base, size_t bytes, SepiaMoeWork *ws) {
     if (!L || !base || !ws) return fail("moe_work_carve: null argument");
@@ -764,6 +1045,8 @@ extern "C" int sepia_cuda_moe_work_carve(const SepiaMoeLayer *L, void *base, siz
     ws->slots = (float *)take(n_slots * (size_t)L->hidden * 4);
     ws->counter = (unsigned int *)take(256);
     ws->router_part = (double *)take(n_total * (size_t)router_chunks(L->hidden) * 8);
+    ws->xtab = take((size_t)(L->hidden / kQK) * kTabSB);
+    ws->htab = take(n_slots * (size_t)(L->ff / kQK) * kTabSB);
     return 1;
 }
 

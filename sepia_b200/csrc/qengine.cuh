@@ -1,0 +1,343 @@
+// sepia_b200/csrc/qengine.cuh -- the streaming tensor-core GEMV engine
+// behind matvec_q and the MoE gate/up and down projections.
+//
+// Work is a list of units; a unit is one 16-row tile (rows 0-7 and 8-15 may
+// come from two matrices, e.g. 8 gate rows and the 8 matching up rows) over
+// all superblocks of the input, possibly cut into `nsplit` items along the
+// superblocks so that one item fits a shared-memory stage. CTAs take units
+// round robin (unit u goes to CTA u % grid) and walk every item of a unit in
+// order, so one CTA owns a unit's whole row sum (deterministic).
+//
+// Warps of a CTA:
+//   producer   one thread copies each item's rows into a stage slot with
+//              1-D cp.async.bulk (one copy per row, 16-byte aligned rows,
+//              padded pitch so the 8 rows of an MMA tile hit distinct
+//              shared-memory banks), completing on the slot's "full" mbarrier;
+//   consumers  G groups of cg warps; group k % G takes item k, its warps
+//              splitting the item's superblocks into cg chunks; each warp
+//              runs the format's tile walk (qtile.cuh) and stores its fp64
+//              row partials, then arrives on the slot's "ready" mbarrier;
+//   reducer    sums the cg partials of every row in chunk order, adds the
+//              unit's splits in order, runs the job's epilogue on the
+//              finished rows and releases the slot on its "empty" mbarrier.
+// Every wait is bounded (mbar_wait): on timeout the kernel records an error
+// code and the waiting role stops.
+#pragma once
+#include "qtile.cuh"
+#include "stream.cuh"
+
+#include <algorithm>
+
+namespace sepia {
+
+constexpr int kQeMaxCons = 16;
+constexpr int kQeMaxStages = 8;
+constexpr int kQeThreadsMax = (kQeMaxCons + 2) * 32;
+
+struct QUnit {
+    int type;              // quant format of both halves
+    int nsb;               // superblocks per row
+    int sbs;               // superblocks per split (the last split may be shorter)
+    int nsplit;
+    int nlo, nhi;          // valid rows in 0-7 and 8-15
+    const uint8_t *lo;     // row i < 8 starts at lo + i*rb
+    const uint8_t *hi;     // row 8+i starts at hi + i*rb
+    int64_t rb;
+    int tab;               // activation table index
+};
+
+__host__ __device__ inline int qe_sb_bytes(int t) { return t == T_Q2_K ? 84 : t == T_Q3_K ? 110 : 144; }
+// Row pitch in a stage for `bytes` bytes per row: 16-byte multiple with an
+// odd number of 16-byte granules (8 consecutive rows -> 8 distinct banks).
+__host__ __device__ inline uint32_t qe_pitch(uint32_t bytes) {
+    uint32_t p = (bytes + 32 + 15) & ~15u;     // + the partial granules around an unaligned row
+    if (((p >> 4) & 1) == 0) p += 16;
+    return p;
+}
+
+// Slot and phase of a stage ring, advanced item by item (no divisions).
+struct QeRing {
+    int slot = 0;
+    uint32_t phase = 0;
+    __device__ __forceinline__ void next(int stages) {
+        if (++slot == stages) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
+struct QeLayout {
+    int G, cg, stages;
+    uint32_t slot_bytes, red_off, tab_off, stage_off;
+    int n_tab, tab_nsb;    // tables x superblocks each
+    int *err;
+};
+
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream serialization attribute may start while its predecessor runs;
+// griddep_wait() blocks until the predecessor grid completed and its writes
+// are visible (a no-op for a normal launch), griddep_launch() lets the
+// successor start launching.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+constexpr int kQeJobSmem = 1024;     // shared scratch of a job (per-CTA unit tables)
+
+// Job interface (see k_qengine):
+//   void init();                              // per-thread setup (reads only data
+//                                             //   that exists before griddep_wait)
+//   void setup(uint8_t *jsm, int tid, bool after_dep);
+//                                             // fill the job's shared scratch; called by
+//                                             //   every thread before and after griddep_wait
+//   int64_t n_units() const;
+//   bool needs_dep(int64_t u) const;          // unit u's rows depend on the predecessor
+//   void unit(const uint8_t *jsm, int64_t u, QUnit &U) const;   // U.nsplit = 0: nothing to do
+//   int n_tab() const;                        // activation tables (<= QeLayout.n_tab)
+//   const uint8_t *tab_global() const;        // prebuilt tables [n_tab][tab_nsb] in global
+//                                             //   memory, or nullptr to build them here
+//   const float *tab_src(int t) const;       // activations of table t (16-byte aligned)
+//   void finish(const uint8_t *jsm, int64_t u, const QUnit &U, double v, int lane) const;
+//       called by the 32 reducer lanes with v = row `lane`'s value (lane < 16)
+template <class Job>
+__global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, const QeLayout P) {
+    Job J = Jp;
+    J.init();
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_cons = P.G * P.cg, prod = n_cons, redw = n_cons + 1;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *ready = full + kQeMaxStages;
+    uint64_t *empty = ready + kQeMaxStages;
+    double *red = reinterpret_cast<double *>(smem + P.red_off);      // [stages][cg][16]
+    uint8_t *tab = smem + P.tab_off;
+    uint8_t *stage0 = smem + P.stage_off;
+    const int64_t n_units = J.n_units();
+    __shared__ __align__(16) uint8_t jsm[kQeJobSmem];
+    J.setup(jsm, threadIdx.x, false);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P.stages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&ready[s], P.cg);
+            mbar_init(&empty[s], 1);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    // producer: item k of this CTA goes to slot k % stages. Each row's bytes
+    // are fetched as the 16-byte granules that cover them (range_issue), so
+    // row i's data starts at stage + i*pitch + (its address & 15).
+    auto issue = [&](const QUnit &U, int sp, int slot) {
+        const int sbB = qe_sb_bytes(U.type);
+        const int s0 = sp * U.sbs, s1 = min(U.nsb, s0 + U.sbs);
+        const uint32_t bytes = (uint32_t)(s1 - s0) * (uint32_t)sbB;
+        const uint32_t pitch = qe_pitch(bytes);
+        const int64_t off = (int64_t)s0 * sbB;
+        uint8_t *dst = stage0 + (size_t)slot * P.slot_bytes;
+        uint32_t tx = 0;
+        for (int i = 0; i < U.nlo; i++) tx += range_copy_bytes(ByteRange{U.lo + i * U.rb + off, bytes});
+        for (int i = 0; i < U.nhi; i++) tx += range_copy_bytes(ByteRange{U.hi + i * U.rb + off, bytes});
+        mbar_arrive_expect_tx(&full[slot], tx);
+        for (int i = 0; i < U.nlo; i++) range_issue(dst + i * pitch, ByteRange{U.lo + i * U.rb + off, bytes}, &full[slot]);
+        for (int i = 0; i < U.nhi; i++)
+            range_issue(dst + (8 + i) * pitch, ByteRange{U.hi + i * U.rb + off, bytes}, &full[slot]);
+    };
+
+    // Producer state: next (unit, split) to issue, item count, ring position.
+    int64_t pu = blockIdx.x;
+    int psp = 0;
+    int64_t pk = 0;
+    QeRing pring;
+    QUnit PU;
+    PU.nsplit = 0;
+    // The first `stages` items need no empty-wait; those of units that do
+    // not depend on the predecessor kernel are issued before waiting for it.
+    if (warp == prod && lane == 0) {
+        while (pu < n_units && pk < P.stages && !J.needs_dep(pu)) {
+            if (psp == 0) J.unit(jsm, pu, PU);
+            if (psp < PU.nsplit) {
+                issue(PU, psp, pring.slot);
+                pk++;
+                pring.next(P.stages);
+            }
+            if (++psp >= PU.nsplit) {
+                psp = 0;
+                pu += gridDim.x;
+            }
+        }
+    }
+    griddep_wait();
+    if (threadIdx.x == 0) griddep_launch();
+    J.setup(jsm, threadIdx.x, true);
+    {
+        const int n_tab = J.n_tab();
+        const uint8_t *tg = J.tab_global();
+        if (tg) {
+            const int4 *src = reinterpret_cast<const int4 *>(tg);
+            int4 *dst = reinterpret_cast<int4 *>(tab);
+            const int n16 = n_tab * P.tab_nsb * kTabSB / 16;
+            for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = __ldcg(src + i);
+        } else {
+            for (int t = 0; t < n_tab; t++)
+                xtab_build(tab + (size_t)t * P.tab_nsb * kTabSB, J.tab_src(t), P.tab_nsb, warp, blockDim.x >> 5,
+                           lane);
+        }
+    }
+    __syncthreads();
+
+    if (warp == prod) {
+        if (lane == 0) {
+            // from round 1 on, item k waits for its slot's release in round - 1
+            bool ok = true;
+            while (pu < n_units) {
+                if (psp == 0) J.unit(jsm, pu, PU);
+                if (psp < PU.nsplit) {
+                    if (pk >= P.stages && !mbar_wait(&empty[pring.slot], pring.phase ^ 1u, P.err)) { ok = false; break; }
+                    issue(PU, psp, pring.slot);
+                    pk++;
+                    pring.next(P.stages);
+                }
+                if (++psp >= PU.nsplit) {
+                    psp = 0;
+                    pu += gridDim.x;
+                }
+            }
+            // no bulk copy may be in flight when the CTA exits
+            if (ok)
+                for (int64_t j = (pk > P.stages ? pk - P.stages : 0); j < pk; j++)
+                    mbar_wait(&full[j % P.stages], (uint32_t)((j / P.stages) & 1), nullptr);
+        }
+        return;
+    }
+
+    if (warp == redw) {
+        QeRing ring;
+        for (int64_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+            QUnit U;
+            J.unit(jsm, u, U);
+            if (U.nsplit == 0) continue;
+            double acc = 0.0;
+            bool ok = true;
+            for (int sp = 0; sp < U.nsplit; sp++) {
+                if (!mbar_wait(&ready[ring.slot], ring.phase, P.err)) { ok = false; break; }
+                if (lane < 16) {
+                    const double *rs = red + (size_t)ring.slot * P.cg * 16 + lane;
+                    for (int c = 0; c < P.cg; c++) acc += rs[c * 16];
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[ring.slot]);
+                ring.next(P.stages);
+            }
+            if (!ok) break;
+            J.finish(jsm, u, U, acc, lane);
+        }
+        return;
+    }
+
+    // consumers
+    const int grp = warp / P.cg, cw = warp % P.cg;
+    const LaneCtx C = lane_ctx(lane);
+    QeRing ring;
+    int g = 0;                        // group of the current item (item index % G)
+    for (int64_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+        QUnit U;
+        J.unit(jsm, u, U);
+        const uint8_t *te_base = tab + (size_t)U.tab * P.tab_nsb * kTabSB;
+        const int sbB = qe_sb_bytes(U.type);
+        for (int sp = 0; sp < U.nsplit; sp++) {
+            const int slot = ring.slot;
+            const uint32_t phase = ring.phase;
+            ring.next(P.stages);
+            const bool mine = (g == grp);
+            if (++g == P.G) g = 0;
+            if (!mine) continue;
+            if (!mbar_wait(&full[slot], phase, P.err)) return;
+            const int s0 = sp * U.sbs, s1 = min(U.nsb, s0 + U.sbs), n = s1 - s0;
+            const uint32_t pitch = qe_pitch((uint32_t)n * (uint32_t)sbB);
+            const int i0 = (cw * n) / P.cg, i1 = ((cw + 1) * n) / P.cg;
+            const uint8_t *st = stage0 + (size_t)slot * P.slot_bytes;
+            const int64_t off = (int64_t)s0 * sbB;
+            // rows past the tile's end hold stale bytes: their results are
+            // never read (rows are independent in the MMA)
+            const uintptr_t a_lo = reinterpret_cast<uintptr_t>(U.lo + C.gid * U.rb + off);
+            const uintptr_t a_hi = reinterpret_cast<uintptr_t>(U.hi + C.gid * U.rb + off);
+            double yg = 0.0, yg8 = 0.0;
+            tile_sbs_rt(U.type, st + C.gid * pitch + (a_lo & 15), st + (C.gid + 8) * pitch + (a_hi & 15),
+                        te_base + (size_t)s0 * kTabSB, i0, i1, (int)(a_lo & 2) >> 1, C, yg, yg8);
+            quad_sum(yg, yg8);
+            if (C.tig == 0) {
+                double *rs = red + ((size_t)slot * P.cg + cw) * 16;
+                rs[C.gid] = yg;
+                rs[C.gid + 8] = yg8;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ready[slot]);   // release: the partials above are visible to the reducer
+        }
+    }
+}
+
+// Activation tables in global memory: n_vec vectors of nsb superblocks
+// (vector v at x + v*x_stride, its tables at tab + v*nsb*kTabSB), one warp
+// per superblock.
+static __global__ void k_xtab(const float *x, int64_t x_stride, int n_vec, int nsb, uint8_t *tab) {
+    const int w = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
+    griddep_wait();
+    griddep_launch();
+    if (w >= n_vec * nsb) return;
+    const int v = w / nsb, sb = w - v * nsb;
+    xtab_build<true>(tab + ((size_t)v * nsb + sb) * kTabSB, x + v * x_stride + (int64_t)sb * kQK, 1, 0, 1,
+                     threadIdx.x & 31);
+}
+
+// Host: superblocks per split for a row of `nsb` superblocks of format t so
+// that one row's item bytes stay within `row_budget`; 0 if impossible.
+inline int qe_sbs(int t, int nsb, uint32_t row_budget, int &nsplit) {
+    const int sb = qe_sb_bytes(t);
+    int sbs = std::min(nsb, (int)(row_budget / (uint32_t)sb));
+    if (sbs <= 0) return 0;
+    nsplit = (nsb + sbs - 1) / sbs;
+    sbs = (nsb + nsplit - 1) / nsplit;          // balanced splits (the last may be shorter)
+    nsplit = (nsb + sbs - 1) / sbs;
+    return sbs;
+}
+
+// Host: consumers per group (cg) for items of at most `maxn` superblocks,
+// and groups G (items in flight), cg * G <= kQeMaxCons. Each consumer takes
+// up to 4 superblocks of an item (fewer when that leaves warps idle): the
+// per-item bookkeeping is then small against the superblocks' work.
+inline void qe_groups(int maxn, int &cg, int &G) {
+    for (int per = 4; per >= 1; per--) {
+        cg = (maxn + per - 1) / per;
+        if (cg > kQeMaxCons) { cg = kQeMaxCons; G = 1; return; }
+        G = std::min(4, kQeMaxCons / cg);
+        if (cg * G >= 12 || per == 1) return;
+    }
+}
+
+// Host: shared-memory layout for a launch. item_bytes_max = the largest
+// item's row bytes (one row); returns 0 if nothing fits.
+inline int qe_layout(QeLayout &P, int G, int cg, uint32_t item_row_bytes_max, int n_tab, int tab_nsb,
+                     int64_t smem_optin, int64_t &smem) {
+    P.G = G;
+    P.cg = cg;
+    P.n_tab = n_tab;
+    P.tab_nsb = tab_nsb;
+    P.slot_bytes = 16 * qe_pitch(item_row_bytes_max);
+    smem_optin -= kQeJobSmem;          // the kernel's static shared memory
+    P.stages = kQeMaxStages;
+    for (;;) {
+        P.red_off = (3 * kQeMaxStages * 8 + 127) & ~127u;
+        P.tab_off = P.red_off + ((P.stages * cg * 16 * 8 + 127) & ~127u);
+        P.stage_off = P.tab_off + (((uint32_t)n_tab * tab_nsb * kTabSB + 127) & ~127u);
+        smem = P.stage_off + (int64_t)P.stages * P.slot_bytes;
+        if (smem <= smem_optin || P.stages <= 2) break;
+        P.stages--;
+    }
+    // items in flight in the consumer groups, plus two being filled
+    while (P.G > 1 && P.stages < P.G + 2) P.G--;
+    return smem <= smem_optin;
+}
+
+}  // namespace sepia

@@ -9,7 +9,7 @@
 #include "../../include/sepia_cuda.h"
 #include "runtime.h"
 #include "stream.cuh"
-#include "mma_gemv.cuh"
+#include "qengine.cuh"
 
 #include <algorithm>
 #include <stdlib.h>
@@ -133,152 +133,70 @@ __global__ void __launch_bounds__(17 * 32) k_matvec(const MvParams P) {
 }
 
 // ------------------------------------------------------------------ tensor-core path
-// Q2_K rows on the integer tensor cores (mma_gemv.cuh). Units are 16-row
-// tiles. Warps: n_cons consumers (consumer c owns superblocks
-// [c*sbw, (c+1)*sbw) of every tile), one producer (bulk copies), one
-// reducer. Per stage slot three mbarriers: full (copy landed), ready (all
-// consumers deposited their fp64 row partials), empty (reducer summed them
-// in consumer order and stored the rows; the slot may be refilled).
-// Consumers never wait on each other.
-struct MvMmaParams {
+// Q2_K / Q3_K / Q4_K rows through the tensor-core engine (qengine.cuh):
+// units are 16-row tiles of the matrix, one activation table (x).
+struct MvJob {
     const uint8_t *w;
-    int64_t row_bytes;
+    int64_t rb, out_dim;
+    int type, nsb, sbs, nsplit;
     const float *x;
     float *y;
-    int64_t out_dim;
-    int nsb, n_cons, sbw, stages;
-    uint32_t slot_bytes, red_off, xl_off, stage_off;
-    int64_t num_units;
-    int *err;
+    __device__ void init() {}
+    __device__ void setup(uint8_t *, int, bool) {}
+    __device__ int64_t n_units() const { return (out_dim + 15) / 16; }
+    __device__ bool needs_dep(int64_t) const { return false; }
+    __device__ const uint8_t *tab_global() const { return nullptr; }
+    __device__ void unit(const uint8_t *, int64_t u, QUnit &U) const {
+        const int64_t r0 = u * 16;
+        const int nr = (int)imin64(16, out_dim - r0);
+        U.type = type; U.nsb = nsb; U.sbs = sbs; U.nsplit = nsplit; U.rb = rb; U.tab = 0;
+        U.nlo = min(8, nr);
+        U.nhi = max(0, nr - 8);
+        U.lo = w + r0 * rb;
+        U.hi = U.lo + 8 * rb;
+    }
+    __device__ int n_tab() const { return 1; }
+    __device__ const float *tab_src(int) const { return x; }
+    __device__ void finish(const uint8_t *, int64_t u, const QUnit &, double v, int lane) const {
+        const int64_t r = u * 16 + lane;
+        if (lane < 16 && r < out_dim) y[r] = (float)v;
+    }
 };
 
-constexpr int kMmaRows = 16;
-constexpr int kMmaStagesMax = 6;
+constexpr uint32_t kQeRowBudget = 2496;    // bytes of one row per item (16 rows ~ 40 KB)
 
-__global__ void __launch_bounds__(18 * 32, 1) k_matvec_mma_q2k(const MvMmaParams P) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_cons = P.n_cons, prod = n_cons, redw = n_cons + 1;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *ready = full + kMmaStagesMax;
-    uint64_t *empty = ready + kMmaStagesMax;
-    double *red = reinterpret_cast<double *>(smem + P.red_off);      // [stages][n_cons][16]
-    const XLimbs X = xlimbs_carve(smem + P.xl_off, P.nsb);
-    uint8_t *stage0 = smem + P.stage_off;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < P.stages; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&ready[s], n_cons);
-            mbar_init(&empty[s], 1);
-        }
-        fence_barrier_init();
-    }
-    __syncthreads();
-    if (warp == prod && lane == 0) {   // start streaming before building the tables
-        int64_t k = 0;
-        for (int64_t u = blockIdx.x; k < P.stages && u < P.num_units; k++, u += gridDim.x) {
-            const int64_t r0 = u * kMmaRows;
-            const ByteRange r{P.w + r0 * P.row_bytes, (uint32_t)(imin64(kMmaRows, P.out_dim - r0) * P.row_bytes)};
-            mbar_arrive_expect_tx(&full[k], range_copy_bytes(r));
-            range_issue(stage0 + (size_t)k * P.slot_bytes, r, &full[k]);
-        }
-    }
-    xlimbs_build(X, P.x, P.nsb, warp, blockDim.x >> 5, lane);
-
-    if (warp == prod) {
-        if (lane == 0) {
-            int64_t k = P.stages, issued = 0;
-            for (int64_t u = blockIdx.x; u < P.num_units && issued < P.stages; u += gridDim.x) issued++;
-            for (int64_t u = blockIdx.x + (int64_t)P.stages * gridDim.x; u < P.num_units; u += gridDim.x, k++) {
-                const int slot = (int)(k % P.stages);
-                if (!mbar_wait(&empty[slot], (uint32_t)(((k / P.stages) - 1) & 1), P.err)) break;
-                const int64_t r0 = u * kMmaRows;
-                const ByteRange r{P.w + r0 * P.row_bytes, (uint32_t)(imin64(kMmaRows, P.out_dim - r0) * P.row_bytes)};
-                mbar_arrive_expect_tx(&full[slot], range_copy_bytes(r));
-                range_issue(stage0 + (size_t)slot * P.slot_bytes, r, &full[slot]);
-                issued = k + 1;
-            }
-            for (int64_t j = (issued > P.stages ? issued - P.stages : 0); j < issued; j++)
-                mbar_wait(&full[j % P.stages], (uint32_t)((j / P.stages) & 1), nullptr);
-        }
-        return;
-    }
-    if (warp == redw) {
-        int64_t k = 0;
-        for (int64_t u = blockIdx.x; u < P.num_units; u += gridDim.x, k++) {
-            const int slot = (int)(k % P.stages);
-            if (!mbar_wait(&ready[slot], (uint32_t)((k / P.stages) & 1), P.err)) break;
-            const int64_t r0 = u * kMmaRows;
-            const int64_t nr = imin64(kMmaRows, P.out_dim - r0);
-            if (lane < nr) {
-                const double *rs = red + (size_t)slot * n_cons * kMmaRows + lane;
-                double s = 0.0;
-                for (int c = 0; c < n_cons; c++) s += rs[c * kMmaRows];
-                P.y[r0 + lane] = (float)s;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        }
-        return;
-    }
-
-    const int cw = warp;
-    const int sb0 = cw * P.sbw, sb1 = min(P.nsb, sb0 + P.sbw);
-    const int gid = lane >> 2, tig = lane & 3;
-    int64_t k = 0;
-    for (int64_t u = blockIdx.x; u < P.num_units; u += gridDim.x, k++) {
-        const int slot = (int)(k % P.stages);
-        if (!mbar_wait(&full[slot], (uint32_t)((k / P.stages) & 1), P.err)) break;
-        const int64_t r0 = u * kMmaRows;
-        const uint8_t *tile = range_data(stage0 + (size_t)slot * P.slot_bytes, ByteRange{P.w + r0 * P.row_bytes, 0});
-        double yg = 0.0, yg8 = 0.0;
-        tile16_q2k(tile, P.row_bytes, sb0, sb1, X, lane, yg, yg8);
-        tile16_finish(yg, yg8);
-        if (tig == 0) {
-            double *rs = red + ((size_t)slot * n_cons + cw) * kMmaRows;
-            rs[gid] = yg;
-            rs[gid + 8] = yg8;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ready[slot]);   // release: the partials above are visible to the reducer
-    }
+static int launch_matvec_engine(int t, const void *w, const float *x, float *y, int64_t out_dim, int64_t in_dim,
+                                int64_t rb, cudaStream_t st) {
+    DevInfo &di = dev_info();
+    MvJob J;
+    J.w = reinterpret_cast<const uint8_t *>(w);
+    J.rb = rb; J.out_dim = out_dim; J.type = t;
+    J.nsb = (int)(in_dim / kQK);
+    J.x = x; J.y = y;
+    J.sbs = qe_sbs(t, J.nsb, kQeRowBudget, J.nsplit);
+    if (!J.sbs) return fail("matvec_q: no tensor-core split for type %d", t);
+    QeLayout P;
+    int cg, G;
+    qe_groups(J.sbs, cg, G);
+    int64_t smem = 0;
+    if (!qe_layout(P, G, cg, (uint32_t)J.sbs * qe_sb_bytes(t), 1, J.nsb, di.smem_optin, smem))
+        return fail("matvec_q: tensor-core tile needs %lld B of shared memory", (long long)smem);
+    P.err = di.err;
+    const void *fn = (const void *)k_qengine<MvJob>;
+    if (!ensure_smem(fn, (int)smem)) return 0;
+    const int64_t units = (out_dim + 15) / 16;
+    const int64_t grid = std::min<int64_t>(units, (int64_t)di.sm_count);
+    k_qengine<MvJob><<<(unsigned)grid, (P.G * P.cg + 2) * 32, (size_t)smem, st>>>(J, P);
+    return check(cudaGetLastError(), "matvec_q (tensor cores) launch");
 }
 
-static int launch_matvec_mma_q2k(const void *w, const float *x, float *y, int64_t out_dim, int64_t in_dim,
-                                 int64_t rb, cudaStream_t st) {
-    DevInfo &di = dev_info();
-    MvMmaParams P;
-    P.w = reinterpret_cast<const uint8_t *>(w);
-    P.row_bytes = rb;
-    P.x = x; P.y = y; P.out_dim = out_dim;
-    P.nsb = (int)(in_dim / kQK);
-    P.n_cons = std::min(16, P.nsb);
-    P.sbw = (P.nsb + P.n_cons - 1) / P.n_cons;
-    P.n_cons = (P.nsb + P.sbw - 1) / P.sbw;
-    P.slot_bytes = slot_bytes_for((uint64_t)kMmaRows * rb);
-    P.stages = kMmaStagesMax;
-    int64_t smem = 0;
-    for (;;) {
-        P.red_off = 3 * kMmaStagesMax * 8 + 16;
-        P.red_off = (P.red_off + 127) & ~127u;
-        P.xl_off = P.red_off + ((P.stages * P.n_cons * kMmaRows * 8 + 127) & ~127);
-        P.stage_off = P.xl_off + ((xlimbs_bytes(P.nsb) + 127) & ~127);
-        smem = P.stage_off + (int64_t)P.stages * P.slot_bytes;
-        if (P.stages <= 2 || smem <= (int64_t)di.smem_optin) break;
-        P.stages--;
-    }
-    if (smem > di.smem_optin) return fail("matvec_q: tensor-core tile needs %lld B of shared memory", (long long)smem);
-    if (!ensure_smem((const void *)k_matvec_mma_q2k, (int)smem)) return 0;
-    P.num_units = (out_dim + kMmaRows - 1) / kMmaRows;
-    P.err = di.err;
-    const int threads = (P.n_cons + 2) * 32;
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_matvec_mma_q2k, threads, (size_t)smem);
-    if (per_sm < 1) per_sm = 1;
-    const int64_t grid = std::min<int64_t>(P.num_units, (int64_t)di.sm_count * per_sm);
-    k_matvec_mma_q2k<<<(unsigned)grid, threads, (size_t)smem, st>>>(P);
-    return check(cudaGetLastError(), "matvec_q (tensor cores) launch");
+// Can this call run on the engine? in_dim whole superblocks, x 16-byte
+// aligned (float4 table loads), every row at the same address mod 4 with
+// 4-byte aligned superblocks (2-byte for Q3_K).
+static bool engine_ok(int t, const void *w, const float *x, int64_t in_dim, int64_t rb, int64_t n_vec) {
+    const uintptr_t wa = reinterpret_cast<uintptr_t>(w);
+    return mma_format(t) && n_vec == 1 && in_dim % kQK == 0 && in_dim / kQK <= 64 && rb % 4 == 0 &&
+           (wa & (t == T_Q3_K ? 1 : 3)) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
 }
 
 // Exact dequantisation: one thread per 32-element part.
@@ -330,10 +248,8 @@ int launch_matvec_q(int t, const void *w, const float *x, float *y, int64_t out_
     const int64_t rb = host_row_bytes(t, in_dim);
     if (rb <= 0) return fail("matvec_q: unsupported ggml type %d or in_dim %lld not block-aligned", t, (long long)in_dim);
     if (!w || !x || !y) return fail("matvec_q: null pointer");
-    // Q2_K with 4-byte aligned rows runs on the integer tensor cores
-    if (t == T_Q2_K && n_vec == 1 && in_dim <= 16384 && ((reinterpret_cast<uintptr_t>(w) & 3) == 0) &&
-        ((reinterpret_cast<uintptr_t>(x) & 15) == 0))
-        return launch_matvec_mma_q2k(w, x, y, out_dim, in_dim, rb, st);
+    // K-quants with aligned rows run on the integer tensor cores
+    if (engine_ok(t, w, x, in_dim, rb, n_vec)) return launch_matvec_engine(t, w, x, y, out_dim, in_dim, rb, st);
     DevInfo &di = dev_info();
     const int nsb = (int)((in_dim + kQK - 1) / kQK);
     int c = 1, nwc = (nsb + 3) / 4;

@@ -1,0 +1,479 @@
+// sepia_b200/csrc/qtile.cuh -- exact quantized dot products on the integer
+// tensor cores, one 16-row tile and one 256-element superblock at a time.
+//
+// Why: a batch-1 GEMV over 2-4 bit weights is HBM-bound only if unpacking
+// costs about one instruction per weight. Decoding to floats and running
+// FMAs costs 3-7, so such a kernel is issue-bound far below the HBM
+// roofline. Here the packed fields are unpacked to 8-bit integers with a few
+// bit operations per 4 weights and the multiply-accumulate runs on the
+// tensor cores (mma.sync m16n8k32 / m16n8k16, u8 or s8 x s8 -> s32).
+//
+// Exactness: each superblock's 256 activations are written as integers
+// x_int = round(x * 2^(kXShift - e)), e = exponent of the superblock's
+// largest |x|, split into four balanced base-256 digits ("limbs", signed
+// bytes). The tensor core forms sum_k w_int[k] * limb_j[k] exactly in int32
+// for each limb j (MMA columns), and the limbs recombine exactly in fp64, so
+// a superblock's dot product is exact; only x's representation rounds, at
+// 2^-(kXShift+1) of the superblock's largest value. Scales and mins enter as
+// small integers (folded into the A operand, applied to the int32 partials
+// with IMAD, or as a second MMA over group sums), and the fp16 superblock
+// scales multiply once per superblock in fp64.
+//
+// Fragment layouts (lane = 4*gid + tig), m16n8k32:
+//   A (16 x 32): a0 = row gid,   k 4tig..+3      a1 = row gid+8, same k
+//                a2 = row gid,   k 16+4tig..+3   a3 = row gid+8, same k
+//   B (32 x 8):  b0 = k 4tig..+3, col gid        b1 = k 16+4tig..+3, col gid
+//   C (16 x 8):  c0 = (gid, 2tig) c1 = (gid, 2tig+1) c2 = (gid+8, 2tig) c3 = (gid+8, 2tig+1)
+// m16n8k16 uses only a0/a1 and b0. The k index of a part's MMA is the
+// element index within the part (32 consecutive elements).
+//
+// Two B arrangements come from one table entry e = (b0, b1) of limb gid&3:
+//   natural: columns 0-3 = limbs 0-3 of the whole part (gid >= 4: zero);
+//   split:   columns 0-3 = limbs of elements 0-15 only, columns 4-7 = limbs
+//            of elements 16-31 only, so one MMA yields the two 16-element
+//            groups' dots separately (lanes tig 0,1: first group; tig 2,3:
+//            second group) -- used where a per-group scale cannot be folded
+//            into A.
+// Either way lane tig's two C columns are limbs 2(tig&1) and 2(tig&1)+1, of
+// weight 256^(2(tig&1)) and 256^(2(tig&1)+1).
+#pragma once
+#include "quant_formats.cuh"
+
+namespace sepia {
+
+constexpr int kXShift = 29;      // x_int = round(x * 2^(kXShift - e)), |x_int| <= 2^30
+constexpr int kTabSB = 1296;     // activation-table bytes per superblock (16-byte multiple)
+// Table entry of one superblock:
+//   [0, 1024)     uint2 b[8 parts][tig*4 + limb]      natural k32 B fragments (4 limbs)
+//   [1024, 1152)  uint32 g16[tig*8 + limb]            k16 B fragments of the 16 group sums
+//   [1152, 1280)  uint32 g32[tig*8 + limb]            k16 B fragments of the 8 part sums
+//   [1280, 1284)  float unit = 2^(e - kXShift)        value of one x_int unit
+// Group and part sums reach 2^35 and take 5 limbs (columns 0-4 of a k16
+// MMA; columns 5-7 are zero).
+constexpr int kTabG16 = 1024, kTabG32 = 1152, kTabUnit = 1280;
+
+// Balanced base-256 digits of v (|v| <= 2^30): v = d0 + 256 d1 + 65536 d2 + 2^24 d3.
+__device__ __forceinline__ void limbs4(int v, int (&d)[4]) {
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        const int lo = ((v + 128) & 255) - 128;
+        d[j] = lo;
+        v = (v - lo) >> 8;
+    }
+    d[3] = v;
+}
+// Five balanced base-256 digits of v (|v| < 2^38).
+__device__ __forceinline__ void limbs5(long long v, int (&d)[5]) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int lo = (int)((v + 128) & 255) - 128;
+        d[j] = lo;
+        v = (v - lo) >> 8;
+    }
+    d[4] = (int)v;
+}
+
+// Build the table entries of x[0 .. nsb*256) into tab (shared or global
+// memory), one warp per superblock (x at least 4-byte aligned). Lane l owns
+// part l/4 and tig l%4: positions 32*part + 4*tig + {0..3} and +16.
+// CG: read x through L2 only (x was written by other CTAs of this grid).
+template <bool CG = false>
+__device__ inline void xtab_build(uint8_t *tab, const float *x, int nsb, int warp, int nwarps, int lane) {
+    const int part = lane >> 2, tig = lane & 3;
+    for (int sb = warp; sb < nsb; sb += nwarps) {
+        uint8_t *te = tab + (size_t)sb * kTabSB;
+        const float *xs = x + (size_t)sb * kQK + 32 * part + 4 * tig;
+        float4 lo, hi;
+        if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+            lo = CG ? __ldcg(reinterpret_cast<const float4 *>(xs)) : *reinterpret_cast<const float4 *>(xs);
+            hi = CG ? __ldcg(reinterpret_cast<const float4 *>(xs + 16)) : *reinterpret_cast<const float4 *>(xs + 16);
+        } else {
+            lo = make_float4(xs[0], xs[1], xs[2], xs[3]);
+            hi = make_float4(xs[16], xs[17], xs[18], xs[19]);
+        }
+        const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(v[j]));
+        m = warp_max(m);
+        int e = (m > 0.f) ? ((__float_as_int(m) >> 23) & 0xFF) - 127 : 0;
+        e = max(-90, min(e, 90));
+        const float scale = __int_as_float((127 + kXShift - e) << 23);
+        int xi[8];
+        uint32_t w0[4] = {0, 0, 0, 0}, w1[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            xi[j] = __float2int_rn(v[j] * scale);
+            int d[4];
+            limbs4(xi[j], d);
+#pragma unroll
+            for (int l = 0; l < 4; l++) {
+                if (j < 4) w0[l] |= (uint32_t)(d[l] & 255) << (8 * j);
+                else w1[l] |= (uint32_t)(d[l] & 255) << (8 * (j - 4));
+            }
+        }
+        uint2 *bd = reinterpret_cast<uint2 *>(te) + part * 16 + tig * 4;
+#pragma unroll
+        for (int l = 0; l < 4; l++) bd[l] = make_uint2(w0[l], w1[l]);
+        // group sums: group 2*part = elements 0-15 of the part (the xi[0..3]
+        // of its 4 lanes), group 2*part+1 = elements 16-31
+        long long g0 = (long long)xi[0] + xi[1] + xi[2] + xi[3], g1 = (long long)xi[4] + xi[5] + xi[6] + xi[7];
+        g0 += __shfl_xor_sync(0xffffffffu, g0, 1);
+        g0 += __shfl_xor_sync(0xffffffffu, g0, 2);
+        g1 += __shfl_xor_sync(0xffffffffu, g1, 1);
+        g1 += __shfl_xor_sync(0xffffffffu, g1, 2);
+        // k16 fragment words: lane (gid = limb, t) holds k = 4t..4t+3
+        uint8_t *g16 = te + kTabG16, *g32 = te + kTabG32;
+        if (tig == 0) {
+            int d0[5], d1[5], dp[5];
+            limbs5(g0, d0);
+            limbs5(g1, d1);
+            limbs5(g0 + g1, dp);
+#pragma unroll
+            for (int l = 0; l < 5; l++) {
+                // groups 2p, 2p+1 -> word t = p/2, bytes 2(p&1), 2(p&1)+1
+                uint8_t *wp = g16 + 4 * ((part >> 1) * 8 + l);
+                wp[2 * (part & 1)] = (uint8_t)(d0[l] & 255);
+                wp[2 * (part & 1) + 1] = (uint8_t)(d1[l] & 255);
+                // part p -> word t = p/4, byte p&3 (k 8..15 are zero)
+                g32[4 * ((part >> 2) * 8 + l) + (part & 3)] = (uint8_t)(dp[l] & 255);
+            }
+        }
+        // zero words: limbs 5-7 everywhere, and k 8..15 of the part sums
+        if (lane < 12) {
+            const int t = lane / 3, l = 5 + lane % 3;
+            reinterpret_cast<uint32_t *>(g16)[t * 8 + l] = 0u;
+            reinterpret_cast<uint32_t *>(g32)[t * 8 + l] = 0u;
+        } else if (lane < 28) {
+            const int t = 2 + (lane - 12) / 8, l = (lane - 12) % 8;
+            reinterpret_cast<uint32_t *>(g32)[t * 8 + l] = 0u;
+        }
+        if (lane == 0) *reinterpret_cast<float *>(te + kTabUnit) = __int_as_float((127 - kXShift + e) << 23);
+    }
+}
+
+// ------------------------------------------------------------ MMA wrappers
+__device__ __forceinline__ void mma_k32(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// C = A.B (no accumulator input)
+__device__ __forceinline__ void mma_k32_z(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void mma_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+}
+__device__ __forceinline__ void mma_k16_ss(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+}
+
+// byte j of w as a 32-bit integer
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int j) { return __byte_perm(w, 0u, 0x4440u + j); }
+__device__ __forceinline__ uint32_t ldw(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
+
+// Per-lane constants of a tile walk.
+struct LaneCtx {
+    int gid, tig;
+    uint32_t boff;       // byte offset of the lane's B entry in a part's 128 bytes
+    uint32_t goff;       // byte offset of the lane's k16 group-sum B word
+    uint32_t mlo, mhi;   // split layout: keep b0 (columns 0-3) / b1 (columns 4-7)
+    float lwn;           // natural layout: weight of the lane's first limb column (0 for tig 2,3)
+    float lws;           // split layout: same, every lane
+    float lwg;           // group-sum MMAs (8 limb columns): 256^(2 tig)
+};
+__device__ __forceinline__ LaneCtx lane_ctx(int lane) {
+    LaneCtx L;
+    L.gid = lane >> 2;
+    L.tig = lane & 3;
+    // columns 4-7 read the entries of limbs 0-3 again: in the natural layout
+    // their results (lanes tig 2,3) are duplicates and get weight 0
+    L.boff = (uint32_t)(L.tig * 4 + (L.gid & 3)) * 8u;
+    L.goff = (uint32_t)(L.tig * 8 + L.gid) * 4u;
+    L.mlo = (L.gid < 4) ? 0xFFFFFFFFu : 0u;
+    L.mhi = ~L.mlo;
+    L.lws = (L.tig & 1) ? 65536.0f : 1.0f;
+    L.lwn = (L.tig < 2) ? L.lws : 0.0f;
+    L.lwg = (L.tig == 0) ? 1.0f : (L.tig == 1) ? 65536.0f : (L.tig == 2) ? 4294967296.0f : 0.0f;
+    return L;
+}
+
+__device__ __forceinline__ uint2 ld_b(const uint8_t *te, int p, const LaneCtx &C) {
+    return *reinterpret_cast<const uint2 *>(te + p * 128 + C.boff);
+}
+__device__ __forceinline__ uint32_t ld_g(const uint8_t *te, int off, const LaneCtx &C) {
+    return *reinterpret_cast<const uint32_t *>(te + off + C.goff);
+}
+__device__ __forceinline__ float ld_unit(const uint8_t *te) { return *reinterpret_cast<const float *>(te + kTabUnit); }
+
+// byte j of w sign-extended to 32 bits (prmt with the sign-replicate bit
+// set in the selector nibbles of bytes 1-3)
+__device__ __forceinline__ int sbyte_of(uint32_t w, int j) {
+    int r;
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"((uint32_t)(j | ((j | 8) << 4) | ((j | 8) << 8) | ((j | 8) << 12))));
+    return r;
+}
+
+// exact value of the lane's two limb columns: (lo + 256 hi) * lw
+__device__ __forceinline__ double limb_pair(int lo, int hi, float lw) {
+    return ((double)lo + 256.0 * (double)hi) * (double)lw;
+}
+
+// ------------------------------------------------------------------ Q2_K
+// 84-byte superblock: scales[16] (low nibble scale, high nibble min of each
+// 16-element group), qs[64], d, dmin (fp16). Element 128h + 32s + l is the
+// 2-bit field at shift 2s of qs[32h + l] (src/quants.c dequantize_row_q2_K).
+// The scale nibble multiplies the field inside A (product <= 180 fits u8);
+// fields at odd s are masked in place (x4) and accumulated separately.
+__device__ __forceinline__ void sb_q2k(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const LaneCtx &C,
+                                       double &yg, double &yg8) {
+    const int tig = C.tig;
+    uint32_t sl[4], sl8[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        sl[j] = ldw(bg + 4 * j) & 0x0F0F0F0Fu;
+        sl8[j] = ldw(bg8 + 4 * j) & 0x0F0F0F0Fu;
+    }
+    int c[4] = {0, 0, 0, 0}, c2[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const uint8_t *q = bg + 16 + 32 * h, *q8 = bg8 + 16 + 32 * h;
+        const uint32_t w[4] = {ldw(q + 4 * tig), ldw(q8 + 4 * tig), ldw(q + 16 + 4 * tig), ldw(q8 + 16 + 4 * tig)};
+        uint32_t w4[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) w4[r] = w[r] >> 4;
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            const int p = 4 * h + s;                                   // groups 2p, 2p+1
+            const uint32_t m = (s & 1) ? 0x0C0C0C0Cu : 0x03030303u;
+            const uint32_t *src = (s < 2) ? w : w4;
+            const uint2 b = ld_b(te, p, C);
+            const uint32_t a0 = (src[0] & m) * byte_of(sl[p >> 1], 2 * (p & 1));
+            const uint32_t a1 = (src[1] & m) * byte_of(sl8[p >> 1], 2 * (p & 1));
+            const uint32_t a2 = (src[2] & m) * byte_of(sl[p >> 1], 2 * (p & 1) + 1);
+            const uint32_t a3 = (src[3] & m) * byte_of(sl8[p >> 1], 2 * (p & 1) + 1);
+            if (s & 1) mma_k32(c2, a0, a1, a2, a3, b.x, b.y);
+            else mma_k32(c, a0, a1, a2, a3, b.x, b.y);
+        }
+    }
+    // min term: A = the 16 min nibbles per row, B = group sums
+    int cm[4] = {0, 0, 0, 0};
+    mma_k16(cm, (ldw(bg + 4 * tig) >> 4) & 0x0F0F0F0Fu, (ldw(bg8 + 4 * tig) >> 4) & 0x0F0F0F0Fu,
+            ld_g(te, kTabG16, C));
+    // |c| < 2^21: the int pairs below cannot overflow
+    const int ia = (c[0] + (c2[0] >> 2)) + 256 * (c[1] + (c2[1] >> 2));
+    const int ia8 = (c[2] + (c2[2] >> 2)) + 256 * (c[3] + (c2[3] >> 2));
+    const int im = cm[0] + 256 * cm[1], im8 = cm[2] + 256 * cm[3];
+    const uint32_t dd = ldw(bg + 80), dd8 = ldw(bg8 + 80);
+    const float un = ld_unit(te);
+    const float u = un * C.lwn, ug = un * C.lwg;
+    yg += (double)(cvt16<true>(dd & 0xFFFFu) * u) * (double)ia - (double)(cvt16<true>(dd >> 16) * ug) * (double)im;
+    yg8 += (double)(cvt16<true>(dd8 & 0xFFFFu) * u) * (double)ia8 - (double)(cvt16<true>(dd8 >> 16) * ug) * (double)im8;
+}
+
+// ------------------------------------------------------------------ Q3_K
+// 110-byte superblock: hmask[32], qs[64], scales[12], d (fp16). Element
+// 128h + 32s + l: u = ((qs[32h+l] >> 2s) & 3) | (bit p of hmask[l]) << 2,
+// p = 4h + s; value = u - 4; group g = 2p + (l >= 16) has the signed 6-bit
+// scale s_g (src/quants.c dequantize_row_q3_K). A holds u (unsigned, odd s
+// in place x4); the split B layout gives per-group partials C_g, scaled by
+// s_g with IMAD; the -4 offset is -4 * sum_g s_g G_g, one s8 x s8 k16 MMA
+// over the group sums G_g.
+// A 110-byte superblock at an odd index of a row sits 2 bytes off a 4-byte
+// boundary; its words are assembled from the two aligned words around them.
+template <bool ODD>
+__device__ __forceinline__ uint32_t ldw2(const uint8_t *p) {
+    if constexpr (ODD) return __byte_perm(ldw(p - 2), ldw(p + 2), 0x5432);
+    else return ldw(p);
+}
+
+// signed scales (sc - 32) of groups 4i..4i+3 as bytes of G[i]
+template <bool ODD>
+__device__ __forceinline__ void q3k_scales(const uint8_t *sc, uint32_t (&G)[4]) {
+    const uint32_t S0 = ldw2<ODD>(sc), S1 = ldw2<ODD>(sc + 4), S2 = ldw2<ODD>(sc + 8);
+    uint32_t U[4];
+    U[0] = (S0 & 0x0F0F0F0Fu) | ((S2 & 0x03030303u) << 4);
+    U[1] = (S1 & 0x0F0F0F0Fu) | (((S2 >> 2) & 0x03030303u) << 4);
+    U[2] = ((S0 >> 4) & 0x0F0F0F0Fu) | (((S2 >> 4) & 0x03030303u) << 4);
+    U[3] = ((S1 >> 4) & 0x0F0F0F0Fu) | (((S2 >> 6) & 0x03030303u) << 4);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        // 6-bit unsigned -> signed byte (sc - 32): flip bit 5, then copy the
+        // new bit 5 into bits 6 and 7
+        const uint32_t t = U[i] ^ 0x20202020u, sg = t & 0x20202020u;
+        G[i] = t | (sg * 6u);
+    }
+}
+
+template <bool ODD>
+__device__ __forceinline__ void sb_q3k(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const LaneCtx &C,
+                                       double &yg, double &yg8) {
+    const int tig = C.tig, t = tig >> 1;
+    uint32_t G[4], G8[4];
+    q3k_scales<ODD>(bg + 96, G);
+    q3k_scales<ODD>(bg8 + 96, G8);
+    const uint32_t hm[4] = {ldw2<ODD>(bg + 4 * tig), ldw2<ODD>(bg8 + 4 * tig), ldw2<ODD>(bg + 16 + 4 * tig),
+                            ldw2<ODD>(bg8 + 16 + 4 * tig)};
+    int acc[4] = {0, 0, 0, 0}, accq[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const uint8_t *q = bg + 32 + 32 * h, *q8 = bg8 + 32 + 32 * h;
+        const uint32_t w[4] = {ldw2<ODD>(q + 4 * tig), ldw2<ODD>(q8 + 4 * tig), ldw2<ODD>(q + 16 + 4 * tig),
+                               ldw2<ODD>(q8 + 16 + 4 * tig)};
+        uint32_t w4[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) w4[r] = w[r] >> 4;
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            const int p = 4 * h + s;
+            const uint32_t qm = (s & 1) ? 0x0C0C0C0Cu : 0x03030303u;
+            const int tb = (s & 1) ? 4 : 2;                 // bit that receives the high bit
+            const uint32_t hmk = 0x01010101u << tb;
+            const uint32_t *src = (s < 2) ? w : w4;
+            uint32_t a[4];
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const uint32_t hb = (tb >= p) ? (hm[r] << (tb - p)) : (hm[r] >> (p - tb));
+                a[r] = (src[r] & qm) | (hb & hmk);
+            }
+            const uint2 e = ld_b(te, p, C);
+            int cc[4];
+            mma_k32_z(cc, a[0], a[1], a[2], a[3], e.x & C.mlo, e.y & C.mhi);
+            // this lane's group: 2p + t
+            const int sg = sbyte_of(G[p >> 1], 2 * (p & 1) + t);
+            const int sg8 = sbyte_of(G8[p >> 1], 2 * (p & 1) + t);
+            int *ac = (s & 1) ? accq : acc;
+            ac[0] += sg * cc[0];
+            ac[1] += sg * cc[1];
+            ac[2] += sg8 * cc[2];
+            ac[3] += sg8 * cc[3];
+        }
+    }
+    // sum_g s_g G_g: A = signed scales of groups 4tig..4tig+3, B = the group
+    // sums' 5 limbs
+    int cm[4] = {0, 0, 0, 0};
+    {
+        const uint32_t gw = (tig == 0) ? G[0] : (tig == 1) ? G[1] : (tig == 2) ? G[2] : G[3];
+        const uint32_t gw8 = (tig == 0) ? G8[0] : (tig == 1) ? G8[1] : (tig == 2) ? G8[2] : G8[3];
+        mma_k16_ss(cm, gw, gw8, ld_g(te, kTabG16, C));
+    }
+    const int v0 = acc[0] + (accq[0] >> 2), v1 = acc[1] + (accq[1] >> 2);
+    const int v2 = acc[2] + (accq[2] >> 2), v3 = acc[3] + (accq[3] >> 2);
+    const float u = ld_unit(te);
+    yg += (double)(cvt16<true>(lds_u16(bg + 108)) * u) * (limb_pair(v0, v1, C.lws) - 4.0 * limb_pair(cm[0], cm[1], C.lwg));
+    yg8 += (double)(cvt16<true>(lds_u16(bg8 + 108)) * u) * (limb_pair(v2, v3, C.lws) - 4.0 * limb_pair(cm[2], cm[3], C.lwg));
+}
+
+// ------------------------------------------------------------------ Q4_K
+// 144-byte superblock: d, dmin (fp16), scales[12] (6-bit scale and min of
+// each 32-element part), qs[128]. Part p: nibble (p&1) of qs[32(p>>1) + l]
+// (src/quants.c dequantize_row_q4_K). One MMA per part into fresh
+// accumulators, scaled by the part's scale with IMAD; the mins are one k16
+// MMA over the part sums.
+__device__ __forceinline__ void q4k_scales(const uint8_t *s, uint32_t &sc0, uint32_t &sc1, uint32_t &m0,
+                                           uint32_t &m1) {
+    const uint32_t W0 = ldw(s), W1 = ldw(s + 4), W2 = ldw(s + 8);
+    sc0 = W0 & 0x3F3F3F3Fu;
+    m0 = W1 & 0x3F3F3F3Fu;
+    sc1 = (W2 & 0x0F0F0F0Fu) | ((W0 >> 2) & 0x30303030u);
+    m1 = ((W2 >> 4) & 0x0F0F0F0Fu) | ((W1 >> 2) & 0x30303030u);
+}
+
+__device__ __forceinline__ void sb_q4k(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const LaneCtx &C,
+                                       double &yg, double &yg8) {
+    const int tig = C.tig;
+    uint32_t sc0, sc1, m0, m1, sc08, sc18, m08, m18;
+    q4k_scales(bg + 4, sc0, sc1, m0, m1);
+    q4k_scales(bg8 + 4, sc08, sc18, m08, m18);
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint8_t *q = bg + 16 + 32 * j, *q8 = bg8 + 16 + 32 * j;
+        const uint32_t w[4] = {ldw(q + 4 * tig), ldw(q8 + 4 * tig), ldw(q + 16 + 4 * tig), ldw(q8 + 16 + 4 * tig)};
+#pragma unroll
+        for (int hi = 0; hi < 2; hi++) {
+            const int p = 2 * j + hi;
+            uint32_t a[4];
+#pragma unroll
+            for (int r = 0; r < 4; r++) a[r] = hi ? ((w[r] >> 4) & 0x0F0F0F0Fu) : (w[r] & 0x0F0F0F0Fu);
+            const uint2 b = ld_b(te, p, C);
+            int cc[4];
+            mma_k32_z(cc, a[0], a[1], a[2], a[3], b.x, b.y);
+            const int s = (int)byte_of(p < 4 ? sc0 : sc1, p & 3), s8 = (int)byte_of(p < 4 ? sc08 : sc18, p & 3);
+            acc[0] += s * cc[0];
+            acc[1] += s * cc[1];
+            acc[2] += s8 * cc[2];
+            acc[3] += s8 * cc[3];
+        }
+    }
+    int cm[4] = {0, 0, 0, 0};
+    {
+        // k = part: lanes tig 0,1 hold parts 0-3, 4-7; k 8..15 meet zero B
+        const uint32_t am = (tig == 0) ? m0 : m1;
+        const uint32_t am8 = (tig == 0) ? m08 : m18;
+        mma_k16(cm, am, am8, ld_g(te, kTabG32, C));
+    }
+    const uint32_t dd = ldw(bg), dd8 = ldw(bg8);
+    const float un = ld_unit(te);
+    const float u = un * C.lwn, ug = un * C.lwg;
+    yg += (double)(cvt16<true>(dd & 0xFFFFu) * u) * ((double)acc[0] + 256.0 * (double)acc[1]) -
+          (double)(cvt16<true>(dd >> 16) * ug) * (double)(cm[0] + 256 * cm[1]);
+    yg8 += (double)(cvt16<true>(dd8 & 0xFFFFu) * u) * ((double)acc[2] + 256.0 * (double)acc[3]) -
+           (double)(cvt16<true>(dd8 >> 16) * ug) * (double)(cm[2] + 256 * cm[3]);
+}
+
+// ------------------------------------------------------------ dispatch
+__host__ __device__ constexpr bool mma_format(int t) { return t == T_Q2_K || t == T_Q3_K || t == T_Q4_K; }
+
+// Superblocks [i0, i1) of the staged rows (row gid at rg, row gid+8 at rg8,
+// superblock i at +i*sb_bytes); table entries start at te0 for i = 0.
+// Q2_K/Q4_K rows must start 4-byte aligned; Q3_K rows 2-byte aligned, with
+// flip = 1 when superblock 0 sits 2 bytes off a 4-byte boundary.
+template <int T>
+__device__ __forceinline__ void tile_sbs(const uint8_t *rg, const uint8_t *rg8, const uint8_t *te0, int i0, int i1,
+                                         int flip, const LaneCtx &C, double &yg, double &yg8) {
+    constexpr int SB = (T == T_Q2_K) ? 84 : (T == T_Q3_K) ? 110 : 144;
+    const uint8_t *r = rg + i0 * SB, *r8 = rg8 + i0 * SB, *te = te0 + (size_t)i0 * kTabSB;
+    for (int i = i0; i < i1; i++, r += SB, r8 += SB, te += kTabSB) {
+        if constexpr (T == T_Q2_K) sb_q2k(r, r8, te, C, yg, yg8);
+        else if constexpr (T == T_Q3_K) {
+            if ((i ^ flip) & 1) sb_q3k<true>(r, r8, te, C, yg, yg8);
+            else sb_q3k<false>(r, r8, te, C, yg, yg8);
+        } else sb_q4k(r, r8, te, C, yg, yg8);
+    }
+}
+
+__device__ __forceinline__ void tile_sbs_rt(int t, const uint8_t *rg, const uint8_t *rg8, const uint8_t *te0, int i0,
+                                            int i1, int flip, const LaneCtx &C, double &yg, double &yg8) {
+    switch (t) {
+    case T_Q2_K: tile_sbs<T_Q2_K>(rg, rg8, te0, i0, i1, flip, C, yg, yg8); break;
+    case T_Q3_K: tile_sbs<T_Q3_K>(rg, rg8, te0, i0, i1, flip, C, yg, yg8); break;
+    default: tile_sbs<T_Q4_K>(rg, rg8, te0, i0, i1, flip, C, yg, yg8); break;
+    }
+}
+
+// Sum the quad's 4 lanes: afterwards every lane of the quad holds the rows'
+// values (row gid in yg, gid+8 in yg8).
+__device__ __forceinline__ void quad_sum(double &yg, double &yg8) {
+    yg += __shfl_xor_sync(0xffffffffu, yg, 1);
+    yg8 += __shfl_xor_sync(0xffffffffu, yg8, 1);
+    yg += __shfl_xor_sync(0xffffffffu, yg, 2);
+    yg8 += __shfl_xor_sync(0xffffffffu, yg8, 2);
+}
+
+}  // namespace sepia

@@ -36,7 +36,8 @@ class SepiaMoeLayer(C.Structure):
 
 
 class SepiaMoeWork(C.Structure):
-    _fields_ = [("logits", vp), ("topk_idx", vp), ("weights", vp), ("h", vp), ("slots", vp), ("counter", vp), ("router_part", vp)]
+    _fields_ = [("logits", vp), ("topk_idx", vp), ("weights", vp), ("h", vp), ("slots", vp), ("counter", vp), ("router_part", vp),
+                ("xtab", vp), ("htab", vp)]
 
 
 class SepiaGpuMoeDesc(C.Structure):
