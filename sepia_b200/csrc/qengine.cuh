@@ -13,6 +13,7 @@
 //              1-D cp.async.bulk (one copy per row, 16-byte aligned rows,
 //              padded pitch so the 8 rows of an MMA tile hit distinct
 //              shared-memory banks), completing on the slot's "full" mbarrier;
+//              prebuilt activation tables arrive by one more bulk copy;
 //   consumers  G groups of cg warps; group k % G takes item k, its warps
 //              splitting the item's superblocks into cg chunks; each warp
 //              runs the format's tile walk (qtile.cuh) and stores its fp64
@@ -33,6 +34,7 @@ namespace sepia {
 constexpr int kQeMaxCons = 16;
 constexpr int kQeMaxStages = 8;
 constexpr int kQeThreadsMax = (kQeMaxCons + 2) * 32;
+constexpr uint32_t kQeTabChunk = 32768;    // bytes per table bulk copy
 
 struct QUnit {
     int type;              // quant format of both halves
@@ -109,6 +111,7 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *ready = full + kQeMaxStages;
     uint64_t *empty = ready + kQeMaxStages;
+    uint64_t *tabbar = empty + kQeMaxStages;      // prebuilt tables landed
     double *red = reinterpret_cast<double *>(smem + P.red_off);      // [stages][cg][16]
     uint8_t *tab = smem + P.tab_off;
     uint8_t *stage0 = smem + P.stage_off;
@@ -122,6 +125,7 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             mbar_init(&ready[s], P.cg);
             mbar_init(&empty[s], 1);
         }
+        mbar_init(tabbar, 1);
         fence_barrier_init();
     }
     __syncthreads();
@@ -171,21 +175,23 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
     griddep_wait();
     if (threadIdx.x == 0) griddep_launch();
     J.setup(jsm, threadIdx.x, true);
-    {
-        const int n_tab = J.n_tab();
-        const uint8_t *tg = J.tab_global();
-        if (tg) {
-            const int4 *src = reinterpret_cast<const int4 *>(tg);
-            int4 *dst = reinterpret_cast<int4 *>(tab);
-            const int n16 = n_tab * P.tab_nsb * kTabSB / 16;
-            for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = __ldcg(src + i);
-        } else {
-            for (int t = 0; t < n_tab; t++)
-                xtab_build(tab + (size_t)t * P.tab_nsb * kTabSB, J.tab_src(t), P.tab_nsb, warp, blockDim.x >> 5,
-                           lane);
+    // Activation tables: prebuilt ones arrive by one bulk copy (consumers
+    // wait on tabbar), otherwise every warp builds them here.
+    const uint8_t *tg = J.tab_global();
+    if (tg) {
+        if (warp == prod && lane == 0) {
+            const uint32_t bytes = (uint32_t)J.n_tab() * P.tab_nsb * kTabSB;
+            mbar_arrive_expect_tx(tabbar, bytes);
+            for (uint32_t o = 0; o < bytes; o += kQeTabChunk)
+                bulk_g2s(tab + o, tg + o, min(kQeTabChunk, bytes - o), tabbar);
         }
+        __syncthreads();                 // the job scratch written by setup()
+    } else {
+        const int n_tab = J.n_tab();
+        for (int t = 0; t < n_tab; t++)
+            xtab_build(tab + (size_t)t * P.tab_nsb * kTabSB, J.tab_src(t), P.tab_nsb, warp, blockDim.x >> 5, lane);
+        __syncthreads();
     }
-    __syncthreads();
 
     if (warp == prod) {
         if (lane == 0) {
@@ -205,6 +211,7 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
                 }
             }
             // no bulk copy may be in flight when the CTA exits
+            if (tg) mbar_wait(tabbar, 0, nullptr);
             if (ok)
                 for (int64_t j = (pk > P.stages ? pk - P.stages : 0); j < pk; j++)
                     mbar_wait(&full[j % P.stages], (uint32_t)((j / P.stages) & 1), nullptr);
@@ -237,6 +244,7 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
     }
 
     // consumers
+    if (tg && !mbar_wait(tabbar, 0, P.err)) return;
     const int grp = warp / P.cg, cw = warp % P.cg;
     const LaneCtx C = lane_ctx(lane);
     QeRing ring;
@@ -328,7 +336,7 @@ inline int qe_layout(QeLayout &P, int G, int cg, uint32_t item_row_bytes_max, in
     smem_optin -= kQeJobSmem;          // the kernel's static shared memory
     P.stages = kQeMaxStages;
     for (;;) {
-        P.red_off = (3 * kQeMaxStages * 8 + 127) & ~127u;
+        P.red_off = ((3 * kQeMaxStages + 1) * 8 + 127) & ~127u;
         P.tab_off = P.red_off + ((P.stages * cg * 16 * 8 + 127) & ~127u);
         P.stage_off = P.tab_off + (((uint32_t)n_tab * tab_nsb * kTabSB + 127) & ~127u);
         smem = P.stage_off + (int64_t)P.stages * P.slot_bytes;
