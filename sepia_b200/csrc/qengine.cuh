@@ -57,6 +57,16 @@ __host__ __device__ inline uint32_t qe_pitch(uint32_t bytes) {
     return p;
 }
 
+// Items of whole rows whose stride is a multiple of 16 bytes with an odd
+// number of 16-byte granules (8 consecutive rows then hit distinct banks) are
+// copied as two blocks of 8 rows -- two bulk copies instead of 16: the copy
+// engine's per-request cost dominates for rows of about a kilobyte.
+__host__ __device__ inline bool qe_block_mode(const QUnit &U) {
+    return U.nsplit == 1 && (U.rb & 15) == 0 && ((U.rb >> 4) & 1);
+}
+// Offset of the second block (rows 8-15) in a stage slot.
+__host__ __device__ inline uint32_t qe_hi_off(int64_t rb) { return (uint32_t)((8 * rb + 30 + 15) & ~(int64_t)15); }
+
 // Slot and phase of a stage ring, advanced item by item (no divisions).
 struct QeRing {
     int slot = 0;
@@ -137,9 +147,17 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
         const int sbB = qe_sb_bytes(U.type);
         const int s0 = sp * U.sbs, s1 = min(U.nsb, s0 + U.sbs);
         const uint32_t bytes = (uint32_t)(s1 - s0) * (uint32_t)sbB;
+        uint8_t *dst = stage0 + (size_t)slot * P.slot_bytes;
+        if (qe_block_mode(U)) {
+            // whole rows with a bank-friendly stride: two copies of 8 rows
+            const ByteRange rl{U.lo, (uint32_t)(U.nlo * U.rb)}, rh{U.hi, (uint32_t)(U.nhi * U.rb)};
+            mbar_arrive_expect_tx(&full[slot], range_copy_bytes(rl) + (U.nhi ? range_copy_bytes(rh) : 0u));
+            range_issue(dst, rl, &full[slot]);
+            if (U.nhi) range_issue(dst + qe_hi_off(U.rb), rh, &full[slot]);
+            return;
+        }
         const uint32_t pitch = qe_pitch(bytes);
         const int64_t off = (int64_t)s0 * sbB;
-        uint8_t *dst = stage0 + (size_t)slot * P.slot_bytes;
         uint32_t tx = 0;
         for (int i = 0; i < U.nlo; i++) tx += range_copy_bytes(ByteRange{U.lo + i * U.rb + off, bytes});
         for (int i = 0; i < U.nhi; i++) tx += range_copy_bytes(ByteRange{U.hi + i * U.rb + off, bytes});
@@ -272,8 +290,12 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             const uintptr_t a_lo = reinterpret_cast<uintptr_t>(U.lo + C.gid * U.rb + off);
             const uintptr_t a_hi = reinterpret_cast<uintptr_t>(U.hi + C.gid * U.rb + off);
             double yg = 0.0, yg8 = 0.0;
-            tile_sbs_rt(U.type, st + C.gid * pitch + (a_lo & 15), st + (C.gid + 8) * pitch + (a_hi & 15),
-                        te_base + (size_t)s0 * kTabSB, i0, i1, (int)(a_lo & 2) >> 1, C, yg, yg8);
+            const bool blk = qe_block_mode(U);
+            const uint8_t *rg = blk ? st + (reinterpret_cast<uintptr_t>(U.lo) & 15) + C.gid * U.rb
+                                    : st + C.gid * pitch + (a_lo & 15);
+            const uint8_t *rg8 = blk ? st + qe_hi_off(U.rb) + (reinterpret_cast<uintptr_t>(U.hi) & 15) + C.gid * U.rb
+                                     : st + (C.gid + 8) * pitch + (a_hi & 15);
+            tile_sbs_rt(U.type, rg, rg8, te_base + (size_t)s0 * kTabSB, i0, i1, (int)(a_lo & 2) >> 1, C, yg, yg8);
             quad_sum(yg, yg8);
             if (C.tig == 0) {
                 double *rs = red + ((size_t)slot * P.cg + cw) * 16;
