@@ -62,7 +62,7 @@ __host__ __device__ inline uint32_t qe_pitch(uint32_t bytes) {
 // copied as two blocks of 8 rows -- two bulk copies instead of 16: the copy
 // engine's per-request cost dominates for rows of about a kilobyte.
 __host__ __device__ inline bool qe_block_mode(const QUnit &U) {
-    return U.nsplit == 1 && (U.rb & 15) == 0 && ((U.rb >> 4) & 1);
+    return U.nsplit == 1 && (U.rb & 15) == 0;
 }
 // Offset of the second block (rows 8-15) in a stage slot.
 __host__ __device__ inline uint32_t qe_hi_off(int64_t rb) { return (uint32_t)((8 * rb + 30 + 15) & ~(int64_t)15); }
