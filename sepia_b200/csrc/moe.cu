@@ -854,7 +854,6 @@ static bool engine_down_ok(const MoeDev &L, const SepiaMoeWork *ws) {
     return true;
 }
 
-constexpr uint32_t kMoeRowBudget = 2400;    // bytes of one row per item
 
 static int launch_gateup_engine(const MoeDev &L, const SepiaMoeWork *ws, cudaStream_t st) {
     DevInfo &di = dev_info();
@@ -863,9 +862,10 @@ static int launch_gateup_engine(const MoeDev &L, const SepiaMoeWork *ws, cudaStr
     J.xtab = ws->xtab;
     J.nsb_h = (int)(L.hidden / kQK); J.tpu = (int)(L.ff / 8);
     J.n_slots = L.topk + L.n_shared;
-    J.sbs_r = qe_sbs(L.gate_type, J.nsb_h, kMoeRowBudget, J.nsplit_r);
+    const uint32_t budget = qe_row_budget(di.smem_optin, (int64_t)J.nsb_h * kTabSB);
+    J.sbs_r = qe_sbs(L.gate_type, J.nsb_h, budget, J.nsplit_r);
     J.sbs_s = J.sbs_r; J.nsplit_s = J.nsplit_r;
-    if (L.n_shared) J.sbs_s = qe_sbs(L.sh_gate_type, J.nsb_h, kMoeRowBudget, J.nsplit_s);
+    if (L.n_shared) J.sbs_s = qe_sbs(L.sh_gate_type, J.nsb_h, budget, J.nsplit_s);
     if (!J.sbs_r || !J.sbs_s) return fail("moe: no tensor-core split for the gate/up rows");
     const uint32_t row_max = std::max((uint32_t)J.sbs_r * qe_sb_bytes(L.gate_type),
                                       L.n_shared ? (uint32_t)J.sbs_s * qe_sb_bytes(L.sh_gate_type) : 0u);
@@ -893,9 +893,10 @@ static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *ou
     J.nsb_f = (int)(L.ff / kQK);
     J.n_slots = L.topk + L.n_shared;
     J.n_tiles = (int)((L.hidden + 15) / 16);
-    J.sbs_r = qe_sbs(L.down_type, J.nsb_f, kMoeRowBudget, J.nsplit_r);
+    const uint32_t budget = qe_row_budget(di.smem_optin, (int64_t)J.n_slots * J.nsb_f * kTabSB);
+    J.sbs_r = qe_sbs(L.down_type, J.nsb_f, budget, J.nsplit_r);
     J.sbs_s = J.sbs_r; J.nsplit_s = J.nsplit_r;
-    if (L.n_shared) J.sbs_s = qe_sbs(L.sh_down_type, J.nsb_f, kMoeRowBudget, J.nsplit_s);
+    if (L.n_shared) J.sbs_s = qe_sbs(L.sh_down_type, J.nsb_f, budget, J.nsplit_s);
     if (!J.sbs_r || !J.sbs_s) return fail("moe: no tensor-core split for the down rows");
     const uint32_t row_max = std::max((uint32_t)J.sbs_r * qe_sb_bytes(L.down_type),
                                       L.n_shared ? (uint32_t)J.sbs_s * qe_sb_bytes(L.sh_down_type) : 0u);

@@ -57,12 +57,12 @@ __host__ __device__ inline uint32_t qe_pitch(uint32_t bytes) {
     return p;
 }
 
-// Items of whole rows whose stride is a multiple of 16 bytes with an odd
-// number of 16-byte granules (8 consecutive rows then hit distinct banks) are
-// copied as two blocks of 8 rows -- two bulk copies instead of 16: the copy
-// engine's per-request cost dominates for rows of about a kilobyte.
+// Items of whole rows are copied as two blocks of 8 consecutive rows -- two
+// bulk copies instead of 16: the copy engine's per-request cost dominates for
+// rows of a few kilobytes, more than the shared-memory bank conflicts that a
+// row stride with an even number of 16-byte granules brings.
 __host__ __device__ inline bool qe_block_mode(const QUnit &U) {
-    return U.nsplit == 1 && (U.rb & 15) == 0;
+    return U.nsplit == 1;
 }
 // Offset of the second block (rows 8-15) in a stage slot.
 __host__ __device__ inline uint32_t qe_hi_off(int64_t rb) { return (uint32_t)((8 * rb + 30 + 15) & ~(int64_t)15); }
@@ -319,6 +319,13 @@ static __global__ void k_xtab(const float *x, int64_t x_stride, int n_vec, int n
     const int v = w / nsb, sb = w - v * nsb;
     xtab_build<true>(tab + ((size_t)v * nsb + sb) * kTabSB, x + v * x_stride + (int64_t)sb * kQK, 1, 0, 1,
                      threadIdx.x & 31);
+}
+
+// Host: the largest row an item may carry whole, given the activation-table
+// bytes the CTA keeps in shared memory: three stages of 16 rows must fit.
+inline uint32_t qe_row_budget(int64_t smem_optin, int64_t tab_bytes) {
+    const int64_t b = (smem_optin - kQeJobSmem - tab_bytes - 8192) / (3 * 16) - 48;
+    return (uint32_t)std::max<int64_t>(512, std::min<int64_t>(4000, b));
 }
 
 // Host: superblocks per split for a row of `nsb` superblocks of format t so

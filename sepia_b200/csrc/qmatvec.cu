@@ -163,7 +163,6 @@ struct MvJob {
     }
 };
 
-constexpr uint32_t kQeRowBudget = 2496;    // bytes of one row per item (16 rows ~ 40 KB)
 
 static int launch_matvec_engine(int t, const void *w, const float *x, float *y, int64_t out_dim, int64_t in_dim,
                                 int64_t rb, cudaStream_t st) {
@@ -173,7 +172,7 @@ static int launch_matvec_engine(int t, const void *w, const float *x, float *y, 
     J.rb = rb; J.out_dim = out_dim; J.type = t;
     J.nsb = (int)(in_dim / kQK);
     J.x = x; J.y = y;
-    J.sbs = qe_sbs(t, J.nsb, kQeRowBudget, J.nsplit);
+    J.sbs = qe_sbs(t, J.nsb, qe_row_budget(di.smem_optin, (int64_t)J.nsb * kTabSB), J.nsplit);
     if (!J.sbs) return fail("matvec_q: no tensor-core split for type %d", t);
     QeLayout P;
     int cg, G;
