@@ -95,22 +95,23 @@ __device__ __forceinline__ float logsigmoid_ref(float x) {
 // are short and __syncthreads rounds would dominate).
 // Warps past the last chunk build the tensor-core activation table of x
 // (one superblock each) for the gate/up projections, when xtab is given.
-__global__ void __launch_bounds__(kRouterWarps * 32) k_router(const MoeDev L, const float *x, float *logits,
-                                                               int32_t *topk_idx, float *weights,
-                                                               unsigned int *counter, double *part, uint8_t *xtab) {
+__global__ void __launch_bounds__(kRouterMaxChunks * 32) k_router(const MoeDev L, const float *x, float *logits,
+                                                                   int32_t *topk_idx, float *weights,
+                                                                   unsigned int *counter, uint8_t *xtab) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwarps = blockDim.x >> 5;
     const int n_total = L.n_routed + L.n_shared;
     const int cpr = router_chunks(L.hidden);
-    const int64_t chunk = (int64_t)blockIdx.x * kRouterWarps + warp;
-    const int64_t n_chunks = (int64_t)n_total * cpr;
+    const int row = blockIdx.x;
+    __shared__ double s_part[kRouterMaxChunks];
     griddep_launch();
-    if (chunk >= n_chunks) {
+    if (row >= n_total) {
+        // CTAs past the last row build the x table, a superblock per warp
         griddep_wait();
-        const int sb = (int)(chunk - n_chunks);
+        const int sb = (row - n_total) * nwarps + warp;
         if (xtab && sb < (int)(L.hidden / kQK)) xtab_build(xtab, x, sb + 1, sb, 1 << 30, lane);
-    } else {
-        const int row = (int)(chunk / cpr), c = (int)(chunk % cpr);
-        const int64_t c0 = (int64_t)c * kRouterChunk;
+    } else if (warp < cpr) {
+        const int64_t c0 = (int64_t)warp * kRouterChunk;
         const int64_t n = imin64(kRouterChunk, L.hidden - c0);
         const float *w = L.router_w + (int64_t)row * L.hidden + c0;
         const float *xc = x + c0;
@@ -139,9 +140,15 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(const MoeDev L, co
             for (int64_t i = lane; i < n; i += 32) acc = fma((double)w[i], (double)xc[i], acc);
         }
         acc = warp_sum_d(acc);
-        if (lane == 0) part[chunk] = acc;
+        if (lane == 0) s_part[warp] = acc;
     }
-    // ---- last CTA: logits, then the selection ----
+    __syncthreads();
+    if (row < n_total && threadIdx.x == 0) {
+        double t = 0.0;
+        for (int c = 0; c < cpr; c++) t += s_part[c];       // chunk order
+        logits[row] = (float)t;
+    }
+    // ---- last CTA: the selection ----
     __shared__ unsigned int s_last;
     __threadfence();
     __syncthreads();
@@ -151,21 +158,9 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(const MoeDev L, co
     __threadfence();
 
     __shared__ float s_logit[kRouterMaxExperts];
-    __shared__ float s_score[kRouterMaxExperts];
-    // row sums in chunk order; a thread's loads are independent (L2: other
-    // CTAs wrote them), so they are all in flight together
-    for (int r = threadIdx.x; r < n_total; r += blockDim.x) {
-        double v[kRouterMaxChunks];
-#pragma unroll
-        for (int c = 0; c < kRouterMaxChunks; c++) v[c] = (c < cpr) ? __ldcg(part + (int64_t)r * cpr + c) : 0.0;
-        double t = 0.0;
-#pragma unroll
-        for (int c = 0; c < kRouterMaxChunks; c++)
-            if (c < cpr) t += v[c];
-        s_logit[r] = (float)t;
-        logits[r] = (float)t;
-    }
+    for (int r = threadIdx.x; r < n_total; r += blockDim.x) s_logit[r] = __ldcg(logits + r);
     __syncthreads();
+    __shared__ float s_score[kRouterMaxExperts];
     for (int i = threadIdx.x; i < L.n_routed; i += blockDim.x)
         s_score[i] = __fadd_rn(sigmoid_ref(s_logit[i]), L.router_bias[i]);
     __syncthreads();
@@ -935,12 +930,14 @@ int launch_router(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaS
     if (router_chunks(L.hidden) > kRouterMaxChunks)
         return fail("moe: hidden %lld exceeds the router's %d", (long long)L.hidden, kRouterMaxChunks * kRouterChunk);
     if (!ws->router_part) return fail("moe: work area has no router partials (carve it with moe_work_carve)");
-    const int64_t chunks = (int64_t)n_total * router_chunks(L.hidden);
+    // one CTA per logit row (a warp per 1024-element chunk), then CTAs that
+    // build the x table for the gate/up engine
     uint8_t *xtab = engine_gateup_ok(L, ws) ? ws->xtab : nullptr;
-    const int64_t warps = chunks + (xtab ? L.hidden / kQK : 0);
-    const unsigned grid = (unsigned)((warps + kRouterWarps - 1) / kRouterWarps);
-    return check(launch_pdl(k_router, grid, kRouterWarps * 32, 0, st, L, x, ws->logits, ws->topk_idx, ws->weights,
-                            ws->counter, ws->router_part, xtab),
+    const int nw = std::max(kRouterWarps, router_chunks(L.hidden));
+    const int64_t tab_ctas = xtab ? (L.hidden / kQK + nw - 1) / nw : 0;
+    const unsigned grid = (unsigned)(n_total + tab_ctas);
+    return check(launch_pdl(k_router, grid, nw * 32, 0, st, L, x, ws->logits, ws->topk_idx, ws->weights, ws->counter,
+                            xtab),
                  "moe router launch");
 }
 
