@@ -24,16 +24,20 @@
 //                a2 = row gid,   k 16+4tig..+3   a3 = row gid+8, same k
 //   B (32 x 8):  b0 = k 4tig..+3, col gid        b1 = k 16+4tig..+3, col gid
 //   C (16 x 8):  c0 = (gid, 2tig) c1 = (gid, 2tig+1) c2 = (gid+8, 2tig) c3 = (gid+8, 2tig+1)
-// m16n8k16 uses only a0/a1 and b0. The k index of a part's MMA is the
-// element index within the part (32 consecutive elements).
+// m16n8k16 uses only a0/a1 and b0. A part's k32 MMA pairs hardware k with
+// the part's elements so that each lane's 8 elements are consecutive: k
+// 4tig+i <-> element 8tig+i, k 16+4tig+i <-> element 8tig+4+i (A and B
+// alike). Lanes tig 0,1 thus hold elements 0-15 (one 16-element group),
+// lanes tig 2,3 elements 16-31, and one scale serves both A registers.
 //
 // Two B arrangements come from one table entry e = (b0, b1) of limb gid&3:
 //   natural: columns 0-3 = limbs 0-3 of the whole part (gid >= 4: zero);
 //   split:   columns 0-3 = limbs of elements 0-15 only, columns 4-7 = limbs
-//            of elements 16-31 only, so one MMA yields the two 16-element
-//            groups' dots separately (lanes tig 0,1: first group; tig 2,3:
-//            second group) -- used where a per-group scale cannot be folded
-//            into A.
+//            of elements 16-31 only (B of lanes tig 0,1 kept for gid < 4,
+//            of lanes tig 2,3 for gid >= 4), so one MMA yields the two
+//            16-element groups' dots separately (C lanes tig 0,1: first
+//            group; tig 2,3: second group) -- used where a per-group scale
+//            cannot be folded into A.
 // Either way lane tig's two C columns are limbs 2(tig&1) and 2(tig&1)+1, of
 // weight 256^(2(tig&1)) and 256^(2(tig&1)+1).
 #pragma once
@@ -75,21 +79,21 @@ __device__ __forceinline__ void limbs5(long long v, int (&d)[5]) {
 
 // Build the table entries of x[0 .. nsb*256) into tab (shared or global
 // memory), one warp per superblock (x at least 4-byte aligned). Lane l owns
-// part l/4 and tig l%4: positions 32*part + 4*tig + {0..3} and +16.
+// part l/4 and tig l%4: positions 32*part + 8*tig + {0..7}.
 // CG: read x through L2 only (x was written by other CTAs of this grid).
 template <bool CG = false>
 __device__ inline void xtab_build(uint8_t *tab, const float *x, int nsb, int warp, int nwarps, int lane) {
     const int part = lane >> 2, tig = lane & 3;
     for (int sb = warp; sb < nsb; sb += nwarps) {
         uint8_t *te = tab + (size_t)sb * kTabSB;
-        const float *xs = x + (size_t)sb * kQK + 32 * part + 4 * tig;
+        const float *xs = x + (size_t)sb * kQK + 32 * part + 8 * tig;
         float4 lo, hi;
         if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
             lo = CG ? __ldcg(reinterpret_cast<const float4 *>(xs)) : *reinterpret_cast<const float4 *>(xs);
-            hi = CG ? __ldcg(reinterpret_cast<const float4 *>(xs + 16)) : *reinterpret_cast<const float4 *>(xs + 16);
+            hi = CG ? __ldcg(reinterpret_cast<const float4 *>(xs + 4)) : *reinterpret_cast<const float4 *>(xs + 4);
         } else {
             lo = make_float4(xs[0], xs[1], xs[2], xs[3]);
-            hi = make_float4(xs[16], xs[17], xs[18], xs[19]);
+            hi = make_float4(xs[4], xs[5], xs[6], xs[7]);
         }
         const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
         float m = 0.f;
@@ -115,13 +119,13 @@ __device__ inline void xtab_build(uint8_t *tab, const float *x, int nsb, int war
         uint2 *bd = reinterpret_cast<uint2 *>(te) + part * 16 + tig * 4;
 #pragma unroll
         for (int l = 0; l < 4; l++) bd[l] = make_uint2(w0[l], w1[l]);
-        // group sums: group 2*part = elements 0-15 of the part (the xi[0..3]
-        // of its 4 lanes), group 2*part+1 = elements 16-31
-        long long g0 = (long long)xi[0] + xi[1] + xi[2] + xi[3], g1 = (long long)xi[4] + xi[5] + xi[6] + xi[7];
-        g0 += __shfl_xor_sync(0xffffffffu, g0, 1);
-        g0 += __shfl_xor_sync(0xffffffffu, g0, 2);
-        g1 += __shfl_xor_sync(0xffffffffu, g1, 1);
-        g1 += __shfl_xor_sync(0xffffffffu, g1, 2);
+        // group sums: group 2*part = elements 0-15 of the part (lanes tig
+        // 0,1), group 2*part+1 = elements 16-31 (lanes tig 2,3)
+        long long gs = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) gs += xi[j];
+        gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+        const long long g0 = gs, g1 = __shfl_xor_sync(0xffffffffu, gs, 2);
         // k16 fragment words: lane (gid = limb, t) holds k = 4t..4t+3
         uint8_t *g16 = te + kTabG16, *g32 = te + kTabG32;
         if (tig == 0) {
@@ -192,10 +196,12 @@ struct LaneCtx {
     int gid, tig;
     uint32_t boff;       // byte offset of the lane's B entry in a part's 128 bytes
     uint32_t goff;       // byte offset of the lane's k16 group-sum B word
-    uint32_t mlo, mhi;   // split layout: keep b0 (columns 0-3) / b1 (columns 4-7)
+    uint32_t msplit;     // split layout: keep this lane's B (its group matches its columns)
+    uint32_t mlo;        // columns 0-3 only
     float lwn;           // natural layout: weight of the lane's first limb column (0 for tig 2,3)
     float lws;           // split layout: same, every lane
     float lwg;           // group-sum MMAs (8 limb columns): 256^(2 tig)
+    uint32_t bsel;       // byte_perm selector of the lane's group scale byte (group 2p + tig/2)
 };
 __device__ __forceinline__ LaneCtx lane_ctx(int lane) {
     LaneCtx L;
@@ -205,11 +211,12 @@ __device__ __forceinline__ LaneCtx lane_ctx(int lane) {
     // their results (lanes tig 2,3) are duplicates and get weight 0
     L.boff = (uint32_t)(L.tig * 4 + (L.gid & 3)) * 8u;
     L.goff = (uint32_t)(L.tig * 8 + L.gid) * 4u;
+    L.msplit = ((L.gid < 4) == (L.tig < 2)) ? 0xFFFFFFFFu : 0u;
     L.mlo = (L.gid < 4) ? 0xFFFFFFFFu : 0u;
-    L.mhi = ~L.mlo;
     L.lws = (L.tig & 1) ? 65536.0f : 1.0f;
     L.lwn = (L.tig < 2) ? L.lws : 0.0f;
     L.lwg = (L.tig == 0) ? 1.0f : (L.tig == 1) ? 65536.0f : (L.tig == 2) ? 4294967296.0f : 0.0f;
+    L.bsel = 0x4440u + (uint32_t)(L.tig >> 1);
     return L;
 }
 
@@ -253,20 +260,20 @@ __device__ __forceinline__ void sb_q2k(const uint8_t *bg, const uint8_t *bg8, co
 #pragma unroll
     for (int h = 0; h < 2; h++) {
         const uint8_t *q = bg + 16 + 32 * h, *q8 = bg8 + 16 + 32 * h;
-        const uint32_t w[4] = {ldw(q + 4 * tig), ldw(q8 + 4 * tig), ldw(q + 16 + 4 * tig), ldw(q8 + 16 + 4 * tig)};
+        const uint32_t w[4] = {ldw(q + 8 * tig), ldw(q8 + 8 * tig), ldw(q + 8 * tig + 4), ldw(q8 + 8 * tig + 4)};
         uint32_t w4[4];
 #pragma unroll
         for (int r = 0; r < 4; r++) w4[r] = w[r] >> 4;
 #pragma unroll
         for (int s = 0; s < 4; s++) {
-            const int p = 4 * h + s;                                   // groups 2p, 2p+1
+            const int p = 4 * h + s;                                   // this lane's group: 2p + tig/2
             const uint32_t m = (s & 1) ? 0x0C0C0C0Cu : 0x03030303u;
             const uint32_t *src = (s < 2) ? w : w4;
             const uint2 b = ld_b(te, p, C);
-            const uint32_t a0 = (src[0] & m) * byte_of(sl[p >> 1], 2 * (p & 1));
-            const uint32_t a1 = (src[1] & m) * byte_of(sl8[p >> 1], 2 * (p & 1));
-            const uint32_t a2 = (src[2] & m) * byte_of(sl[p >> 1], 2 * (p & 1) + 1);
-            const uint32_t a3 = (src[3] & m) * byte_of(sl8[p >> 1], 2 * (p & 1) + 1);
+            const uint32_t sc = __byte_perm(sl[p >> 1], 0u, C.bsel + 2 * (p & 1));
+            const uint32_t sc8 = __byte_perm(sl8[p >> 1], 0u, C.bsel + 2 * (p & 1));
+            const uint32_t a0 = (src[0] & m) * sc, a1 = (src[1] & m) * sc8;
+            const uint32_t a2 = (src[2] & m) * sc, a3 = (src[3] & m) * sc8;
             if (s & 1) mma_k32(c2, a0, a1, a2, a3, b.x, b.y);
             else mma_k32(c, a0, a1, a2, a3, b.x, b.y);
         }
@@ -327,14 +334,14 @@ __device__ __forceinline__ void sb_q3k(const uint8_t *bg, const uint8_t *bg8, co
     uint32_t G[4], G8[4];
     q3k_scales<ODD>(bg + 96, G);
     q3k_scales<ODD>(bg8 + 96, G8);
-    const uint32_t hm[4] = {ldw2<ODD>(bg + 4 * tig), ldw2<ODD>(bg8 + 4 * tig), ldw2<ODD>(bg + 16 + 4 * tig),
-                            ldw2<ODD>(bg8 + 16 + 4 * tig)};
+    const uint32_t hm[4] = {ldw2<ODD>(bg + 8 * tig), ldw2<ODD>(bg8 + 8 * tig), ldw2<ODD>(bg + 8 * tig + 4),
+                            ldw2<ODD>(bg8 + 8 * tig + 4)};
     int acc[4] = {0, 0, 0, 0}, accq[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int h = 0; h < 2; h++) {
         const uint8_t *q = bg + 32 + 32 * h, *q8 = bg8 + 32 + 32 * h;
-        const uint32_t w[4] = {ldw2<ODD>(q + 4 * tig), ldw2<ODD>(q8 + 4 * tig), ldw2<ODD>(q + 16 + 4 * tig),
-                               ldw2<ODD>(q8 + 16 + 4 * tig)};
+        const uint32_t w[4] = {ldw2<ODD>(q + 8 * tig), ldw2<ODD>(q8 + 8 * tig), ldw2<ODD>(q + 8 * tig + 4),
+                               ldw2<ODD>(q8 + 8 * tig + 4)};
         uint32_t w4[4];
 #pragma unroll
         for (int r = 0; r < 4; r++) w4[r] = w[r] >> 4;
@@ -353,7 +360,7 @@ __device__ __forceinline__ void sb_q3k(const uint8_t *bg, const uint8_t *bg8, co
             }
             const uint2 e = ld_b(te, p, C);
             int cc[4];
-            mma_k32_z(cc, a[0], a[1], a[2], a[3], e.x & C.mlo, e.y & C.mhi);
+            mma_k32_z(cc, a[0], a[1], a[2], a[3], e.x & C.msplit, e.y & C.msplit);
             // this lane's group: 2p + t
             const int sg = sbyte_of(G[p >> 1], 2 * (p & 1) + t);
             const int sg8 = sbyte_of(G8[p >> 1], 2 * (p & 1) + t);
@@ -404,7 +411,7 @@ __device__ __forceinline__ void sb_q4k(const uint8_t *bg, const uint8_t *bg8, co
 #pragma unroll
     for (int j = 0; j < 4; j++) {
         const uint8_t *q = bg + 16 + 32 * j, *q8 = bg8 + 16 + 32 * j;
-        const uint32_t w[4] = {ldw(q + 4 * tig), ldw(q8 + 4 * tig), ldw(q + 16 + 4 * tig), ldw(q8 + 16 + 4 * tig)};
+        const uint32_t w[4] = {ldw(q + 8 * tig), ldw(q8 + 8 * tig), ldw(q + 8 * tig + 4), ldw(q8 + 8 * tig + 4)};
 #pragma unroll
         for (int hi = 0; hi < 2; hi++) {
             const int p = 2 * j + hi;
