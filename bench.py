@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--no-graph", action="store_true", help="eager launches instead of one CUDA graph per layer")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--parity", action="store_true", help="check one step against the CPU oracle")
+    ap.add_argument("--workload", default="moe_layer", choices=["moe_layer", "kernels"],
+                    help="moe_layer: the headline line (config 2); kernels: one line per BASELINE config-1/3/4 "
+                         "kernel (device time, 1 GPU)")
     return ap.parse_args()
 
 
@@ -208,10 +211,90 @@ def committed_traffic():
 
 
 # ------------------------------------------------------------------- main
+def kernel_lines(args):
+    """Device-timed bandwidth of the other BASELINE kernels on one GPU:
+    config 1 (Q2_K SwiGLU slab: three matvecs + silu_mul), config 3 (IQ1_S /
+    IQ2_XXS matvec, rows 2048/7168/16384 x 7168, batch 1/4/16), config 4
+    (banded attention decode, H=64 Hkv=8 Dh=128 fp16 K/V, global at 32768 and
+    window 4096). Weights rotate through buffers larger than L2."""
+    import torch
+    from sepia_b200 import ops, quants as Q, synth
+    from sepia_b200.lib import load, ok
+    L = load()
+    peak, kind = peak_hbm()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+
+    def timeit(fn, n):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        torch.cuda._sleep(50_000_000)
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for i in range(n):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n * 1e-3
+
+    def emit(name, nbytes, sec, extra):
+        gbs = nbytes / sec / 1e9
+        print(json.dumps({"metric": "kernel HBM GB/s", "kernel": name, "value": round(gbs, 1), "unit": "GB/s",
+                          "us": round(sec * 1e6, 2), "bytes": nbytes, "frac_of_measured_peak": round(gbs / peak, 4),
+                          "peak_kind": kind, "data": "synthetic", **extra}), flush=True)
+
+    def mats(t, rows, cols):
+        nb = Q.row_bytes(t, cols) * rows
+        return [synth.blocks_device(gen, t, rows * cols // Q.block_elems(t)) for _ in range(max(2, int(800e6 // nb)))]
+
+    g, u, d = mats(Q.Q2_K, 2048, 7168), mats(Q.Q2_K, 2048, 7168), mats(Q.Q2_K, 7168, 2048)
+    x = torch.randn(7168, device="cuda")
+    ga, ua, y = torch.empty(2048, device="cuda"), torch.empty(2048, device="cuda"), torch.empty(7168, device="cuda")
+    h = torch.empty(2048, device="cuda")
+
+    def slab(i):
+        k = i % len(g)
+        ok(L.sepia_cuda_matvec_q(Q.Q2_K, g[k].data_ptr(), x.data_ptr(), ga.data_ptr(), 2048, 7168, 1, None))
+        ok(L.sepia_cuda_matvec_q(Q.Q2_K, u[k].data_ptr(), x.data_ptr(), ua.data_ptr(), 2048, 7168, 1, None))
+        ok(L.sepia_cuda_silu_mul(ga.data_ptr(), ua.data_ptr(), h.data_ptr(), 2048, None))
+        ok(L.sepia_cuda_matvec_q(Q.Q2_K, d[k].data_ptr(), h.data_ptr(), y.data_ptr(), 7168, 2048, 1, None))
+    emit("config1_q2k_swiglu_slab", 14516224, timeit(slab, 100), {"launches": 4})
+    del g, u, d
+    for t, name in ((Q.IQ1_S, "iq1_s"), (Q.IQ2_XXS, "iq2_xxs")):
+        for rows in (2048, 7168, 16384):
+            ws = mats(t, rows, 7168)
+            for b in (1, 4, 16):
+                xb = torch.randn(b, 7168, device="cuda")
+                yb = torch.empty(b, rows, device="cuda")
+                fn = lambda i: ok(L.sepia_cuda_matvec_q(t, ws[i % len(ws)].data_ptr(), xb.data_ptr(), yb.data_ptr(),
+                                                        rows, 7168, b, None))
+                nbytes = Q.row_bytes(t, 7168) * rows + 4 * b * (7168 + rows)
+                emit(f"config3_{name}_{rows}x7168_b{b}", nbytes, timeit(fn, 50), {"rows": rows, "batch": b})
+            del ws
+    for ctx, window in ((32768, 0), (4096, 4096)):
+        H, Hkv, Dh, E = 64, 8, 128, 256
+        kvd = Hkv * Dh
+        k = torch.randn(ctx, kvd, device="cuda").half()
+        v = torch.randn(ctx, kvd, device="cuda").half()
+        q = torch.randn(H * Dh, device="cuda")
+        rl = torch.randn(H * E, device="cuda") * 0.02
+        hi = torch.tensor([ctx - 1], dtype=torch.int64, device="cuda")
+        lo = torch.tensor([max(0, ctx - window) if window else 0], dtype=torch.int64, device="cuda")
+        tau = torch.ones(1, device="cuda")
+        fn = lambda i: ops.banded_attn(q, k, v, rl, lo, hi, tau, 1, H, Hkv, Dh, E, ctx - 1, kvd, 1.0 / Dh)
+        nbytes = ctx * kvd * 2 * 2 + 4 * (H * Dh * 2 + H * E)
+        emit(f"config4_attn_ctx{ctx}_{'global' if not window else 'window'}", nbytes, timeit(fn, 50),
+             {"ctx": ctx, "note": "K/V stay L2-resident between calls at ctx 4096"})
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload == "kernels":
+        kernel_lines(args)
         return
     import torch
     import torch.distributed as dist

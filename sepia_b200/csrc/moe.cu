@@ -628,6 +628,9 @@ struct GuJob {
     __device__ int64_t n_units() const { return (int64_t)n_slots * tpu; }
     __device__ int slot_of(int a) const { return a < L.n_shared ? L.topk + a : a - L.n_shared; }
     __device__ bool needs_dep(int64_t u) const { return slot_of((int)u / tpu) < L.topk; }
+    __device__ int splits(const uint8_t *jsm, int64_t u) const {
+        return reinterpret_cast<const MoeSlot *>(jsm)[slot_of((int)u / tpu)].nsplit;
+    }
     __device__ void unit(const uint8_t *jsm, int64_t u, QUnit &U) const {
         const int a = (int)u / tpu, r = (int)u - a * tpu;
         const MoeSlot &m = reinterpret_cast<const MoeSlot *>(jsm)[slot_of(a)];
@@ -690,6 +693,9 @@ struct DnJob {
     }
     __device__ int64_t n_units() const { return (int64_t)n_slots * n_tiles; }
     __device__ bool needs_dep(int64_t) const { return false; }
+    __device__ int splits(const uint8_t *jsm, int64_t u) const {
+        return reinterpret_cast<const MoeSlot *>(jsm)[(int)u % n_slots].nsplit;
+    }
     __device__ void unit(const uint8_t *jsm, int64_t u, QUnit &U) const {
         const int t = (int)u / n_slots, s = (int)u - t * n_slots;
         const MoeSlot &m = reinterpret_cast<const MoeSlot *>(jsm)[s];

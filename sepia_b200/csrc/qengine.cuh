@@ -105,6 +105,7 @@ constexpr int kQeJobSmem = 1024;     // shared scratch of a job (per-CTA unit ta
 //   int64_t n_units() const;
 //   bool needs_dep(int64_t u) const;          // unit u's rows depend on the predecessor
 //   void unit(const uint8_t *jsm, int64_t u, QUnit &U) const;   // U.nsplit = 0: nothing to do
+//   int splits(const uint8_t *jsm, int64_t u) const;             // U.nsplit alone (cheap)
 //   int n_tab() const;                        // activation tables (<= QeLayout.n_tab)
 //   const uint8_t *tab_global() const;        // prebuilt tables [n_tab][tab_nsb] in global
 //                                             //   memory, or nullptr to build them here
@@ -267,11 +268,20 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
     const LaneCtx C = lane_ctx(lane);
     QeRing ring;
     int g = 0;                        // group of the current item (item index % G)
+    const float inv_cg = 1.0f / (float)P.cg;
     for (int64_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+        // units whose items all go to other groups need only their split count
+        const int ns = J.splits(jsm, u);
+        if (P.G > 1 && ns == 1 && g != grp) {
+            ring.next(P.stages);
+            if (++g == P.G) g = 0;
+            continue;
+        }
         QUnit U;
         J.unit(jsm, u, U);
         const uint8_t *te_base = tab + (size_t)U.tab * P.tab_nsb * kTabSB;
         const int sbB = qe_sb_bytes(U.type);
+        const int rb = (int)U.rb;
         for (int sp = 0; sp < U.nsplit; sp++) {
             const int slot = ring.slot;
             const uint32_t phase = ring.phase;
@@ -282,18 +292,21 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             if (!mbar_wait(&full[slot], phase, P.err)) return;
             const int s0 = sp * U.sbs, s1 = min(U.nsb, s0 + U.sbs), n = s1 - s0;
             const uint32_t pitch = qe_pitch((uint32_t)n * (uint32_t)sbB);
-            const int i0 = (cw * n) / P.cg, i1 = ((cw + 1) * n) / P.cg;
+            // (cw*n)/cg exactly: the +0.5 keeps the float product away from
+            // integers by 0.5/cg, far beyond its rounding error
+            const int i0 = __float2int_rz(((float)(cw * n) + 0.5f) * inv_cg);
+            const int i1 = __float2int_rz(((float)((cw + 1) * n) + 0.5f) * inv_cg);
             const uint8_t *st = stage0 + (size_t)slot * P.slot_bytes;
-            const int64_t off = (int64_t)s0 * sbB;
+            const int off = s0 * sbB;
             // rows past the tile's end hold stale bytes: their results are
             // never read (rows are independent in the MMA)
-            const uintptr_t a_lo = reinterpret_cast<uintptr_t>(U.lo + C.gid * U.rb + off);
-            const uintptr_t a_hi = reinterpret_cast<uintptr_t>(U.hi + C.gid * U.rb + off);
+            const uintptr_t a_lo = reinterpret_cast<uintptr_t>(U.lo + (C.gid * rb + off));
+            const uintptr_t a_hi = reinterpret_cast<uintptr_t>(U.hi + (C.gid * rb + off));
             double yg = 0.0, yg8 = 0.0;
             const bool blk = qe_block_mode(U);
-            const uint8_t *rg = blk ? st + (reinterpret_cast<uintptr_t>(U.lo) & 15) + C.gid * U.rb
+            const uint8_t *rg = blk ? st + (reinterpret_cast<uintptr_t>(U.lo) & 15) + C.gid * rb
                                     : st + C.gid * pitch + (a_lo & 15);
-            const uint8_t *rg8 = blk ? st + qe_hi_off(U.rb) + (reinterpret_cast<uintptr_t>(U.hi) & 15) + C.gid * U.rb
+            const uint8_t *rg8 = blk ? st + qe_hi_off(rb) + (reinterpret_cast<uintptr_t>(U.hi) & 15) + C.gid * rb
                                      : st + (C.gid + 8) * pitch + (a_hi & 15);
             tile_sbs_rt(U.type, rg, rg8, te_base + (size_t)s0 * kTabSB, i0, i1, (int)(a_lo & 2) >> 1, C, yg, yg8);
             quad_sum(yg, yg8);
