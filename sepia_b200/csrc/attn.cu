@@ -29,7 +29,6 @@ constexpr int kAttnThreads = 128;
 constexpr int kAttnKT = 64;          // kv positions per tile
 constexpr int kAttnMaxDh = 128;
 constexpr int kAttnMaxG = 16;        // query heads per KV head
-constexpr int kAttnPad = 4;          // smem row padding (floats) against bank conflicts
 
 struct AttnParams {
     const float *q;            // [T, H, Dh]
@@ -44,25 +43,34 @@ struct AttnParams {
     int64_t max_chunk;         // kv positions per split (upper bound)
 };
 
-template <typename KV>
-__device__ __forceinline__ float kv_at(const KV *p, int64_t i);
-template <>
-__device__ __forceinline__ float kv_at<float>(const float *p, int64_t i) { return __ldg(p + i); }
-template <>
-__device__ __forceinline__ float kv_at<__half>(const __half *p, int64_t i) { return __half2float(p[i]); }
 
 template <typename KV>
+__device__ __forceinline__ double kv_d(const KV *p);
+template <>
+__device__ __forceinline__ double kv_d<float>(const float *p) { return (double)*p; }
+template <>
+__device__ __forceinline__ double kv_d<__half>(const __half *p) { return (double)__half2float(*p); }
+
+// Shared-memory row length (elements) of a staged K/V tile: 16-byte multiple.
+template <typename KV>
+__host__ __device__ constexpr int attn_ldk(int Dh) { return Dh + 16 / (int)sizeof(KV); }
+
+// One CTA per (kv split, KV head, token). K/V tiles of kAttnKT rows are
+// staged in their own type with 16-byte cp.async copies, double buffered
+// (the next tile is in flight while this one is used); VEC = false stages
+// element by element (rows not 16-byte aligned).
+template <typename KV, bool VEC>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P) {
-    extern __shared__ __align__(16) float sm[];
+    extern __shared__ __align__(16) uint8_t smraw[];
     const int s = blockIdx.x, hk = blockIdx.y;
     const int64_t t = blockIdx.z;
     const int G = (int)(P.H / P.Hkv), Dh = (int)P.Dh;
-    const int ld = Dh + kAttnPad;
-    float *sq = sm;                              // [G][ld]
-    float *sk = sq + G * ld;                     // [KT][ld]
-    float *sv = sk + kAttnKT * ld;               // [KT][ld]
-    float *ss = sv + kAttnKT * ld;               // [G][KT]
-    float *sml = ss + G * kAttnKT;               // [G][2] running m, l
+    const int ldq = Dh + 4, ldk = attn_ldk<KV>(Dh);
+    float *sq = reinterpret_cast<float *>(smraw);                 // [G][ldq]
+    KV *skb = reinterpret_cast<KV *>(sq + G * ldq);              // [2][KT][ldk]
+    KV *svb = skb + 2 * kAttnKT * ldk;                           // [2][KT][ldk]
+    float *ss = reinterpret_cast<float *>(svb + 2 * kAttnKT * ldk);   // [G][KT]
+    float *sml = ss + G * kAttnKT;                               // [G][2] running m, l
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t lo = P.kv_lo[t], hi = P.kv_hi[t];
@@ -76,10 +84,34 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
     const KV *V = reinterpret_cast<const KV *>(P.v);
 
     for (int i = tid; i < G * Dh; i += kAttnThreads) {
-        const int g = i / Dh, d = i % Dh;
-        sq[g * ld + d] = P.q[(t * P.H + (int64_t)hk * G + g) * P.Dh + d];
+        const int g = i / Dh, d = i - g * Dh;
+        sq[g * ldq + d] = P.q[(t * P.H + (int64_t)hk * G + g) * P.Dh + d];
     }
     if (tid < G) { sml[2 * tid] = -INFINITY; sml[2 * tid + 1] = 0.0f; }
+
+    // stage rows [base, base+nt) of this KV head into buffer b
+    const int gpr = Dh * (int)sizeof(KV) / 16;                     // 16-byte granules per row
+    auto stage = [&](int64_t base, int nt, int b) {
+        KV *sk = skb + b * kAttnKT * ldk, *sv = svb + b * kAttnKT * ldk;
+        if constexpr (VEC) {
+            for (int i = tid; i < nt * gpr; i += kAttnThreads) {
+                const int r = i / gpr, c = i - r * gpr;
+                const int64_t off = (base + r) * P.kv_dim + (int64_t)hk * Dh;
+                cp_async16(reinterpret_cast<uint8_t *>(sk + r * ldk) + 16 * c,
+                           reinterpret_cast<const uint8_t *>(K + off) + 16 * c);
+                cp_async16(reinterpret_cast<uint8_t *>(sv + r * ldk) + 16 * c,
+                           reinterpret_cast<const uint8_t *>(V + off) + 16 * c);
+            }
+            cp_async_commit();
+        } else {
+            for (int i = tid; i < nt * Dh; i += kAttnThreads) {
+                const int r = i / Dh, d = i - r * Dh;
+                const int64_t off = (base + r) * P.kv_dim + (int64_t)hk * Dh + d;
+                sk[r * ldk + d] = K[off];
+                sv[r * ldk + d] = V[off];
+            }
+        }
+    };
 
     // PV ownership: warp w owns heads g = w, w+4, ...; lane owns dims lane + 32j
     constexpr int kHPW = kAttnMaxG / 4;
@@ -88,19 +120,25 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
     for (int a = 0; a < kHPW; a++)
 #pragma unroll
         for (int j = 0; j < kAttnMaxDh / 32; j++) acc[a][j] = 0.0;
-    __syncthreads();
 
-    for (int64_t base = c0; base < c1; base += kAttnKT) {
+    if (c0 < c1) stage(c0, (int)min((int64_t)kAttnKT, c1 - c0), 0);
+    int buf = 0;
+    for (int64_t base = c0; base < c1; base += kAttnKT, buf ^= 1) {
         const int nt = (c1 - base < kAttnKT) ? (int)(c1 - base) : kAttnKT;
-        // ---- stage K and V rows of this KV head (converted to fp32) ----
-        for (int i = tid; i < nt * Dh; i += kAttnThreads) {
-            const int r = i / Dh, d = i % Dh;
-            const int64_t off = (base + r) * P.kv_dim + (int64_t)hk * Dh + d;
-            sk[r * ld + d] = kv_at<KV>(K, off);
-            sv[r * ld + d] = kv_at<KV>(V, off);
+        const int64_t nb = base + kAttnKT;
+        if constexpr (VEC) {
+            if (nb < c1) {
+                stage(nb, (int)min((int64_t)kAttnKT, c1 - nb), buf ^ 1);
+                cp_async_wait<1>();
+            } else {
+                cp_async_wait<0>();
+            }
+        } else {
+            if (base != c0) stage(base, nt, buf);
         }
         __syncthreads();
-        // ---- scores: thread -> (kv row r, heads g = gi, gi+stride...) ----
+        const KV *sk = skb + buf * kAttnKT * ldk, *sv = svb + buf * kAttnKT * ldk;
+        // ---- scores: thread -> kv row r, heads g0, g0+gstep, ... ----
         {
             const int r = tid % kAttnKT;
             const int g0 = tid / kAttnKT;            // 0 or 1
@@ -108,21 +146,32 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
             if (r < nt) {
                 const int64_t kv = base + r;
                 const int64_t dist = q_pos - kv;
-                for (int g = g0; g < G; g += gstep) {
-                    // the reference's score arithmetic (src/sepia.c:1216-1220):
-                    // fp64 dot rounded to float, then content + bias in fp64,
-                    // rounded once -- a one-ulp score change moves exp() by
-                    // ~1e-6 relative, more than the whole error budget
-                    double d0 = 0.0, d1 = 0.0;
-                    const float *qr = sq + g * ld, *kr = sk + r * ld;
-                    for (int d = 0; d < Dh; d += 2) {
-                        d0 = fma((double)qr[d], (double)kr[d], d0);
-                        d1 = fma((double)qr[d + 1], (double)kr[d + 1], d1);
+                // the reference's score arithmetic (src/sepia.c:1216-1220):
+                // fp64 dot rounded to float, then content + bias in fp64,
+                // rounded once -- a one-ulp score change moves exp() by
+                // ~1e-6 relative, more than the whole error budget. Each k
+                // element is converted once for all of the thread's heads.
+                double dd[kAttnMaxG / 2];
+#pragma unroll
+                for (int j = 0; j < kAttnMaxG / 2; j++) dd[j] = 0.0;
+                const KV *kr = sk + r * ldk;
+                for (int d = 0; d < Dh; d++) {
+                    const double kd = kv_d<KV>(kr + d);
+#pragma unroll
+                    for (int j = 0; j < kAttnMaxG / 2; j++) {
+                        const int g = g0 + gstep * j;
+                        if (g < G) dd[j] = fma((double)sq[g * ldq + d], kd, dd[j]);
                     }
-                    double sc = (double)(float)(d0 + d1) * (double)P.inv_head_dim;
-                    if (dist < P.E && dist >= 0)
-                        sc += (double)P.rel_logits[(t * P.H + (int64_t)hk * G + g) * P.E + dist] * (double)tau;
-                    ss[g * kAttnKT + r] = (float)sc;
+                }
+#pragma unroll
+                for (int j = 0; j < kAttnMaxG / 2; j++) {
+                    const int g = g0 + gstep * j;
+                    if (g < G) {
+                        double sc = (double)(float)dd[j] * (double)P.inv_head_dim;
+                        if (dist < P.E && dist >= 0)
+                            sc += (double)P.rel_logits[(t * P.H + (int64_t)hk * G + g) * P.E + dist] * (double)tau;
+                        ss[g * kAttnKT + r] = (float)sc;
+                    }
                 }
             } else {
                 for (int g = g0; g < G; g += gstep) ss[g * kAttnKT + r] = -INFINITY;
@@ -149,11 +198,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
 #pragma unroll
                 for (int j = 0; j < kAttnMaxDh / 32; j++) acc[a][j] *= (double)corr;
                 for (int r = 0; r < nt; r++) {
-                    const float pr = ss[g * kAttnKT + r];
+                    const double pr = (double)ss[g * kAttnKT + r];
 #pragma unroll
                     for (int j = 0; j < kAttnMaxDh / 32; j++) {
                         const int d = lane + 32 * j;
-                        if (d < Dh) acc[a][j] = fma((double)pr, (double)sv[r * ld + d], acc[a][j]);
+                        if (d < Dh) acc[a][j] = fma(pr, kv_d<KV>(sv + r * ldk + d), acc[a][j]);
                     }
                 }
             }
@@ -175,6 +224,26 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
             }
         }
     }
+}
+
+template <typename KV>
+static size_t attn_smem(int G, int Dh) {
+    return sizeof(float) * (size_t)G * (Dh + 4) + sizeof(KV) * 4 * (size_t)kAttnKT * attn_ldk<KV>(Dh) +
+           sizeof(float) * ((size_t)G * kAttnKT + 2 * G);
+}
+
+template <typename KV>
+static int attn_launch_split(const AttnParams &P, int G, cudaStream_t st) {
+    const int Dh = (int)P.Dh;
+    const size_t smem = attn_smem<KV>(G, Dh);
+    const bool vec = (Dh * (int)sizeof(KV)) % 16 == 0 && (P.kv_dim * (int64_t)sizeof(KV)) % 16 == 0 &&
+                     ((reinterpret_cast<uintptr_t>(P.k) | reinterpret_cast<uintptr_t>(P.v)) & 15) == 0;
+    const void *fn = vec ? (const void *)k_attn_split<KV, true> : (const void *)k_attn_split<KV, false>;
+    if (!ensure_smem(fn, (int)smem)) return 0;
+    dim3 grid((unsigned)P.S, (unsigned)P.Hkv, (unsigned)P.T);
+    if (vec) k_attn_split<KV, true><<<grid, kAttnThreads, smem, st>>>(P);
+    else k_attn_split<KV, false><<<grid, kAttnThreads, smem, st>>>(P);
+    return check(cudaGetLastError(), "banded_attn launch");
 }
 
 // out[t,h,:] = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M), splits in order.
@@ -240,14 +309,7 @@ int launch_banded_attn(int kv_f16, const float *q, const void *k, const void *v,
     P.part = part; P.T = T; P.H = H; P.Hkv = Hkv; P.Dh = Dh; P.E = E; P.q_pos_base = q_pos_base; P.kv_dim = kv_dim;
     P.inv_head_dim = inv_head_dim; P.S = S; P.max_chunk = 0;
     const int G = (int)(H / Hkv);
-    const int ld = (int)Dh + kAttnPad;
-    const size_t smem = sizeof(float) * ((size_t)G * ld + 2 * (size_t)kAttnKT * ld + (size_t)G * kAttnKT + 2 * G);
-    const void *fn = kv_f16 ? (const void *)k_attn_split<__half> : (const void *)k_attn_split<float>;
-    if (!ensure_smem(fn, (int)smem)) return 0;
-    dim3 grid((unsigned)S, (unsigned)Hkv, (unsigned)T);
-    if (kv_f16) k_attn_split<__half><<<grid, kAttnThreads, smem, st>>>(P);
-    else k_attn_split<float><<<grid, kAttnThreads, smem, st>>>(P);
-    if (!check(cudaGetLastError(), "banded_attn launch")) return 0;
+    if (!(kv_f16 ? attn_launch_split<__half>(P, G, st) : attn_launch_split<float>(P, G, st))) return 0;
     k_attn_combine<<<(unsigned)(T * H), 128, 0, st>>>(part, out, T * H, S, Dh);
     return check(cudaGetLastError(), "banded_attn combine launch");
 }

@@ -169,6 +169,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     return true;
 }
 
+// 16-byte asynchronous copy global -> shared (L2 only); groups of them are
+// committed and waited for with cp_async_commit / cp_async_wait<N> (at most
+// N groups still in flight).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // 1-D bulk copy global -> shared, completion signalled on `bar` as
 // transaction bytes. dst/src 16-byte aligned, bytes a multiple of 16.
 // No multicast: every CTA fetches its own bytes.
