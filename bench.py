@@ -218,7 +218,7 @@ def kernel_lines(args):
     (banded attention decode, H=64 Hkv=8 Dh=128 fp16 K/V, global at 32768 and
     window 4096). Weights rotate through buffers larger than L2."""
     import torch
-    from sepia_b200 import ops, quants as Q, synth
+    from sepia_b200 import quants as Q, synth
     from sepia_b200.lib import load, ok
     L = load()
     peak, kind = peak_hbm()
@@ -282,7 +282,14 @@ def kernel_lines(args):
         hi = torch.tensor([ctx - 1], dtype=torch.int64, device="cuda")
         lo = torch.tensor([max(0, ctx - window) if window else 0], dtype=torch.int64, device="cuda")
         tau = torch.ones(1, device="cuda")
-        fn = lambda i: ops.banded_attn(q, k, v, rl, lo, hi, tau, 1, H, Hkv, Dh, E, ctx - 1, kvd, 1.0 / Dh)
+        out = torch.empty(H * Dh, device="cuda")
+        max_kv = ctx - int(lo.item())
+        wsb = L.sepia_cuda_banded_attn_ws_bytes(1, H, Hkv, Dh, max_kv)
+        ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda")
+        fn = lambda i: ok(L.sepia_cuda_banded_attn(1, q.data_ptr(), k.data_ptr(), v.data_ptr(), rl.data_ptr(),
+                                                   out.data_ptr(), lo.data_ptr(), hi.data_ptr(), tau.data_ptr(), 1, H,
+                                                   Hkv, Dh, E, ctx - 1, kvd, 1.0 / Dh, max_kv, ws.data_ptr(), wsb,
+                                                   None))
         nbytes = ctx * kvd * 2 * 2 + 4 * (H * Dh * 2 + H * E)
         emit(f"config4_attn_ctx{ctx}_{'global' if not window else 'window'}", nbytes, timeit(fn, 50),
              {"ctx": ctx, "note": "K/V stay L2-resident between calls at ctx 4096"})

@@ -25,7 +25,8 @@
 
 namespace sepia {
 
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kAttnKT = 64;          // kv positions per tile
 constexpr int kAttnMaxDh = 128;
 constexpr int kAttnMaxG = 16;        // query heads per KV head
@@ -59,14 +60,14 @@ __host__ __device__ constexpr int attn_ldk(int Dh) { return Dh + 16 / (int)sizeo
 // staged in their own type with 16-byte cp.async copies, double buffered
 // (the next tile is in flight while this one is used); VEC = false stages
 // element by element (rows not 16-byte aligned).
-template <typename KV, bool VEC>
+template <typename KV, bool VEC, int GM>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P) {
     extern __shared__ __align__(16) uint8_t smraw[];
     const int s = blockIdx.x, hk = blockIdx.y;
     const int64_t t = blockIdx.z;
     const int G = (int)(P.H / P.Hkv), Dh = (int)P.Dh;
-    const int ldq = Dh + 4, ldk = attn_ldk<KV>(Dh);
-    float *sq = reinterpret_cast<float *>(smraw);                 // [G][ldq]
+    const int ldq = Dh + 2, ldk = attn_ldk<KV>(Dh);
+    double *sq = reinterpret_cast<double *>(smraw);               // [G][ldq] (converted once)
     KV *skb = reinterpret_cast<KV *>(sq + G * ldq);              // [2][KT][ldk]
     KV *svb = skb + 2 * kAttnKT * ldk;                           // [2][KT][ldk]
     float *ss = reinterpret_cast<float *>(svb + 2 * kAttnKT * ldk);   // [G][KT]
@@ -85,7 +86,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
 
     for (int i = tid; i < G * Dh; i += kAttnThreads) {
         const int g = i / Dh, d = i - g * Dh;
-        sq[g * ldq + d] = P.q[(t * P.H + (int64_t)hk * G + g) * P.Dh + d];
+        sq[g * ldq + d] = (double)P.q[(t * P.H + (int64_t)hk * G + g) * P.Dh + d];
     }
     if (tid < G) { sml[2 * tid] = -INFINITY; sml[2 * tid + 1] = 0.0f; }
 
@@ -113,8 +114,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
         }
     };
 
-    // PV ownership: warp w owns heads g = w, w+4, ...; lane owns dims lane + 32j
-    constexpr int kHPW = kAttnMaxG / 4;
+    // PV ownership: warp w owns heads g = w, w+8, ...; lane owns dims lane + 32j
+    constexpr int kHPW = (GM + kAttnWarps - 1) / kAttnWarps;   // heads per warp (GM >= G)
+    constexpr int kHPT = (GM + (kAttnThreads / kAttnKT) - 1) / (kAttnThreads / kAttnKT);   // score heads per thread
     double acc[kHPW][kAttnMaxDh / 32];   // fp64: long kv chains stay at fp32 rounding
 #pragma unroll
     for (int a = 0; a < kHPW; a++)
@@ -141,8 +143,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
         // ---- scores: thread -> kv row r, heads g0, g0+gstep, ... ----
         {
             const int r = tid % kAttnKT;
-            const int g0 = tid / kAttnKT;            // 0 or 1
-            const int gstep = kAttnThreads / kAttnKT; // 2
+            const int g0 = tid / kAttnKT;
+            const int gstep = kAttnThreads / kAttnKT;
             if (r < nt) {
                 const int64_t kv = base + r;
                 const int64_t dist = q_pos - kv;
@@ -151,20 +153,20 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
                 // rounded once -- a one-ulp score change moves exp() by
                 // ~1e-6 relative, more than the whole error budget. Each k
                 // element is converted once for all of the thread's heads.
-                double dd[kAttnMaxG / 2];
+                double dd[kHPT];
 #pragma unroll
-                for (int j = 0; j < kAttnMaxG / 2; j++) dd[j] = 0.0;
+                for (int j = 0; j < kHPT; j++) dd[j] = 0.0;
                 const KV *kr = sk + r * ldk;
                 for (int d = 0; d < Dh; d++) {
                     const double kd = kv_d<KV>(kr + d);
 #pragma unroll
-                    for (int j = 0; j < kAttnMaxG / 2; j++) {
+                    for (int j = 0; j < kHPT; j++) {
                         const int g = g0 + gstep * j;
-                        if (g < G) dd[j] = fma((double)sq[g * ldq + d], kd, dd[j]);
+                        if (g < G) dd[j] = fma(sq[g * ldq + d], kd, dd[j]);
                     }
                 }
 #pragma unroll
-                for (int j = 0; j < kAttnMaxG / 2; j++) {
+                for (int j = 0; j < kHPT; j++) {
                     const int g = g0 + gstep * j;
                     if (g < G) {
                         double sc = (double)(float)dd[j] * (double)P.inv_head_dim;
@@ -178,10 +180,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
             }
         }
         __syncthreads();
-        // ---- online softmax update + PV, per head owned by this warp ----
+        // ---- online softmax update, per head owned by this warp ----
 #pragma unroll
         for (int a = 0; a < kHPW; a++) {
-            const int g = warp + 4 * a;
+            const int g = warp + kAttnWarps * a;
             if (g < G) {
                 const float v0 = ss[g * kAttnKT + lane], v1 = ss[g * kAttnKT + lane + 32];
                 const float tmax = warp_max(fmaxf(v0, v1));
@@ -197,13 +199,25 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
                 if (lane == 0) { sml[2 * g] = m_new; sml[2 * g + 1] = sml[2 * g + 1] * corr + psum; }
 #pragma unroll
                 for (int j = 0; j < kAttnMaxDh / 32; j++) acc[a][j] *= (double)corr;
-                for (int r = 0; r < nt; r++) {
-                    const double pr = (double)ss[g * kAttnKT + r];
+            }
+        }
+        __syncwarp();
+        // ---- P.V: each v element is converted once for all of the warp's heads ----
+        for (int r = 0; r < nt; r++) {
+            double pr[kHPW];
 #pragma unroll
-                    for (int j = 0; j < kAttnMaxDh / 32; j++) {
-                        const int d = lane + 32 * j;
-                        if (d < Dh) acc[a][j] = fma(pr, kv_d<KV>(sv + r * ldk + d), acc[a][j]);
-                    }
+            for (int a = 0; a < kHPW; a++) {
+                const int g = warp + kAttnWarps * a;
+                pr[a] = (g < G) ? (double)ss[g * kAttnKT + r] : 0.0;
+            }
+#pragma unroll
+            for (int j = 0; j < kAttnMaxDh / 32; j++) {
+                const int d = lane + 32 * j;
+                if (d < Dh) {
+                    const double vd = kv_d<KV>(sv + r * ldk + d);
+#pragma unroll
+                    for (int a = 0; a < kHPW; a++)
+                        if (warp + kAttnWarps * a < G) acc[a][j] = fma(pr[a], vd, acc[a][j]);
                 }
             }
         }
@@ -212,7 +226,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
     // ---- write this split's partial per head ----
 #pragma unroll
     for (int a = 0; a < kHPW; a++) {
-        const int g = warp + 4 * a;
+        const int g = warp + kAttnWarps * a;
         if (g < G) {
             const int64_t h = (int64_t)hk * G + g;
             double *pp = P.part + ((t * P.H + h) * P.S + s) * (P.Dh + 2);
@@ -228,8 +242,25 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
 
 template <typename KV>
 static size_t attn_smem(int G, int Dh) {
-    return sizeof(float) * (size_t)G * (Dh + 4) + sizeof(KV) * 4 * (size_t)kAttnKT * attn_ldk<KV>(Dh) +
+    return sizeof(double) * (size_t)G * (Dh + 2) + sizeof(KV) * 4 * (size_t)kAttnKT * attn_ldk<KV>(Dh) +
            sizeof(float) * ((size_t)G * kAttnKT + 2 * G);
+}
+
+template <typename KV, bool VEC, int GM>
+static int attn_launch_g(const AttnParams &P, size_t smem, cudaStream_t st) {
+    const void *fn = (const void *)k_attn_split<KV, VEC, GM>;
+    if (!ensure_smem(fn, (int)smem)) return 0;
+    dim3 grid((unsigned)P.S, (unsigned)P.Hkv, (unsigned)P.T);
+    k_attn_split<KV, VEC, GM><<<grid, kAttnThreads, smem, st>>>(P);
+    return check(cudaGetLastError(), "banded_attn launch");
+}
+
+template <typename KV, bool VEC>
+static int attn_launch_v(const AttnParams &P, int G, size_t smem, cudaStream_t st) {
+    if (G <= 2) return attn_launch_g<KV, VEC, 2>(P, smem, st);
+    if (G <= 4) return attn_launch_g<KV, VEC, 4>(P, smem, st);
+    if (G <= 8) return attn_launch_g<KV, VEC, 8>(P, smem, st);
+    return attn_launch_g<KV, VEC, kAttnMaxG>(P, smem, st);
 }
 
 template <typename KV>
@@ -238,32 +269,35 @@ static int attn_launch_split(const AttnParams &P, int G, cudaStream_t st) {
     const size_t smem = attn_smem<KV>(G, Dh);
     const bool vec = (Dh * (int)sizeof(KV)) % 16 == 0 && (P.kv_dim * (int64_t)sizeof(KV)) % 16 == 0 &&
                      ((reinterpret_cast<uintptr_t>(P.k) | reinterpret_cast<uintptr_t>(P.v)) & 15) == 0;
-    const void *fn = vec ? (const void *)k_attn_split<KV, true> : (const void *)k_attn_split<KV, false>;
-    if (!ensure_smem(fn, (int)smem)) return 0;
-    dim3 grid((unsigned)P.S, (unsigned)P.Hkv, (unsigned)P.T);
-    if (vec) k_attn_split<KV, true><<<grid, kAttnThreads, smem, st>>>(P);
-    else k_attn_split<KV, false><<<grid, kAttnThreads, smem, st>>>(P);
-    return check(cudaGetLastError(), "banded_attn launch");
+    return vec ? attn_launch_v<KV, true>(P, G, smem, st) : attn_launch_v<KV, false>(P, G, smem, st);
 }
 
 // out[t,h,:] = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M), splits in order.
+// The split weights e^(m_s - M) are computed once per (t, h) into shared memory.
+constexpr int kAttnMaxSplits = 256;
 __global__ void k_attn_combine(const double *part, float *out, int64_t TH, int S, int64_t Dh) {
     const int64_t th = blockIdx.x;
     if (th >= TH) return;
+    __shared__ double s_w[kAttnMaxSplits];
+    __shared__ double s_L;
     const double *pp = part + th * S * (Dh + 2);
     double M = -INFINITY;
     for (int s = 0; s < S; s++) M = fmax(M, pp[s * (Dh + 2)]);
-    double L = 0.0;
-    for (int s = 0; s < S; s++) {
+    for (int s = threadIdx.x; s < S; s += blockDim.x) {
         const double m = pp[s * (Dh + 2)];
-        if (m != -INFINITY) L += pp[s * (Dh + 2) + 1] * exp(m - M);
+        s_w[s] = (m != -INFINITY) ? exp(m - M) : 0.0;
     }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double L = 0.0;
+        for (int s = 0; s < S; s++) L += pp[s * (Dh + 2) + 1] * s_w[s];
+        s_L = L;
+    }
+    __syncthreads();
+    const double L = s_L;
     for (int64_t d = threadIdx.x; d < Dh; d += blockDim.x) {
         double a = 0.0;
-        for (int s = 0; s < S; s++) {
-            const double m = pp[s * (Dh + 2)];
-            if (m != -INFINITY) a += pp[s * (Dh + 2) + 2 + d] * exp(m - M);
-        }
+        for (int s = 0; s < S; s++) a += pp[s * (Dh + 2) + 2 + d] * s_w[s];
         out[th * Dh + d] = (float)(a / L);
     }
 }
