@@ -85,6 +85,60 @@ __device__ __forceinline__ float logsigmoid_ref(float x) {
     return x - log1pf((float)exp((double)x));
 }
 
+// Order-preserving 32-bit key of a score: larger key = larger score, +0 and
+// -0 equal (they compare equal in the reference's scan). 0 is below every
+// score's key and marks a taken or absent entry.
+__device__ __forceinline__ uint32_t score_key(float f) {
+    const uint32_t u = __float_as_uint(f == 0.0f ? 0.0f : f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// moe_route_select (src/sepia.c:1329-1375) on one warp. Expert e's key sits
+// in lane e % 32, register e / 32. The reference's repeated strict-'>' scan
+// picks, at each step, the highest remaining score and the lowest index
+// among equal ones: per step a warp max of the keys (redux.sync), then a
+// warp min of the indices holding that key. Weights: log-sigmoid softmax
+// over the k raw logits and the shared-sink logits, in slot order.
+template <int KPL>
+__device__ __forceinline__ void router_select(const MoeDev &L, const float2 *row_out, int32_t *topk_idx,
+                                              float *weights, int lane) {
+    uint32_t key[KPL];
+#pragma unroll
+    for (int j = 0; j < KPL; j++) {
+        const int e = lane + 32 * j;
+        key[j] = e < L.n_routed ? score_key(__ldcg(&row_out[e].x)) : 0u;
+    }
+    int my_sel = -1;        // lane j < topk: the j-th pick
+    for (int k = 0; k < L.topk; k++) {
+        uint32_t m = 0;
+#pragma unroll
+        for (int j = 0; j < KPL; j++) m = max(m, key[j]);
+        m = __reduce_max_sync(0xffffffffu, m);
+        uint32_t cand = 0xFFFFFFFFu;
+#pragma unroll
+        for (int j = KPL - 1; j >= 0; j--)
+            if (key[j] == m) cand = (uint32_t)(lane + 32 * j);
+        const int e = (int)__reduce_min_sync(0xffffffffu, cand);
+#pragma unroll
+        for (int j = 0; j < KPL; j++)
+            if (lane + 32 * j == e) key[j] = 0u;
+        if (lane == k) my_sel = e;
+    }
+    const int n_sel = L.topk + L.n_shared;
+    float lp = -INFINITY;
+    if (lane < n_sel) lp = __ldcg(&row_out[lane < L.topk ? my_sel : L.n_routed + (lane - L.topk)].y);
+    float lmax = lp;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    const double ex = (lane < n_sel) ? exp((double)(lp - lmax)) : 0.0;
+    double se = 0.0;
+    for (int j = 0; j < n_sel; j++) se += __shfl_sync(0xffffffffu, ex, j);   // slot order
+    const double lse = (double)lmax + log(se);
+    const double scl = (double)L.route_scale * (double)L.global_scale;
+    if (lane < n_sel) weights[lane] = (float)(exp((double)lp - lse) * scl);
+    if (lane < L.topk) topk_idx[lane] = my_sel;
+}
+
 // Router GEMV: the [n_total, hidden] f32 matrix is cut into chunks of
 // kRouterChunk consecutive elements of one row; one warp per chunk, every
 // lane issuing all of its 16-byte loads before the first FMA, so the whole
@@ -97,7 +151,8 @@ __device__ __forceinline__ float logsigmoid_ref(float x) {
 // (one superblock each) for the gate/up projections, when xtab is given.
 __global__ void __launch_bounds__(kRouterMaxChunks * 32) k_router(const MoeDev L, const float *x, float *logits,
                                                                    int32_t *topk_idx, float *weights,
-                                                                   unsigned int *counter, uint8_t *xtab) {
+                                                                   unsigned int *counter, float2 *row_out,
+                                                                   uint8_t *xtab) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nwarps = blockDim.x >> 5;
     const int n_total = L.n_routed + L.n_shared;
@@ -142,62 +197,29 @@ __global__ void __launch_bounds__(kRouterMaxChunks * 32) k_router(const MoeDev L
         acc = warp_sum_d(acc);
         if (lane == 0) s_part[warp] = acc;
     }
-    __syncthreads();
-    if (row < n_total && threadIdx.x == 0) {
-        double t = 0.0;
-        for (int c = 0; c < cpr; c++) t += s_part[c];       // chunk order
-        logits[row] = (float)t;
-    }
-    // ---- last CTA: the selection ----
-    __shared__ unsigned int s_last;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_last = (atomicAdd(counter, 1u) == gridDim.x - 1) ? 1u : 0u;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-
-    __shared__ float s_logit[kRouterMaxExperts];
-    for (int r = threadIdx.x; r < n_total; r += blockDim.x) s_logit[r] = __ldcg(logits + r);
-    __syncthreads();
-    __shared__ float s_score[kRouterMaxExperts];
-    for (int i = threadIdx.x; i < L.n_routed; i += blockDim.x)
-        s_score[i] = __fadd_rn(sigmoid_ref(s_logit[i]), L.router_bias[i]);
-    __syncthreads();
-    // top-k by rank: entry i is the (rank_i)-th pick of the reference's
-    // repeated strict-'>' scan from index 0, where rank_i counts the entries
-    // that beat it (higher score, or equal score at a lower index). One pass,
-    // every thread ranking its own entries against all others.
-    __shared__ int s_sel[kMaxSlots];
-    for (int i = threadIdx.x; i < L.n_routed; i += blockDim.x) {
-        const float v = s_score[i];
-        int rank = 0;
-        for (int j = 0; j < L.n_routed; j++) {
-            const float u = s_score[j];
-            rank += (u > v || (u == v && j < i)) ? 1 : 0;
-        }
-        if (rank < L.topk) s_sel[rank] = i;
-    }
+    // the row's selection score and log-sigmoid, computed here so that the
+    // serial tail below only selects and normalises
+    const float bias = (row < L.n_routed && threadIdx.x == 0) ? L.router_bias[row] : 0.0f;
     __syncthreads();
     if (warp != 0) return;
-    // weights: softmax over the k selected raw logits and the shared-sink
-    // logits in log-sigmoid space (src/sepia.c:1349-1374); lane j owns slot j
-    const int n_sel = L.topk + L.n_shared;
-    float lp = -INFINITY;
-    if (lane < n_sel) {
-        const float l = (lane < L.topk) ? s_logit[s_sel[lane]] : s_logit[L.n_routed + (lane - L.topk)];
-        lp = logsigmoid_ref(l);
+    unsigned int last = 0;
+    if (lane == 0) {
+        if (row < n_total) {
+            double t = 0.0;
+            for (int c = 0; c < cpr; c++) t += s_part[c];       // chunk order
+            const float l = (float)t;
+            logits[row] = l;
+            const float score = row < L.n_routed ? __fadd_rn(sigmoid_ref(l), bias) : 0.0f;
+            row_out[row] = make_float2(score, logsigmoid_ref(l));
+        }
+        __threadfence();     // release this CTA's writes before counting it
+        last = (atomicAdd(counter, 1u) == gridDim.x - 1) ? 1u : 0u;
     }
-    float lmax = lp;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
-    const double e = (lane < n_sel) ? exp((double)(lp - lmax)) : 0.0;
-    double se = 0.0;
-    for (int j = 0; j < n_sel; j++) se += __shfl_sync(0xffffffffu, e, j);   // slot order
-    const double lse = (double)lmax + log(se);
-    const double scl = (double)L.route_scale * (double)L.global_scale;
-    if (lane < n_sel) weights[lane] = (float)(exp((double)lp - lse) * scl);
-    if (lane < L.topk) topk_idx[lane] = s_sel[lane];
+    if (!__shfl_sync(0xffffffffu, last, 0)) return;
+    __threadfence();
+    // ---- last CTA, one warp: top-k and the weights ----
+    if (L.n_routed <= 8 * 32) router_select<8>(L, row_out, topk_idx, weights, lane);
+    else router_select<kRouterMaxExperts / 32>(L, row_out, topk_idx, weights, lane);
     if (lane == 0) {
         *counter = 0u;   // ready for the next launch
         __threadfence();
@@ -643,6 +665,7 @@ struct GuJob {
     }
     __device__ int n_tab() const { return 1; }
     __device__ const uint8_t *tab_global() const { return xtab; }
+    __device__ uint32_t tab_mask(const uint8_t *) const { return 1u; }
     __device__ const float *tab_src(int) const { return nullptr; }
     // lanes 0-7: h = silu(g) * u in the reference's float arithmetic
     // (src/sepia.c:1405-1410; shared experts: * gamma, src/sepia.c:1432-1444)
@@ -711,6 +734,20 @@ struct DnJob {
     }
     __device__ int n_tab() const { return n_slots; }
     __device__ const uint8_t *tab_global() const { return htab; }
+    // units u = blockIdx.x + k*gridDim.x read table u % n_slots: the slots
+    // repeat with period at most n_slots, and inactive slots need none
+    __device__ uint32_t tab_mask(const uint8_t *jsm) const {
+        const MoeSlot *m = reinterpret_cast<const MoeSlot *>(jsm);
+        uint32_t mask = 0;
+        const int64_t nu = n_units();
+        for (int k = 0; k < n_slots; k++) {
+            const int64_t u = blockIdx.x + (int64_t)k * gridDim.x;
+            if (u >= nu) break;
+            const int s = (int)(u % n_slots);
+            if (m[s].nsplit) mask |= 1u << s;
+        }
+        return mask;
+    }
     __device__ const float *tab_src(int) const { return nullptr; }
     __device__ void finish(const uint8_t *, int64_t u, const QUnit &, double v, int lane) const {
         const int t = (int)u / n_slots, s = (int)u - t * n_slots;
@@ -935,7 +972,7 @@ int launch_router(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaS
     if (n_total > kRouterMaxExperts) return fail("moe: %d experts exceed the router's %d", n_total, kRouterMaxExperts);
     if (router_chunks(L.hidden) > kRouterMaxChunks)
         return fail("moe: hidden %lld exceeds the router's %d", (long long)L.hidden, kRouterMaxChunks * kRouterChunk);
-    if (!ws->router_part) return fail("moe: work area has no router partials (carve it with moe_work_carve)");
+    if (!ws->router_part) return fail("moe: work area has no router scratch (carve it with moe_work_carve)");
     // one CTA per logit row (a warp per 1024-element chunk), then CTAs that
     // build the x table for the gate/up engine
     uint8_t *xtab = engine_gateup_ok(L, ws) ? ws->xtab : nullptr;
@@ -943,7 +980,7 @@ int launch_router(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaS
     const int64_t tab_ctas = xtab ? (L.hidden / kQK + nw - 1) / nw : 0;
     const unsigned grid = (unsigned)(n_total + tab_ctas);
     return check(launch_pdl(k_router, grid, nw * 32, 0, st, L, x, ws->logits, ws->topk_idx, ws->weights, ws->counter,
-                            xtab),
+                            reinterpret_cast<float2 *>(ws->router_part), xtab),
                  "moe router launch");
 }
 

@@ -109,6 +109,8 @@ constexpr int kQeJobSmem = 1024;     // shared scratch of a job (per-CTA unit ta
 //   int n_tab() const;                        // activation tables (<= QeLayout.n_tab)
 //   const uint8_t *tab_global() const;        // prebuilt tables [n_tab][tab_nsb] in global
 //                                             //   memory, or nullptr to build them here
+//   uint32_t tab_mask(const uint8_t *jsm) const;  // bit t: this CTA reads prebuilt table t
+//                                             //   (n_tab <= 32 when tab_global is set)
 //   const float *tab_src(int t) const;       // activations of table t (16-byte aligned)
 //   void finish(const uint8_t *jsm, int64_t u, const QUnit &U, double v, int lane) const;
 //       called by the 32 reducer lanes with v = row `lane`'s value (lane < 16)
@@ -199,10 +201,20 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
     const uint8_t *tg = J.tab_global();
     if (tg) {
         if (warp == prod && lane == 0) {
-            const uint32_t bytes = (uint32_t)J.n_tab() * P.tab_nsb * kTabSB;
+            // only the tables this CTA's units read
+            const uint32_t tb = (uint32_t)P.tab_nsb * kTabSB;
+            const uint32_t mask = J.tab_mask(jsm);
+            const int n_tab = J.n_tab();
+            uint32_t bytes = 0;
+            for (int t = 0; t < n_tab; t++)
+                if ((mask >> t) & 1u) bytes += tb;
             mbar_arrive_expect_tx(tabbar, bytes);
-            for (uint32_t o = 0; o < bytes; o += kQeTabChunk)
-                bulk_g2s(tab + o, tg + o, min(kQeTabChunk, bytes - o), tabbar);
+            for (int t = 0; t < n_tab; t++) {
+                if (!((mask >> t) & 1u)) continue;
+                const uint32_t base = (uint32_t)t * tb;
+                for (uint32_t o = 0; o < tb; o += kQeTabChunk)
+                    bulk_g2s(tab + base + o, tg + base + o, min(kQeTabChunk, tb - o), tabbar);
+            }
         }
         __syncthreads();                 // the job scratch written by setup()
     } else {

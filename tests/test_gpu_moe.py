@@ -121,3 +121,35 @@ def test_repeat_is_deterministic(layers):
     D.forward(x, b)
     torch.cuda.synchronize()
     assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+
+
+@pytest.mark.parametrize("n_routed,n_shared,dup", [(256, 2, False), (256, 2, True), (384, 2, True),
+                                                    (1022, 2, False), (1024, 0, True)])
+def test_router_selection_wide_and_ties(lib, oracle, n_routed, n_shared, dup):
+    """Router ids and weights for expert counts on both sides of the one-warp
+    selection's 256-entry register split, with exact score ties (duplicated
+    router rows and biases: the lower index must win)."""
+    import torch
+    from sepia_b200.lib import ok
+    from sepia_b200.moe import MoeLayerDevice
+    shape = MoeShape(hidden=1024, ff=256, n_routed=n_routed, n_shared=n_shared, topk=6)
+    rng = np.random.default_rng(n_routed)
+    n_total = n_routed + n_shared
+    w = (rng.standard_normal((n_total, shape.hidden), dtype=np.float32) * np.float32(0.02))
+    bias = rng.uniform(-0.1, 0.1, size=n_routed).astype(np.float32)
+    if dup:
+        w[1:n_routed:2] = w[0:n_routed - 1:2]
+        bias[1::2] = bias[0:n_routed - 1:2]
+        bias[:] = np.round(bias * 8) / 8      # many equal biases across pairs too
+    D = MoeLayerDevice.random(shape, seed=3)
+    D.router_w.copy_(torch.from_numpy(w))
+    D.router_bias.copy_(torch.from_numpy(bias))
+    st = torch.cuda.current_stream().cuda_stream
+    for seed in (1, 2, 5, 11):
+        x = torch.from_numpy(hidden_state(seed, shape.hidden)).cuda()
+        ok(lib.sepia_cuda_moe_router(C.byref(D.struct), x.data_ptr(), C.byref(D.ws), st))
+        torch.cuda.synchronize()
+        logits = D.logits.cpu().numpy()
+        idx, wt = oracle.route_select(logits, bias, n_routed, n_shared, 6, shape.route_scale, shape.global_scale)
+        assert np.array_equal(D.topk_idx.cpu().numpy(), idx), (seed, D.topk_idx.cpu().numpy(), idx)
+        assert oracle.rel_err(D.weights.cpu().numpy(), wt) <= 1e-5, seed
