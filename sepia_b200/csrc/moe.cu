@@ -625,6 +625,7 @@ struct GuJob {
     float *h;
     const uint8_t *xtab;
     int nsb_h, tpu, n_slots;
+    float inv_tpu;      // 1/tpu (qe_div; n_units < kQeDivMax)
     int sbs_r, nsplit_r, sbs_s, nsplit_s;
     __device__ void init() {}
     __device__ void setup(uint8_t *jsm, int tid, bool after_dep) {
@@ -649,12 +650,12 @@ struct GuJob {
     }
     __device__ int64_t n_units() const { return (int64_t)n_slots * tpu; }
     __device__ int slot_of(int a) const { return a < L.n_shared ? L.topk + a : a - L.n_shared; }
-    __device__ bool needs_dep(int64_t u) const { return slot_of((int)u / tpu) < L.topk; }
+    __device__ bool needs_dep(int64_t u) const { return slot_of(qe_div((int)u, inv_tpu)) < L.topk; }
     __device__ int splits(const uint8_t *jsm, int64_t u) const {
-        return reinterpret_cast<const MoeSlot *>(jsm)[slot_of((int)u / tpu)].nsplit;
+        return reinterpret_cast<const MoeSlot *>(jsm)[slot_of(qe_div((int)u, inv_tpu))].nsplit;
     }
     __device__ void unit(const uint8_t *jsm, int64_t u, QUnit &U) const {
-        const int a = (int)u / tpu, r = (int)u - a * tpu;
+        const int a = qe_div((int)u, inv_tpu), r = (int)u - a * tpu;
         const MoeSlot &m = reinterpret_cast<const MoeSlot *>(jsm)[slot_of(a)];
         U.type = m.type; U.rb = m.rb; U.sbs = m.sbs; U.nsplit = m.nsplit;
         U.nsb = nsb_h;
@@ -670,7 +671,7 @@ struct GuJob {
     // lanes 0-7: h = silu(g) * u in the reference's float arithmetic
     // (src/sepia.c:1405-1410; shared experts: * gamma, src/sepia.c:1432-1444)
     __device__ void finish(const uint8_t *, int64_t u, const QUnit &, double v, int lane) const {
-        const int a = (int)u / tpu, r = (int)u - a * tpu;
+        const int a = qe_div((int)u, inv_tpu), r = (int)u - a * tpu;
         const int s = slot_of(a);
         const float uv = (float)__shfl_sync(0xffffffffu, v, (lane + 8) & 31);
         if (lane < 8) {
@@ -693,6 +694,7 @@ struct DnJob {
     const uint8_t *htab;
     float *slots_out;
     int nsb_f, n_slots, n_tiles;
+    float inv_slots;    // 1/n_slots (qe_div; n_units < kQeDivMax)
     int sbs_r, nsplit_r, sbs_s, nsplit_s;
     __device__ void init() {}
     // the router finished before the gate/up kernel let its successors
@@ -717,10 +719,11 @@ struct DnJob {
     __device__ int64_t n_units() const { return (int64_t)n_slots * n_tiles; }
     __device__ bool needs_dep(int64_t) const { return false; }
     __device__ int splits(const uint8_t *jsm, int64_t u) const {
-        return reinterpret_cast<const MoeSlot *>(jsm)[(int)u % n_slots].nsplit;
+        const int t = qe_div((int)u, inv_slots);
+        return reinterpret_cast<const MoeSlot *>(jsm)[(int)u - t * n_slots].nsplit;
     }
     __device__ void unit(const uint8_t *jsm, int64_t u, QUnit &U) const {
-        const int t = (int)u / n_slots, s = (int)u - t * n_slots;
+        const int t = qe_div((int)u, inv_slots), s = (int)u - t * n_slots;
         const MoeSlot &m = reinterpret_cast<const MoeSlot *>(jsm)[s];
         const int64_t r0 = (int64_t)t * 16;
         const int nr = (int)imin64(16, L.hidden - r0);
@@ -750,7 +753,7 @@ struct DnJob {
     }
     __device__ const float *tab_src(int) const { return nullptr; }
     __device__ void finish(const uint8_t *, int64_t u, const QUnit &, double v, int lane) const {
-        const int t = (int)u / n_slots, s = (int)u - t * n_slots;
+        const int t = qe_div((int)u, inv_slots), s = (int)u - t * n_slots;
         const int64_t r0 = (int64_t)t * 16;
         if (lane < 16 && r0 + lane < L.hidden) {
             const float e = (float)v;
@@ -899,6 +902,7 @@ static int launch_gateup_engine(const MoeDev &L, const SepiaMoeWork *ws, cudaStr
     J.L = L; J.idx = ws->topk_idx; J.weights = ws->weights; J.h = ws->h;
     J.xtab = ws->xtab;
     J.nsb_h = (int)(L.hidden / kQK); J.tpu = (int)(L.ff / 8);
+    J.inv_tpu = 1.0f / (float)J.tpu;
     J.n_slots = L.topk + L.n_shared;
     const uint32_t budget = qe_row_budget(di.smem_optin, (int64_t)J.nsb_h * kTabSB);
     J.sbs_r = qe_sbs(L.gate_type, J.nsb_h, budget, J.nsplit_r);
@@ -917,6 +921,7 @@ static int launch_gateup_engine(const MoeDev &L, const SepiaMoeWork *ws, cudaStr
     const void *fn = (const void *)k_qengine<GuJob>;
     if (!ensure_smem(fn, (int)smem)) return 0;
     const int64_t units = (int64_t)J.n_slots * J.tpu;
+    if (units >= kQeDivMax) return fail("moe: %lld gate/up units exceed the engine's index range", (long long)units);
     const unsigned grid = (unsigned)std::min<int64_t>(units, di.sm_count);
     return check(launch_pdl(k_qengine<GuJob>, grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, J, P),
                  "moe gate/up (tensor cores) launch");
@@ -931,6 +936,8 @@ static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *ou
     J.nsb_f = (int)(L.ff / kQK);
     J.n_slots = L.topk + L.n_shared;
     J.n_tiles = (int)((L.hidden + 15) / 16);
+    J.inv_slots = 1.0f / (float)J.n_slots;
+    if ((int64_t)J.n_slots * J.n_tiles >= kQeDivMax) return fail("moe: too many down units");
     const uint32_t budget = qe_row_budget(di.smem_optin, (int64_t)J.n_slots * J.nsb_f * kTabSB);
     J.sbs_r = qe_sbs(L.down_type, J.nsb_f, budget, J.nsplit_r);
     J.sbs_s = J.sbs_r; J.nsplit_s = J.nsplit_r;

@@ -94,6 +94,12 @@ struct QeLayout {
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// u / n for 0 <= u < 2^22 without an integer division: (u + 0.5) / n lies
+// at least 0.5/n from an integer, more than the float product's error
+// ((u + 0.5) / n * 2^-23) for such u; inv_n = 1/n rounded to float.
+constexpr int kQeDivMax = 1 << 22;
+__device__ __forceinline__ int qe_div(int u, float inv_n) { return __float2int_rz(((float)u + 0.5f) * inv_n); }
+
 constexpr int kQeJobSmem = 1024;     // shared scratch of a job (per-CTA unit tables)
 
 // Job interface (see k_qengine):
