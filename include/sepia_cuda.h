@@ -93,8 +93,6 @@ typedef struct {
     float *slots;           /* [topk + n_shared, hidden] per-slot terms (sharded mode) */
     unsigned int *counter;  /* router completion counter; zero before first use */
     double *router_part;    /* [n_routed + n_shared, ceil(hidden/1024)] router scratch (per-row scores) */
-    uint8_t *xtab;          /* tensor-core activation table of x (hidden/256 superblocks) */
-    uint8_t *htab;          /* tables of h, [topk + n_shared, ff/256] superblocks */
 } SepiaMoeWork;
 
 size_t sepia_cuda_moe_work_bytes(const SepiaMoeLayer *L);

@@ -147,25 +147,16 @@ __device__ __forceinline__ void router_select(const MoeDev &L, const float2 *row
 // in chunk order by the last CTA, so the result does not depend on
 // scheduling. That CTA then runs the selection (one warp: the serial parts
 // are short and __syncthreads rounds would dominate).
-// Warps past the last chunk build the tensor-core activation table of x
-// (one superblock each) for the gate/up projections, when xtab is given.
 __global__ void __launch_bounds__(kRouterMaxChunks * 32) k_router(const MoeDev L, const float *x, float *logits,
                                                                    int32_t *topk_idx, float *weights,
-                                                                   unsigned int *counter, float2 *row_out,
-                                                                   uint8_t *xtab) {
+                                                                   unsigned int *counter, float2 *row_out) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nwarps = blockDim.x >> 5;
     const int n_total = L.n_routed + L.n_shared;
     const int cpr = router_chunks(L.hidden);
     const int row = blockIdx.x;
     __shared__ double s_part[kRouterMaxChunks];
     griddep_launch();
-    if (row >= n_total) {
-        // CTAs past the last row build the x table, a superblock per warp
-        griddep_wait();
-        const int sb = (row - n_total) * nwarps + warp;
-        if (xtab && sb < (int)(L.hidden / kQK)) xtab_build(xtab, x, sb + 1, sb, 1 << 30, lane);
-    } else if (warp < cpr) {
+    if (warp < cpr) {
         const int64_t c0 = (int64_t)warp * kRouterChunk;
         const int64_t n = imin64(kRouterChunk, L.hidden - c0);
         const float *w = L.router_w + (int64_t)row * L.hidden + c0;
@@ -608,11 +599,13 @@ __global__ void k_combine(const float *slots, int n_slots, int64_t hidden, float
 
 // Per-slot row sources of one launch, kept in the engine's shared job
 // scratch: matrix bases (gate/up, or down), row bytes, format and splits;
-// nsplit = 0 for slots this rank does not own.
+// nsplit = 0 for slots this rank does not own; w = the slot's combine
+// weight (down kernel: routed slots' router weights, 1 for shared ones).
 struct MoeSlot {
     const uint8_t *a, *b;
     int64_t rb;
-    int type, sbs, nsplit, pad;
+    int type, sbs, nsplit;
+    float w;
 };
 static_assert(kMaxSlots * sizeof(MoeSlot) <= (size_t)kQeJobSmem, "slot table exceeds the job scratch");
 
@@ -623,7 +616,7 @@ struct GuJob {
     const int32_t *idx;
     const float *weights;
     float *h;
-    const uint8_t *xtab;
+    const float *x;
     int nsb_h, tpu, n_slots;
     float inv_tpu;      // 1/tpu (qe_div; n_units < kQeDivMax)
     int sbs_r, nsplit_r, sbs_s, nsplit_s;
@@ -665,9 +658,8 @@ struct GuJob {
         U.hi = m.b + (int64_t)r * 8 * m.rb;
     }
     __device__ int n_tab() const { return 1; }
-    __device__ const uint8_t *tab_global() const { return xtab; }
     __device__ uint32_t tab_mask(const uint8_t *) const { return 1u; }
-    __device__ const float *tab_src(int) const { return nullptr; }
+    __device__ const float *tab_src(int) const { return x; }
     // lanes 0-7: h = silu(g) * u in the reference's float arithmetic
     // (src/sepia.c:1405-1410; shared experts: * gamma, src/sepia.c:1432-1444)
     __device__ void finish(const uint8_t *, int64_t u, const QUnit &, double v, int lane) const {
@@ -691,14 +683,14 @@ struct DnJob {
     MoeDev L;
     const int32_t *idx;
     const float *weights;
-    const uint8_t *htab;
+    const float *h;
     float *slots_out;
     int nsb_f, n_slots, n_tiles;
     float inv_slots;    // 1/n_slots (qe_div; n_units < kQeDivMax)
     int sbs_r, nsplit_r, sbs_s, nsplit_s;
     __device__ void init() {}
     // the router finished before the gate/up kernel let its successors
-    // launch, so the expert ids are final already
+    // launch, so the expert ids and weights are final already
     __device__ void setup(uint8_t *jsm, int tid, bool after_dep) {
         if (after_dep || tid >= n_slots) return;
         MoeSlot &m = reinterpret_cast<MoeSlot *>(jsm)[tid];
@@ -707,8 +699,10 @@ struct DnJob {
             m.a = L.sh_down + (int64_t)e * L.sh_down_stride;
             m.rb = L.rb_sh_down; m.type = L.sh_down_type; m.sbs = sbs_s;
             m.nsplit = (e % L.world == L.rank) ? nsplit_s : 0;
+            m.w = 1.0f;
         } else {
-            const int e = idx[tid];
+            const int e = __ldcg(idx + tid);
+            m.w = __ldcg(weights + tid);
             const bool own = e >= 0 && e < L.n_routed && e % L.world == L.rank;
             m.a = L.down + (own ? local_expert(L, e) : 0) * L.down_stride;
             m.rb = L.rb_down; m.type = L.down_type; m.sbs = sbs_r;
@@ -736,7 +730,6 @@ struct DnJob {
         U.hi = U.lo + 8 * m.rb;
     }
     __device__ int n_tab() const { return n_slots; }
-    __device__ const uint8_t *tab_global() const { return htab; }
     // units u = blockIdx.x + k*gridDim.x read table u % n_slots: the slots
     // repeat with period at most n_slots, and inactive slots need none
     __device__ uint32_t tab_mask(const uint8_t *jsm) const {
@@ -751,13 +744,14 @@ struct DnJob {
         }
         return mask;
     }
-    __device__ const float *tab_src(int) const { return nullptr; }
-    __device__ void finish(const uint8_t *, int64_t u, const QUnit &, double v, int lane) const {
+    __device__ const float *tab_src(int t) const { return h + (int64_t)t * L.ff; }
+    __device__ void finish(const uint8_t *jsm, int64_t u, const QUnit &, double v, int lane) const {
         const int t = qe_div((int)u, inv_slots), s = (int)u - t * n_slots;
         const int64_t r0 = (int64_t)t * 16;
         if (lane < 16 && r0 + lane < L.hidden) {
             const float e = (float)v;
-            slots_out[(int64_t)s * L.hidden + r0 + lane] = (s < L.topk) ? __fmul_rn(e, weights[s]) : e;
+            const float w = reinterpret_cast<const MoeSlot *>(jsm)[s].w;
+            slots_out[(int64_t)s * L.hidden + r0 + lane] = (s < L.topk) ? __fmul_rn(e, w) : e;
         }
     }
 };
@@ -873,7 +867,6 @@ static bool rows_ok(const void *base, int64_t stride, int64_t rb) {
     return ((reinterpret_cast<uintptr_t>(base) | (uintptr_t)stride | (uintptr_t)rb) & 3) == 0;
 }
 static bool engine_gateup_ok(const MoeDev &L, const SepiaMoeWork *ws) {
-    if (!ws->xtab || !ws->htab) return false;
     if (L.hidden % kQK || L.ff % kQK || L.hidden / kQK > 64 || L.ff / kQK > 16) return false;
     if (!mma_format(L.gate_type) || L.up_type != L.gate_type) return false;
     if (!rows_ok(L.gate, L.gate_stride, L.rb_gate) || !rows_ok(L.up, L.up_stride, L.rb_up) ||
@@ -888,7 +881,7 @@ static bool engine_gateup_ok(const MoeDev &L, const SepiaMoeWork *ws) {
     return true;
 }
 static bool engine_down_ok(const MoeDev &L, const SepiaMoeWork *ws) {
-    if (!ws->htab || L.ff % kQK || L.ff / kQK > 16) return false;
+    if (L.ff % kQK || L.ff / kQK > 16) return false;
     if (!mma_format(L.down_type) || !rows_ok(L.down, L.down_stride, L.rb_down)) return false;
     if (L.n_shared > 0 && (!mma_format(L.sh_down_type) || !rows_ok(L.sh_down, L.sh_down_stride, L.rb_sh_down)))
         return false;
@@ -896,11 +889,11 @@ static bool engine_down_ok(const MoeDev &L, const SepiaMoeWork *ws) {
 }
 
 
-static int launch_gateup_engine(const MoeDev &L, const SepiaMoeWork *ws, cudaStream_t st) {
+static int launch_gateup_engine(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaStream_t st) {
     DevInfo &di = dev_info();
     GuJob J;
     J.L = L; J.idx = ws->topk_idx; J.weights = ws->weights; J.h = ws->h;
-    J.xtab = ws->xtab;
+    J.x = x;
     J.nsb_h = (int)(L.hidden / kQK); J.tpu = (int)(L.ff / 8);
     J.inv_tpu = 1.0f / (float)J.tpu;
     J.n_slots = L.topk + L.n_shared;
@@ -931,7 +924,7 @@ static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *ou
                               cudaStream_t st) {
     DevInfo &di = dev_info();
     DnJob J;
-    J.L = L; J.idx = ws->topk_idx; J.weights = ws->weights; J.htab = ws->htab;
+    J.L = L; J.idx = ws->topk_idx; J.weights = ws->weights; J.h = ws->h;
     J.slots_out = slots_out ? slots_out : ws->slots;
     J.nsb_f = (int)(L.ff / kQK);
     J.n_slots = L.topk + L.n_shared;
@@ -957,12 +950,8 @@ static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *ou
     if (slots_out &&
         !check(cudaMemsetAsync(slots_out, 0, (size_t)J.n_slots * L.hidden * sizeof(float), st), "moe slot clear"))
         return 0;
-    // tables of every slot's h, then the down projections, then the combine
-    const int tab_warps = J.n_slots * J.nsb_f;
-    if (!check(launch_pdl(k_xtab, (unsigned)((tab_warps + 7) / 8), 256, 0, st, (const float *)ws->h, (int64_t)L.ff,
-                          J.n_slots, J.nsb_f, ws->htab),
-               "moe h tables launch"))
-        return 0;
+    // the down projections (each CTA builds the h tables it reads), then
+    // the combine
     const int64_t units = (int64_t)J.n_slots * J.n_tiles;
     const unsigned grid = (unsigned)std::min<int64_t>(units, di.sm_count);
     if (!check(launch_pdl(k_qengine<DnJob>, grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, J, P),
@@ -980,19 +969,15 @@ int launch_router(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaS
     if (router_chunks(L.hidden) > kRouterMaxChunks)
         return fail("moe: hidden %lld exceeds the router's %d", (long long)L.hidden, kRouterMaxChunks * kRouterChunk);
     if (!ws->router_part) return fail("moe: work area has no router scratch (carve it with moe_work_carve)");
-    // one CTA per logit row (a warp per 1024-element chunk), then CTAs that
-    // build the x table for the gate/up engine
-    uint8_t *xtab = engine_gateup_ok(L, ws) ? ws->xtab : nullptr;
+    // one CTA per logit row, a warp per 1024-element chunk
     const int nw = std::max(kRouterWarps, router_chunks(L.hidden));
-    const int64_t tab_ctas = xtab ? (L.hidden / kQK + nw - 1) / nw : 0;
-    const unsigned grid = (unsigned)(n_total + tab_ctas);
-    return check(launch_pdl(k_router, grid, nw * 32, 0, st, L, x, ws->logits, ws->topk_idx, ws->weights, ws->counter,
-                            reinterpret_cast<float2 *>(ws->router_part), xtab),
+    return check(launch_pdl(k_router, (unsigned)n_total, nw * 32, 0, st, L, x, ws->logits, ws->topk_idx, ws->weights,
+                            ws->counter, reinterpret_cast<float2 *>(ws->router_part)),
                  "moe router launch");
 }
 
 int launch_gateup(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaStream_t st) {
-    if (engine_gateup_ok(L, ws)) return launch_gateup_engine(L, ws, st);
+    if (engine_gateup_ok(L, ws)) return launch_gateup_engine(L, x, ws, st);
     DevInfo &di = dev_info();
     GuParams G;
     G.L = L; G.x = x; G.idx = ws->topk_idx; G.weights = ws->weights; G.h = ws->h;
@@ -1072,8 +1057,6 @@ extern "C" size_t sepia_cuda_moe_work_bytes(const SepiaMoeLayer *L) {
     add(n_slots * (size_t)L->hidden * 4);  // slots
     add(256);                         // counter
     add(n_total * (size_t)router_chunks(L->hidden) * 8);  // router_part
-    add((size_t)(L->hidden / kQK) * kTabSB);                        // xtab
-    add(n_slots * (size_t)(L->ff / kQK) * kTabSB);                  // htab
     return b;
 }
 
@@ -1093,8 +1076,6 @@ extern "C" int sepia_cuda_moe_work_carve(const SepiaMoeLayer *L, void *base, siz
     ws->slots = (float *)take(n_slots * (size_t)L->hidden * 4);
     ws->counter = (unsigned int *)take(256);
     ws->router_part = (double *)take(n_total * (size_t)router_chunks(L->hidden) * 8);
-    ws->xtab = take((size_t)(L->hidden / kQK) * kTabSB);
-    ws->htab = take(n_slots * (size_t)(L->ff / kQK) * kTabSB);
     return 1;
 }
 
@@ -1152,3 +1133,9 @@ extern "C" int sepia_cuda_topk_select(const float *scores, int32_t n, int32_t to
     k_topk<<<1, 32, 0, as_stream(stream)>>>(scores, n, topk, idx);
     return check(cudaGetLastError(), "topk launch");
 }
+
+#ifdef SEPIA_QE_STAMPS
+extern "C" __attribute__((visibility("default"))) int sepia_qe_stamps(void *dst) {
+    return cudaMemcpyFromSymbol(dst, sepia::g_qe_stamps, sizeof(sepia::g_qe_stamps)) == cudaSuccess;
+}
+#endif

@@ -13,7 +13,7 @@
 //              1-D cp.async.bulk (one copy per row, 16-byte aligned rows,
 //              padded pitch so the 8 rows of an MMA tile hit distinct
 //              shared-memory banks), completing on the slot's "full" mbarrier;
-//              prebuilt activation tables arrive by one more bulk copy;
+//              the other warps build the activation tables first;
 //   consumers  G groups of cg warps; group k % G takes item k, its warps
 //              splitting the item's superblocks into cg chunks; each warp
 //              runs the format's tile walk (qtile.cuh) and stores its fp64
@@ -34,7 +34,7 @@ namespace sepia {
 constexpr int kQeMaxCons = 16;
 constexpr int kQeMaxStages = 8;
 constexpr int kQeThreadsMax = (kQeMaxCons + 2) * 32;
-constexpr uint32_t kQeTabChunk = 32768;    // bytes per table bulk copy
+constexpr int kQeBuildBatch = 4;           // table superblocks a warp loads before computing
 
 struct QUnit {
     int type;              // quant format of both halves
@@ -100,6 +100,22 @@ __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.
 constexpr int kQeDivMax = 1 << 22;
 __device__ __forceinline__ int qe_div(int u, float inv_n) { return __float2int_rz(((float)u + 0.5f) * inv_n); }
 
+// Optional phase timestamps for profiling builds (-DSEPIA_QE_STAMPS):
+// [job kind][CTA][phase] of the last launch, in globaltimer nanoseconds.
+#ifdef SEPIA_QE_STAMPS
+__device__ unsigned long long g_qe_stamps[2][1024][8];
+#define QE_STAMP(k)                                                                 \
+    do {                                                                            \
+        unsigned long long t_;                                                      \
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                      \
+        if (blockIdx.x < 1024) g_qe_stamps[J.n_tab() > 1][blockIdx.x][k] = t_;      \
+    } while (0)
+#else
+#define QE_STAMP(k) \
+    do {            \
+    } while (0)
+#endif
+
 constexpr int kQeJobSmem = 1024;     // shared scratch of a job (per-CTA unit tables)
 
 // Job interface (see k_qengine):
@@ -113,24 +129,22 @@ constexpr int kQeJobSmem = 1024;     // shared scratch of a job (per-CTA unit ta
 //   void unit(const uint8_t *jsm, int64_t u, QUnit &U) const;   // U.nsplit = 0: nothing to do
 //   int splits(const uint8_t *jsm, int64_t u) const;             // U.nsplit alone (cheap)
 //   int n_tab() const;                        // activation tables (<= QeLayout.n_tab)
-//   const uint8_t *tab_global() const;        // prebuilt tables [n_tab][tab_nsb] in global
-//                                             //   memory, or nullptr to build them here
-//   uint32_t tab_mask(const uint8_t *jsm) const;  // bit t: this CTA reads prebuilt table t
-//                                             //   (n_tab <= 32 when tab_global is set)
-//   const float *tab_src(int t) const;       // activations of table t (16-byte aligned)
+//   uint32_t tab_mask(const uint8_t *jsm) const;  // bit t: this CTA's units read table t (n_tab <= 32)
+//   const float *tab_src(int t) const;       // activations of table t, written before the
+//                                             //   predecessor completed (read through L2)
 //   void finish(const uint8_t *jsm, int64_t u, const QUnit &U, double v, int lane) const;
 //       called by the 32 reducer lanes with v = row `lane`'s value (lane < 16)
 template <class Job>
 __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, const QeLayout P) {
     Job J = Jp;
     J.init();
+    if (threadIdx.x == 0) QE_STAMP(0);
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_cons = P.G * P.cg, prod = n_cons, redw = n_cons + 1;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *ready = full + kQeMaxStages;
     uint64_t *empty = ready + kQeMaxStages;
-    uint64_t *tabbar = empty + kQeMaxStages;      // prebuilt tables landed
     double *red = reinterpret_cast<double *>(smem + P.red_off);      // [stages][cg][16]
     uint8_t *tab = smem + P.tab_off;
     uint8_t *stage0 = smem + P.stage_off;
@@ -144,7 +158,6 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             mbar_init(&ready[s], P.cg);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(tabbar, 1);
         fence_barrier_init();
     }
     __syncthreads();
@@ -199,35 +212,49 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             }
         }
     }
+    if (warp == prod && lane == 0) QE_STAMP(7);
     griddep_wait();
-    if (threadIdx.x == 0) griddep_launch();
+    if (threadIdx.x == 0) {
+        QE_STAMP(1);
+        griddep_launch();
+    }
     J.setup(jsm, threadIdx.x, true);
-    // Activation tables: prebuilt ones arrive by one bulk copy (consumers
-    // wait on tabbar), otherwise every warp builds them here.
-    const uint8_t *tg = J.tab_global();
-    if (tg) {
-        if (warp == prod && lane == 0) {
-            // only the tables this CTA's units read
-            const uint32_t tb = (uint32_t)P.tab_nsb * kTabSB;
-            const uint32_t mask = J.tab_mask(jsm);
-            const int n_tab = J.n_tab();
-            uint32_t bytes = 0;
-            for (int t = 0; t < n_tab; t++)
-                if ((mask >> t) & 1u) bytes += tb;
-            mbar_arrive_expect_tx(tabbar, bytes);
-            for (int t = 0; t < n_tab; t++) {
-                if (!((mask >> t) & 1u)) continue;
-                const uint32_t base = (uint32_t)t * tb;
-                for (uint32_t o = 0; o < tb; o += kQeTabChunk)
-                    bulk_g2s(tab + base + o, tg + base + o, min(kQeTabChunk, tb - o), tabbar);
-            }
-        }
-        __syncthreads();                 // the job scratch written by setup()
+    // The producer needs only warp 0's post-dependency job scratch (named
+    // barrier 1: warp 0 arrives, the producer waits); the other warps build
+    // the activation tables their units read and meet on barrier 2. The
+    // producer, possibly still blocked issuing its first copies, holds
+    // nobody up.
+    if (warp == prod) {
+        named_bar_sync(1, 64);
     } else {
-        const int n_tab = J.n_tab();
-        for (int t = 0; t < n_tab; t++)
-            xtab_build(tab + (size_t)t * P.tab_nsb * kTabSB, J.tab_src(t), P.tab_nsb, warp, blockDim.x >> 5, lane);
-        __syncthreads();
+        if (warp == 0) named_bar_arrive(1, 64);
+        // superblock q of the needed tables (in table order) goes to warp
+        // q % nbw; a warp loads up to kQeBuildBatch of them before it
+        // computes any, so their L2 latencies overlap
+        const uint32_t mask = J.tab_mask(jsm);
+        const int n_build = __popc(mask) * P.tab_nsb;
+        const int bw = warp < prod ? warp : warp - 1, nbw = n_cons + 1;
+        for (int q0 = bw; q0 < n_build; q0 += kQeBuildBatch * nbw) {
+            float v[kQeBuildBatch][8];
+            uint8_t *te[kQeBuildBatch];
+#pragma unroll
+            for (int i = 0; i < kQeBuildBatch; i++) {
+                const int q = q0 + i * nbw;
+                te[i] = nullptr;
+                if (q < n_build) {
+                    const int k = q / P.tab_nsb, sb = q - k * P.tab_nsb;
+                    uint32_t m = mask;
+                    for (int j = 0; j < k; j++) m &= m - 1;      // drop the k lowest tables
+                    const int t = __ffs(m) - 1;
+                    te[i] = tab + ((size_t)t * P.tab_nsb + sb) * kTabSB;
+                    xtab_load<true>(J.tab_src(t) + (size_t)sb * kQK, lane, v[i]);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kQeBuildBatch; i++)
+                if (te[i]) xtab_emit(te[i], v[i], lane);
+        }
+        named_bar_sync(2, (n_cons + 1) * 32);
     }
 
     if (warp == prod) {
@@ -247,8 +274,8 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
                     pu += gridDim.x;
                 }
             }
+            QE_STAMP(6);
             // no bulk copy may be in flight when the CTA exits
-            if (tg) mbar_wait(tabbar, 0, nullptr);
             if (ok)
                 for (int64_t j = (pk > P.stages ? pk - P.stages : 0); j < pk; j++)
                     mbar_wait(&full[j % P.stages], (uint32_t)((j / P.stages) & 1), nullptr);
@@ -277,11 +304,13 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             if (!ok) break;
             J.finish(jsm, u, U, acc, lane);
         }
+        if (lane == 0) QE_STAMP(5);
         return;
     }
 
     // consumers
-    if (tg && !mbar_wait(tabbar, 0, P.err)) return;
+    if (warp == 0 && lane == 0) QE_STAMP(2);
+    bool first = true;
     const int grp = warp / P.cg, cw = warp % P.cg;
     const LaneCtx C = lane_ctx(lane);
     QeRing ring;
@@ -308,6 +337,8 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             if (++g == P.G) g = 0;
             if (!mine) continue;
             if (!mbar_wait(&full[slot], phase, P.err)) return;
+            if (first && warp == 0 && lane == 0) QE_STAMP(3);
+            first = false;
             const int s0 = sp * U.sbs, s1 = min(U.nsb, s0 + U.sbs), n = s1 - s0;
             const uint32_t pitch = qe_pitch((uint32_t)n * (uint32_t)sbB);
             // (cw*n)/cg exactly: the +0.5 keeps the float product away from
@@ -337,19 +368,7 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             if (lane == 0) mbar_arrive(&ready[slot]);   // release: the partials above are visible to the reducer
         }
     }
-}
-
-// Activation tables in global memory: n_vec vectors of nsb superblocks
-// (vector v at x + v*x_stride, its tables at tab + v*nsb*kTabSB), one warp
-// per superblock.
-static __global__ void k_xtab(const float *x, int64_t x_stride, int n_vec, int nsb, uint8_t *tab) {
-    const int w = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
-    griddep_wait();
-    griddep_launch();
-    if (w >= n_vec * nsb) return;
-    const int v = w / nsb, sb = w - v * nsb;
-    xtab_build<true>(tab + ((size_t)v * nsb + sb) * kTabSB, x + v * x_stride + (int64_t)sb * kQK, 1, 0, 1,
-                     threadIdx.x & 31);
+    if (warp == 0 && lane == 0) QE_STAMP(4);
 }
 
 // Host: the largest row an item may carry whole, given the activation-table

@@ -145,7 +145,6 @@ struct MvJob {
     __device__ void setup(uint8_t *, int, bool) {}
     __device__ int64_t n_units() const { return (out_dim + 15) / 16; }
     __device__ bool needs_dep(int64_t) const { return false; }
-    __device__ const uint8_t *tab_global() const { return nullptr; }
     __device__ uint32_t tab_mask(const uint8_t *) const { return 1u; }
     __device__ int splits(const uint8_t *, int64_t) const { return nsplit; }
     __device__ void unit(const uint8_t *, int64_t u, QUnit &U) const {

@@ -77,82 +77,94 @@ __device__ __forceinline__ void limbs5(long long v, int (&d)[5]) {
     d[4] = (int)v;
 }
 
+// Table entry of one superblock, in two steps so that a warp can issue the
+// loads of several superblocks before it computes any. Lane l owns part
+// l/4 and tig l%4: positions 32*part + 8*tig + {0..7} of the superblock.
+// CG: read through L2 only (x was written by another grid or other CTAs).
+template <bool CG = false>
+__device__ __forceinline__ void xtab_load(const float *xsb, int lane, float (&v)[8]) {
+    const float *xs = xsb + 32 * (lane >> 2) + 8 * (lane & 3);
+    if ((reinterpret_cast<uintptr_t>(xs) & 15) == 0) {
+        const float4 lo = CG ? __ldcg(reinterpret_cast<const float4 *>(xs)) : *reinterpret_cast<const float4 *>(xs);
+        const float4 hi =
+            CG ? __ldcg(reinterpret_cast<const float4 *>(xs + 4)) : *reinterpret_cast<const float4 *>(xs + 4);
+        v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
+        v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = CG ? __ldcg(xs + j) : xs[j];
+    }
+}
+
+__device__ inline void xtab_emit(uint8_t *te, const float (&v)[8], int lane) {
+    const int part = lane >> 2, tig = lane & 3;
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(v[j]));
+    m = warp_max(m);
+    int e = (m > 0.f) ? ((__float_as_int(m) >> 23) & 0xFF) - 127 : 0;
+    e = max(-90, min(e, 90));
+    const float scale = __int_as_float((127 + kXShift - e) << 23);
+    int xi[8];
+    uint32_t w0[4] = {0, 0, 0, 0}, w1[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        xi[j] = __float2int_rn(v[j] * scale);
+        int d[4];
+        limbs4(xi[j], d);
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            if (j < 4) w0[l] |= (uint32_t)(d[l] & 255) << (8 * j);
+            else w1[l] |= (uint32_t)(d[l] & 255) << (8 * (j - 4));
+        }
+    }
+    uint2 *bd = reinterpret_cast<uint2 *>(te) + part * 16 + tig * 4;
+#pragma unroll
+    for (int l = 0; l < 4; l++) bd[l] = make_uint2(w0[l], w1[l]);
+    // group sums: group 2*part = elements 0-15 of the part (lanes tig
+    // 0,1), group 2*part+1 = elements 16-31 (lanes tig 2,3)
+    long long gs = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) gs += xi[j];
+    gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+    const long long g0 = gs, g1 = __shfl_xor_sync(0xffffffffu, gs, 2);
+    // k16 fragment words: lane (gid = limb, t) holds k = 4t..4t+3
+    uint8_t *g16 = te + kTabG16, *g32 = te + kTabG32;
+    if (tig == 0) {
+        int d0[5], d1[5], dp[5];
+        limbs5(g0, d0);
+        limbs5(g1, d1);
+        limbs5(g0 + g1, dp);
+#pragma unroll
+        for (int l = 0; l < 5; l++) {
+            // groups 2p, 2p+1 -> word t = p/2, bytes 2(p&1), 2(p&1)+1
+            uint8_t *wp = g16 + 4 * ((part >> 1) * 8 + l);
+            wp[2 * (part & 1)] = (uint8_t)(d0[l] & 255);
+            wp[2 * (part & 1) + 1] = (uint8_t)(d1[l] & 255);
+            // part p -> word t = p/4, byte p&3 (k 8..15 are zero)
+            g32[4 * ((part >> 2) * 8 + l) + (part & 3)] = (uint8_t)(dp[l] & 255);
+        }
+    }
+    // zero words: limbs 5-7 everywhere, and k 8..15 of the part sums
+    if (lane < 12) {
+        const int t = lane / 3, l = 5 + lane % 3;
+        reinterpret_cast<uint32_t *>(g16)[t * 8 + l] = 0u;
+        reinterpret_cast<uint32_t *>(g32)[t * 8 + l] = 0u;
+    } else if (lane < 28) {
+        const int t = 2 + (lane - 12) / 8, l = (lane - 12) % 8;
+        reinterpret_cast<uint32_t *>(g32)[t * 8 + l] = 0u;
+    }
+    if (lane == 0) *reinterpret_cast<float *>(te + kTabUnit) = __int_as_float((127 - kXShift + e) << 23);
+}
+
 // Build the table entries of x[0 .. nsb*256) into tab (shared or global
-// memory), one warp per superblock (x at least 4-byte aligned). Lane l owns
-// part l/4 and tig l%4: positions 32*part + 8*tig + {0..7}.
-// CG: read x through L2 only (x was written by other CTAs of this grid).
+// memory), one warp per superblock (x at least 4-byte aligned).
 template <bool CG = false>
 __device__ inline void xtab_build(uint8_t *tab, const float *x, int nsb, int warp, int nwarps, int lane) {
-    const int part = lane >> 2, tig = lane & 3;
     for (int sb = warp; sb < nsb; sb += nwarps) {
-        uint8_t *te = tab + (size_t)sb * kTabSB;
-        const float *xs = x + (size_t)sb * kQK + 32 * part + 8 * tig;
-        float4 lo, hi;
-        if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-            lo = CG ? __ldcg(reinterpret_cast<const float4 *>(xs)) : *reinterpret_cast<const float4 *>(xs);
-            hi = CG ? __ldcg(reinterpret_cast<const float4 *>(xs + 4)) : *reinterpret_cast<const float4 *>(xs + 4);
-        } else {
-            lo = make_float4(xs[0], xs[1], xs[2], xs[3]);
-            hi = make_float4(xs[4], xs[5], xs[6], xs[7]);
-        }
-        const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-        float m = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(v[j]));
-        m = warp_max(m);
-        int e = (m > 0.f) ? ((__float_as_int(m) >> 23) & 0xFF) - 127 : 0;
-        e = max(-90, min(e, 90));
-        const float scale = __int_as_float((127 + kXShift - e) << 23);
-        int xi[8];
-        uint32_t w0[4] = {0, 0, 0, 0}, w1[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            xi[j] = __float2int_rn(v[j] * scale);
-            int d[4];
-            limbs4(xi[j], d);
-#pragma unroll
-            for (int l = 0; l < 4; l++) {
-                if (j < 4) w0[l] |= (uint32_t)(d[l] & 255) << (8 * j);
-                else w1[l] |= (uint32_t)(d[l] & 255) << (8 * (j - 4));
-            }
-        }
-        uint2 *bd = reinterpret_cast<uint2 *>(te) + part * 16 + tig * 4;
-#pragma unroll
-        for (int l = 0; l < 4; l++) bd[l] = make_uint2(w0[l], w1[l]);
-        // group sums: group 2*part = elements 0-15 of the part (lanes tig
-        // 0,1), group 2*part+1 = elements 16-31 (lanes tig 2,3)
-        long long gs = 0;
-#pragma unroll
-        for (int j = 0; j < 8; j++) gs += xi[j];
-        gs += __shfl_xor_sync(0xffffffffu, gs, 1);
-        const long long g0 = gs, g1 = __shfl_xor_sync(0xffffffffu, gs, 2);
-        // k16 fragment words: lane (gid = limb, t) holds k = 4t..4t+3
-        uint8_t *g16 = te + kTabG16, *g32 = te + kTabG32;
-        if (tig == 0) {
-            int d0[5], d1[5], dp[5];
-            limbs5(g0, d0);
-            limbs5(g1, d1);
-            limbs5(g0 + g1, dp);
-#pragma unroll
-            for (int l = 0; l < 5; l++) {
-                // groups 2p, 2p+1 -> word t = p/2, bytes 2(p&1), 2(p&1)+1
-                uint8_t *wp = g16 + 4 * ((part >> 1) * 8 + l);
-                wp[2 * (part & 1)] = (uint8_t)(d0[l] & 255);
-                wp[2 * (part & 1) + 1] = (uint8_t)(d1[l] & 255);
-                // part p -> word t = p/4, byte p&3 (k 8..15 are zero)
-                g32[4 * ((part >> 2) * 8 + l) + (part & 3)] = (uint8_t)(dp[l] & 255);
-            }
-        }
-        // zero words: limbs 5-7 everywhere, and k 8..15 of the part sums
-        if (lane < 12) {
-            const int t = lane / 3, l = 5 + lane % 3;
-            reinterpret_cast<uint32_t *>(g16)[t * 8 + l] = 0u;
-            reinterpret_cast<uint32_t *>(g32)[t * 8 + l] = 0u;
-        } else if (lane < 28) {
-            const int t = 2 + (lane - 12) / 8, l = (lane - 12) % 8;
-            reinterpret_cast<uint32_t *>(g32)[t * 8 + l] = 0u;
-        }
-        if (lane == 0) *reinterpret_cast<float *>(te + kTabUnit) = __int_as_float((127 - kXShift + e) << 23);
+        float v[8];
+        xtab_load<CG>(x + (size_t)sb * kQK, lane, v);
+        xtab_emit(tab + (size_t)sb * kTabSB, v, lane);
     }
 }
 

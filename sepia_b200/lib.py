@@ -36,8 +36,7 @@ class SepiaMoeLayer(C.Structure):
 
 
 class SepiaMoeWork(C.Structure):
-    _fields_ = [("logits", vp), ("topk_idx", vp), ("weights", vp), ("h", vp), ("slots", vp), ("counter", vp), ("router_part", vp),
-                ("xtab", vp), ("htab", vp)]
+    _fields_ = [("logits", vp), ("topk_idx", vp), ("weights", vp), ("h", vp), ("slots", vp), ("counter", vp), ("router_part", vp)]
 
 
 class SepiaGpuMoeDesc(C.Structure):
