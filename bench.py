@@ -370,7 +370,7 @@ def main():
         ms = float(t.item())
     tok_bytes = shape.token_bytes()
     gbs = args.steps * tok_bytes / (ms / 1e3) / 1e9
-    launches_per_step = 3 if world == 1 else 4
+    launches_per_step = 4   # router, gate/up, down, combine (N > 1: the all-reduce is NCCL's)
 
     # ---- per-kernel live timing (same workload, events between launches) ----
     kt = per_kernel_times(layers, X, args, world, group)
