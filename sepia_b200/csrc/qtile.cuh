@@ -214,6 +214,7 @@ struct LaneCtx {
     float lws;           // split layout: same, every lane
     float lwg;           // group-sum MMAs (8 limb columns): 256^(2 tig)
     uint32_t bsel;       // byte_perm selector of the lane's group scale byte (group 2p + tig/2)
+    uint32_t ssel0, ssel1;   // prmt selectors: byte tig/2 (resp. 2 + tig/2), sign-extended
 };
 __device__ __forceinline__ LaneCtx lane_ctx(int lane) {
     LaneCtx L;
@@ -229,6 +230,9 @@ __device__ __forceinline__ LaneCtx lane_ctx(int lane) {
     L.lwn = (L.tig < 2) ? L.lws : 0.0f;
     L.lwg = (L.tig == 0) ? 1.0f : (L.tig == 1) ? 65536.0f : (L.tig == 2) ? 4294967296.0f : 0.0f;
     L.bsel = 0x4440u + (uint32_t)(L.tig >> 1);
+    const uint32_t j0 = (uint32_t)(L.tig >> 1), j1 = j0 + 2;
+    L.ssel0 = j0 | ((j0 | 8) << 4) | ((j0 | 8) << 8) | ((j0 | 8) << 12);
+    L.ssel1 = j1 | ((j1 | 8) << 4) | ((j1 | 8) << 8) | ((j1 | 8) << 12);
     return L;
 }
 
@@ -321,31 +325,33 @@ __device__ __forceinline__ uint32_t ldw2(const uint8_t *p) {
     else return ldw(p);
 }
 
-// signed scales (sc - 32) of groups 4i..4i+3 as bytes of G[i]
+// prmt of w with a precomputed selector (sign-extending byte select)
+__device__ __forceinline__ int prmt_sel(uint32_t w, uint32_t sel) {
+    int r;
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(sel));
+    return r;
+}
+
+// Signed scales (sc - 32) of groups 4i..4i+3 as the bytes of one word, for
+// i = tig: each lane of a quad unpacks one of the four words of its row.
 template <bool ODD>
-__device__ __forceinline__ void q3k_scales(const uint8_t *sc, uint32_t (&G)[4]) {
-    const uint32_t S0 = ldw2<ODD>(sc), S1 = ldw2<ODD>(sc + 4), S2 = ldw2<ODD>(sc + 8);
-    uint32_t U[4];
-    U[0] = (S0 & 0x0F0F0F0Fu) | ((S2 & 0x03030303u) << 4);
-    U[1] = (S1 & 0x0F0F0F0Fu) | (((S2 >> 2) & 0x03030303u) << 4);
-    U[2] = ((S0 >> 4) & 0x0F0F0F0Fu) | (((S2 >> 4) & 0x03030303u) << 4);
-    U[3] = ((S1 >> 4) & 0x0F0F0F0Fu) | (((S2 >> 6) & 0x03030303u) << 4);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        // 6-bit unsigned -> signed byte (sc - 32): flip bit 5, then copy the
-        // new bit 5 into bits 6 and 7
-        const uint32_t t = U[i] ^ 0x20202020u, sg = t & 0x20202020u;
-        G[i] = t | (sg * 6u);
-    }
+__device__ __forceinline__ uint32_t q3k_scale_word(const uint8_t *sc, int tig) {
+    const uint32_t Sa = ldw2<ODD>(sc + 4 * (tig & 1)), S2 = ldw2<ODD>(sc + 8);
+    const uint32_t U = ((Sa >> (2 * (tig & 2))) & 0x0F0F0F0Fu) | (((S2 >> (2 * tig)) & 0x03030303u) << 4);
+    // 6-bit unsigned -> signed byte (sc - 32): flip bit 5, then copy the
+    // new bit 5 into bits 6 and 7
+    const uint32_t t = U ^ 0x20202020u, sg = t & 0x20202020u;
+    return t | (sg * 6u);
 }
 
 template <bool ODD>
 __device__ __forceinline__ void sb_q3k(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const LaneCtx &C,
                                        double &yg, double &yg8) {
-    const int tig = C.tig, t = tig >> 1;
-    uint32_t G[4], G8[4];
-    q3k_scales<ODD>(bg + 96, G);
-    q3k_scales<ODD>(bg8 + 96, G8);
+    const int tig = C.tig;
+    // this lane's scale word (groups 4tig..4tig+3) of rows gid and gid+8;
+    // part p's scales come from quad lane p/2
+    const uint32_t Gw = q3k_scale_word<ODD>(bg + 96, tig), Gw8 = q3k_scale_word<ODD>(bg8 + 96, tig);
+    const int qbase = 4 * C.gid;
     const uint32_t hm[4] = {ldw2<ODD>(bg + 8 * tig), ldw2<ODD>(bg8 + 8 * tig), ldw2<ODD>(bg + 8 * tig + 4),
                             ldw2<ODD>(bg8 + 8 * tig + 4)};
     int acc[4] = {0, 0, 0, 0}, accq[4] = {0, 0, 0, 0};
@@ -357,6 +363,10 @@ __device__ __forceinline__ void sb_q3k(const uint8_t *bg, const uint8_t *bg8, co
         uint32_t w4[4];
 #pragma unroll
         for (int r = 0; r < 4; r++) w4[r] = w[r] >> 4;
+        const uint32_t ga = __shfl_sync(0xffffffffu, Gw, qbase + 2 * h);
+        const uint32_t gb = __shfl_sync(0xffffffffu, Gw, qbase + 2 * h + 1);
+        const uint32_t ga8 = __shfl_sync(0xffffffffu, Gw8, qbase + 2 * h);
+        const uint32_t gb8 = __shfl_sync(0xffffffffu, Gw8, qbase + 2 * h + 1);
 #pragma unroll
         for (int s = 0; s < 4; s++) {
             const int p = 4 * h + s;
@@ -374,8 +384,10 @@ __device__ __forceinline__ void sb_q3k(const uint8_t *bg, const uint8_t *bg8, co
             int cc[4];
             mma_k32_z(cc, a[0], a[1], a[2], a[3], e.x & C.msplit, e.y & C.msplit);
             // this lane's group: 2p + t
-            const int sg = sbyte_of(G[p >> 1], 2 * (p & 1) + t);
-            const int sg8 = sbyte_of(G8[p >> 1], 2 * (p & 1) + t);
+            // group 2p + t: byte 2(p&1) + t of word p/2 (= 2h + s/2)
+            const uint32_t sl = (p & 1) ? C.ssel1 : C.ssel0;
+            const int sg = prmt_sel((s < 2) ? ga : gb, sl);
+            const int sg8 = prmt_sel((s < 2) ? ga8 : gb8, sl);
             int *ac = (s & 1) ? accq : acc;
             ac[0] += sg * cc[0];
             ac[1] += sg * cc[1];
@@ -387,9 +399,7 @@ __device__ __forceinline__ void sb_q3k(const uint8_t *bg, const uint8_t *bg8, co
     // sums' 5 limbs
     int cm[4] = {0, 0, 0, 0};
     {
-        const uint32_t gw = (tig == 0) ? G[0] : (tig == 1) ? G[1] : (tig == 2) ? G[2] : G[3];
-        const uint32_t gw8 = (tig == 0) ? G8[0] : (tig == 1) ? G8[1] : (tig == 2) ? G8[2] : G8[3];
-        mma_k16_ss(cm, gw, gw8, ld_g(te, kTabG16, C));
+        mma_k16_ss(cm, Gw, Gw8, ld_g(te, kTabG16, C));
     }
     const int v0 = acc[0] + (accq[0] >> 2), v1 = acc[1] + (accq[1] >> 2);
     const int v2 = acc[2] + (accq[2] >> 2), v3 = acc[3] + (accq[3] >> 2);
