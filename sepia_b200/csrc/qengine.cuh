@@ -196,10 +196,13 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
     QeRing pring;
     QUnit PU;
     PU.nsplit = 0;
-    // The first `stages` items need no empty-wait; those of units that do
-    // not depend on the predecessor kernel are issued before waiting for it.
+    // The first `stages` items need no empty-wait. Up to half of them, of
+    // units that do not depend on the predecessor kernel, are issued before
+    // waiting for it: more would only queue the table loads that follow the
+    // wait behind weight data (measured +1 % on the MoE layer).
     if (warp == prod && lane == 0) {
-        while (pu < n_units && pk < P.stages && !J.needs_dep(pu)) {
+        const int pre = max(1, P.stages / 2);
+        while (pu < n_units && pk < pre && !J.needs_dep(pu)) {
             if (psp == 0) J.unit(jsm, pu, PU);
             if (psp < PU.nsplit) {
                 issue(PU, psp, pring.slot);
