@@ -164,6 +164,72 @@ __device__ __forceinline__ float dot_q4_k(const uint8_t *b, int p, const XPart &
     return fmaf(dl * (x.inv * 16.0f), s0 + s1, -ml * (x.s16[0] + x.s16[1]));
 }
 
+// ------------------------------------------------------------ IQ2_XXS / IQ1_S
+// Codebook formats with unscaled activations: each grid byte v (0..255)
+// becomes the exact float 2^23 + v by one byte permute with the exponent
+// byte 0x4B, and one subtraction; signs flip the activation's sign bit. The
+// part's 32 products sum in fp32 (relative error ~1e-7, far inside the
+// 1e-4 parity bound) and the part scale multiplies once.
+__device__ __forceinline__ float grid_byte_f(uint32_t w, int j) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, (uint32_t)j | 0x7650u)) - 8388608.0f;
+}
+__device__ __forceinline__ float flip_if(float x, uint32_t s, int j) {
+    return __int_as_float(__float_as_int(x) ^ (int)((s << (31 - j)) & 0x80000000u));
+}
+
+// gguf IQ2_XXS: per 32 elements idx (4 grid rows of 8 bytes), signs and a
+// 4-bit scale: db = d * (0.5 + s) * 0.25 (src decode: decode_part_exact).
+__device__ __forceinline__ float dot_iq2_xxs(const uint8_t *b, int p, const XPart &x) {
+    const float d = cvt16<true>(rd16(b));
+    const uint32_t idx = rd32(b + 2 + 8 * p), sg = rd32(b + 6 + 8 * p);
+    const float db = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(sg >> 28))), 0.25f);
+    float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+    for (int l = 0; l < 4; l++) {
+        const uint64_t row = sepia_iq2xxs_grid[(idx >> (8 * l)) & 255];
+        const uint32_t s = sepia_ksigns_iq2xs[(sg >> (7 * l)) & 127];
+        const uint32_t lo = (uint32_t)row, hi = (uint32_t)(row >> 32);
+        const float *xv = x.v + 8 * l;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            t0 = fmaf(grid_byte_f(lo, j), flip_if(xv[j], s, j), t0);
+            t1 = fmaf(grid_byte_f(hi, j), flip_if(xv[4 + j], s, 4 + j), t1);
+        }
+    }
+    return db * (t0 + t1);
+}
+
+// gguf IQ1_S: grid bytes g in {-1, 0, 1}, value dl * (g + delta). The
+// bytewise u = g + 1 in {0, 1, 2} (carry-free) becomes the float g exactly
+// as (2^23 + u) - (2^23 + 1); sum (g + delta) x = sum g x + delta * sum x
+// (summing g x directly: no cancellation against sum x).
+__device__ __forceinline__ uint32_t plus1_bytes(uint32_t w) {
+    return ((w & 0x7F7F7F7Fu) + 0x01010101u) ^ (w & 0x80808080u);
+}
+__device__ __forceinline__ float grid_g_f(uint32_t u, int j) {
+    return __uint_as_float(__byte_perm(u, 0x4B000000u, (uint32_t)j | 0x7650u)) - 8388609.0f;
+}
+__device__ __forceinline__ float dot_iq1_s(const uint8_t *b, int p, const XPart &x) {
+    const float d = cvt16<true>(rd16(b));
+    const uint32_t h = rd16(b + 34 + 2 * p);
+    const float dl = __fmul_rn(d, (float)(2 * ((h >> 12) & 7) + 1));
+    const float delta = (h & 0x8000u) ? -0.125f : 0.125f;
+    const uint8_t *qs = b + 2 + 4 * p;
+    float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+    for (int l = 0; l < 4; l++) {
+        const uint64_t row = sepia_iq1s_grid[qs[l] | (((h >> (3 * l)) & 7) << 8)];
+        const uint32_t lo = plus1_bytes((uint32_t)row), hi = plus1_bytes((uint32_t)(row >> 32));
+        const float *xv = x.v + 8 * l;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            t0 = fmaf(grid_g_f(lo, j), xv[j], t0);
+            t1 = fmaf(grid_g_f(hi, j), xv[4 + j], t1);
+        }
+    }
+    return dl * fmaf(delta, x.s16[0] + x.s16[1], t0 + t1);
+}
+
 // ------------------------------------------------------------ generic
 __device__ __forceinline__ float dot_generic(int t, const uint8_t *b, int p, const XPart &x, int n_valid) {
     float y[32];
@@ -186,6 +252,8 @@ __device__ __forceinline__ float dot_part(const uint8_t *b, int p, const XPart &
     if constexpr (T == T_Q2_K) return dot_q2_k(b, p, x);
     else if constexpr (T == T_Q3_K) return dot_q3_k(b, p, x);
     else if constexpr (T == T_Q4_K) return dot_q4_k(b, p, x);
+    else if constexpr (T == T_IQ2_XXS) return dot_iq2_xxs(b, p, x);
+    else if constexpr (T == T_IQ1_S) return dot_iq1_s(b, p, x);
     else return dot_generic(T, b, p, x, n_valid);
 }
 
