@@ -164,7 +164,7 @@ __device__ __forceinline__ float dot_q4_k(const uint8_t *b, int p, const XPart &
     return fmaf(dl * (x.inv * 16.0f), s0 + s1, -ml * (x.s16[0] + x.s16[1]));
 }
 
-// ------------------------------------------------------------ IQ2_XXS / IQ1_S
+// ------------------------------------------------------------ IQ codebook formats
 // Codebook formats with unscaled activations: each grid byte v (0..255)
 // becomes the exact float 2^23 + v by one byte permute with the exponent
 // byte 0x4B, and one subtraction; signs flip the activation's sign bit. The
@@ -194,6 +194,54 @@ __device__ __forceinline__ float dot_iq2_xxs(const uint8_t *b, int p, const XPar
         for (int j = 0; j < 4; j++) {
             t0 = fmaf(grid_byte_f(lo, j), flip_if(xv[j], s, j), t0);
             t1 = fmaf(grid_byte_f(hi, j), flip_if(xv[4 + j], s, 4 + j), t1);
+        }
+    }
+    return db * (t0 + t1);
+}
+
+// gguf IQ2_XS: per 8 elements a 16-bit word (9-bit grid row, 7-bit sign
+// index); 4-bit scales per 16 elements.
+__device__ __forceinline__ float dot_iq2_xs(const uint8_t *b, int p, const XPart &x) {
+    const float d = cvt16<true>(rd16(b));
+    const int sc = b[66 + p];
+    const float db0 = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(sc & 15))), 0.25f);
+    const float db1 = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(sc >> 4))), 0.25f);
+    float t[2] = {0.f, 0.f};
+#pragma unroll
+    for (int l = 0; l < 4; l++) {
+        const uint32_t q = rd16(b + 2 + 2 * (4 * p + l));
+        const uint64_t row = sepia_iq2xs_grid[q & 511];
+        const uint32_t s = sepia_ksigns_iq2xs[q >> 9];
+        const uint32_t lo = (uint32_t)row, hi = (uint32_t)(row >> 32);
+        const float *xv = x.v + 8 * l;
+        float a = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            a = fmaf(grid_byte_f(lo, j), flip_if(xv[j], s, j), a);
+            a = fmaf(grid_byte_f(hi, j), flip_if(xv[4 + j], s, 4 + j), a);
+        }
+        t[l >> 1] += a;
+    }
+    return fmaf(db0, t[0], db1 * t[1]);
+}
+
+// gguf IQ3_XXS: per 8 elements two 4-byte grid rows and a sign index;
+// db = d * (0.5 + s) * 0.5.
+__device__ __forceinline__ float dot_iq3_xxs(const uint8_t *b, int p, const XPart &x) {
+    const float d = cvt16<true>(rd16(b));
+    const uint32_t a = rd32(b + 66 + 4 * p);
+    const float db = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(a >> 28))), 0.5f);
+    const uint8_t *qs = b + 2 + 8 * p;
+    float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+    for (int l = 0; l < 4; l++) {
+        const uint32_t s = sepia_ksigns_iq2xs[(a >> (7 * l)) & 127];
+        const uint32_t g1 = sepia_iq3xxs_grid[qs[2 * l]], g2 = sepia_iq3xxs_grid[qs[2 * l + 1]];
+        const float *xv = x.v + 8 * l;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            t0 = fmaf(grid_byte_f(g1, j), flip_if(xv[j], s, j), t0);
+            t1 = fmaf(grid_byte_f(g2, j), flip_if(xv[4 + j], s, 4 + j), t1);
         }
     }
     return db * (t0 + t1);
@@ -254,6 +302,8 @@ __device__ __forceinline__ float dot_part(const uint8_t *b, int p, const XPart &
     else if constexpr (T == T_Q4_K) return dot_q4_k(b, p, x);
     else if constexpr (T == T_IQ2_XXS) return dot_iq2_xxs(b, p, x);
     else if constexpr (T == T_IQ1_S) return dot_iq1_s(b, p, x);
+    else if constexpr (T == T_IQ2_XS) return dot_iq2_xs(b, p, x);
+    else if constexpr (T == T_IQ3_XXS) return dot_iq3_xxs(b, p, x);
     else return dot_generic(T, b, p, x, n_valid);
 }
 
