@@ -45,6 +45,7 @@ def parse():
     ap.add_argument("--no-graph", action="store_true", help="eager launches instead of one CUDA graph per layer")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--parity", action="store_true", help="check one step against the CPU oracle")
+    ap.add_argument("--only", default="", help="kernels workload: run only the lines whose name contains this")
     ap.add_argument("--workload", default="moe_layer", choices=["moe_layer", "kernels"],
                     help="moe_layer: the headline line (config 2); kernels: one line per BASELINE config-1/3/4 "
                          "kernel (device time, 1 GPU)")
@@ -248,23 +249,31 @@ def kernel_lines(args):
         nb = Q.row_bytes(t, cols) * rows
         return [synth.blocks_device(gen, t, rows * cols // Q.block_elems(t)) for _ in range(max(2, int(800e6 // nb)))]
 
-    g, u, d = mats(Q.Q2_K, 2048, 7168), mats(Q.Q2_K, 2048, 7168), mats(Q.Q2_K, 7168, 2048)
-    x = torch.randn(7168, device="cuda")
-    ga, ua, y = torch.empty(2048, device="cuda"), torch.empty(2048, device="cuda"), torch.empty(7168, device="cuda")
-    h = torch.empty(2048, device="cuda")
+    def want(name):
+        return args.only in name
 
-    def slab(i):
-        k = i % len(g)
-        ok(L.sepia_cuda_matvec_q(Q.Q2_K, g[k].data_ptr(), x.data_ptr(), ga.data_ptr(), 2048, 7168, 1, None))
-        ok(L.sepia_cuda_matvec_q(Q.Q2_K, u[k].data_ptr(), x.data_ptr(), ua.data_ptr(), 2048, 7168, 1, None))
-        ok(L.sepia_cuda_silu_mul(ga.data_ptr(), ua.data_ptr(), h.data_ptr(), 2048, None))
-        ok(L.sepia_cuda_matvec_q(Q.Q2_K, d[k].data_ptr(), h.data_ptr(), y.data_ptr(), 7168, 2048, 1, None))
-    emit("config1_q2k_swiglu_slab", 14516224, timeit(slab, 100), {"launches": 4})
-    del g, u, d
+    if want("config1_q2k_swiglu_slab"):
+        g, u, d = mats(Q.Q2_K, 2048, 7168), mats(Q.Q2_K, 2048, 7168), mats(Q.Q2_K, 7168, 2048)
+        x = torch.randn(7168, device="cuda")
+        ga, ua, y = torch.empty(2048, device="cuda"), torch.empty(2048, device="cuda"), torch.empty(7168, device="cuda")
+        h = torch.empty(2048, device="cuda")
+
+        def slab(i):
+            k = i % len(g)
+            ok(L.sepia_cuda_matvec_q(Q.Q2_K, g[k].data_ptr(), x.data_ptr(), ga.data_ptr(), 2048, 7168, 1, None))
+            ok(L.sepia_cuda_matvec_q(Q.Q2_K, u[k].data_ptr(), x.data_ptr(), ua.data_ptr(), 2048, 7168, 1, None))
+            ok(L.sepia_cuda_silu_mul(ga.data_ptr(), ua.data_ptr(), h.data_ptr(), 2048, None))
+            ok(L.sepia_cuda_matvec_q(Q.Q2_K, d[k].data_ptr(), h.data_ptr(), y.data_ptr(), 7168, 2048, 1, None))
+        emit("config1_q2k_swiglu_slab", 14516224, timeit(slab, 100), {"launches": 4})
+        del g, u, d
     for t, name in ((Q.IQ1_S, "iq1_s"), (Q.IQ2_XXS, "iq2_xxs")):
         for rows in (2048, 7168, 16384):
+            if not any(want(f"config3_{name}_{rows}x7168_b{b}") for b in (1, 4, 16)):
+                continue
             ws = mats(t, rows, 7168)
             for b in (1, 4, 16):
+                if not want(f"config3_{name}_{rows}x7168_b{b}"):
+                    continue
                 xb = torch.randn(b, 7168, device="cuda")
                 yb = torch.empty(b, rows, device="cuda")
                 fn = lambda i: ok(L.sepia_cuda_matvec_q(t, ws[i % len(ws)].data_ptr(), xb.data_ptr(), yb.data_ptr(),
@@ -273,6 +282,8 @@ def kernel_lines(args):
                 emit(f"config3_{name}_{rows}x7168_b{b}", nbytes, timeit(fn, 50), {"rows": rows, "batch": b})
             del ws
     for ctx, window in ((32768, 0), (4096, 4096)):
+        if not want(f"config4_attn_ctx{ctx}_{'global' if not window else 'window'}"):
+            continue
         H, Hkv, Dh, E = 64, 8, 128, 256
         kvd = Hkv * Dh
         k = torch.randn(ctx, kvd, device="cuda").half()

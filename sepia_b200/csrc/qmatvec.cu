@@ -212,6 +212,286 @@ __global__ void k_dequant(int t, const uint8_t *raw, float *out, int64_t n) {
     for (int i = 0; i < nvalid; i++) out[first + i] = y[i];
 }
 
+// ------------------------------------------------------- batched IQ path
+// n_vec > 1 for the IQ grid formats. k_matvec decodes every weight once per
+// vector; here a lane decodes its 32-weight part once into exact floats
+// (grid byte with the sign folded into the weight instead of the
+// activation: the product is bit-identical) and reuses it for up to kIqVB
+// vectors staged in shared memory. Per vector the part's fp32 accumulation
+// order is the one of dot_iq2_xxs / dot_iq2_xs / dot_iq3_xxs / dot_iq1_s, so
+// each row's value equals the n_vec = 1 result of that vector.
+//
+// Shared layout: x[v][in_dim] with the 16-byte chunk c of part P stored at
+// chunk c ^ (P & 7) (8 consecutive parts -- one quarter-warp of 16-byte
+// loads -- hit distinct banks), then the IQ1_S part sums S[v][P] =
+// sum(x[0..15]) + sum(x[16..31]) in dot_iq1_s's order.
+// Grid (vector groups, row blocks): the groups of one row block are
+// adjacent block indices, so the later groups read the rows from L2.
+constexpr int kIqVB = 8;
+constexpr int kIqWarps = 16;
+constexpr int kIqRowsPerWarp = 4;
+constexpr int kIqPL = 4;    // parts a lane loads ahead
+
+__device__ __forceinline__ uint32_t g16(const uint8_t *p) { return __ldg(reinterpret_cast<const unsigned short *>(p)); }
+__device__ __forceinline__ uint32_t g32(const uint8_t *p) { return g16(p) | (g16(p + 2) << 16); }
+__device__ __forceinline__ float g_half(const uint8_t *p) { return __half2float(__ushort_as_half((unsigned short)g16(p))); }
+
+// Raw bytes of part p (0..7) of block b, loaded before any decode so a
+// lane's loads for a whole row are in flight together.
+struct IqRaw { uint32_t d, a, b, c; };
+
+template <int T>
+__device__ __forceinline__ IqRaw iq_load(const uint8_t *b, int p) {
+    IqRaw r;
+    r.d = g16(b);
+    if constexpr (T == T_IQ2_XXS) {
+        r.a = g32(b + 2 + 8 * p); r.b = g32(b + 6 + 8 * p); r.c = 0;
+    } else if constexpr (T == T_IQ2_XS) {
+        r.a = g32(b + 2 + 8 * p); r.b = g32(b + 6 + 8 * p); r.c = g16(b + 66 + (p & ~1)) >> (8 * (p & 1)) & 255;
+    } else if constexpr (T == T_IQ3_XXS) {
+        r.a = g32(b + 66 + 4 * p); r.b = g32(b + 2 + 8 * p); r.c = g32(b + 6 + 8 * p);
+    } else {   // T_IQ1_S
+        r.a = g16(b + 34 + 2 * p); r.b = g32(b + 2 + 4 * p); r.c = 0;
+    }
+    return r;
+}
+
+// 32 weights w of a loaded part (exact floats) and the scale terms the
+// combine needs (sa, sb: see iq_combine).
+template <int T>
+__device__ __forceinline__ void iq_decode(const IqRaw &r, float (&w)[32], float &sa, float &sb) {
+    const float d = __half2float(__ushort_as_half((unsigned short)r.d));
+    if constexpr (T == T_IQ2_XXS) {
+        const uint32_t idx = r.a, sg = r.b;
+        sa = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(sg >> 28))), 0.25f);
+        sb = 0.f;
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const uint64_t row = sepia_iq2xxs_grid[(idx >> (8 * l)) & 255];
+            const uint32_t s = sepia_ksigns_iq2xs[(sg >> (7 * l)) & 127];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                w[8 * l + j] = flip_if(grid_byte_f((uint32_t)row, j), s, j);
+                w[8 * l + 4 + j] = flip_if(grid_byte_f((uint32_t)(row >> 32), j), s, 4 + j);
+            }
+        }
+    } else if constexpr (T == T_IQ2_XS) {
+        const uint32_t sc = r.c;
+        sa = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(sc & 15))), 0.25f);
+        sb = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(sc >> 4))), 0.25f);
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const uint32_t q = ((l < 2 ? r.a : r.b) >> (16 * (l & 1))) & 0xFFFFu;
+            const uint64_t row = sepia_iq2xs_grid[q & 511];
+            const uint32_t s = sepia_ksigns_iq2xs[q >> 9];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                w[8 * l + j] = flip_if(grid_byte_f((uint32_t)row, j), s, j);
+                w[8 * l + 4 + j] = flip_if(grid_byte_f((uint32_t)(row >> 32), j), s, 4 + j);
+            }
+        }
+    } else if constexpr (T == T_IQ3_XXS) {
+        const uint32_t a = r.a;
+        sa = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(a >> 28))), 0.5f);
+        sb = 0.f;
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const uint32_t qq = (l < 2) ? r.b : r.c;
+            const uint32_t s = sepia_ksigns_iq2xs[(a >> (7 * l)) & 127];
+            const uint32_t g1 = sepia_iq3xxs_grid[(qq >> (16 * (l & 1))) & 255];
+            const uint32_t g2 = sepia_iq3xxs_grid[(qq >> (16 * (l & 1) + 8)) & 255];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                w[8 * l + j] = flip_if(grid_byte_f(g1, j), s, j);
+                w[8 * l + 4 + j] = flip_if(grid_byte_f(g2, j), s, 4 + j);
+            }
+        }
+    } else {   // T_IQ1_S
+        const uint32_t h = r.a, qs = r.b;
+        sa = __fmul_rn(d, (float)(2 * ((h >> 12) & 7) + 1));
+        sb = (h & 0x8000u) ? -0.125f : 0.125f;
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const uint64_t row = sepia_iq1s_grid[((qs >> (8 * l)) & 255) | (((h >> (3 * l)) & 7) << 8)];
+            const uint32_t lo = plus1_bytes((uint32_t)row), hi = plus1_bytes((uint32_t)(row >> 32));
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                w[8 * l + j] = grid_g_f(lo, j);
+                w[8 * l + 4 + j] = grid_g_f(hi, j);
+            }
+        }
+    }
+}
+
+// Dot of decoded part w with one vector's part (swizzled chunks at xs).
+template <int T>
+__device__ __forceinline__ float iq_combine(const float (&w)[32], const float *xs, int sw, float sa, float sb,
+                                            float S) {
+    float x[32];
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+        const float4 f = *reinterpret_cast<const float4 *>(xs + 4 * (c ^ sw));
+        x[4 * c] = f.x; x[4 * c + 1] = f.y; x[4 * c + 2] = f.z; x[4 * c + 3] = f.w;
+    }
+    if constexpr (T == T_IQ2_XS) {
+        float t[2] = {0.f, 0.f};
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            float a = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                a = fmaf(w[8 * l + j], x[8 * l + j], a);
+                a = fmaf(w[8 * l + 4 + j], x[8 * l + 4 + j], a);
+            }
+            t[l >> 1] += a;
+        }
+        return fmaf(sa, t[0], sb * t[1]);
+    } else {
+        float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+        for (int l = 0; l < 4; l++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                t0 = fmaf(w[8 * l + j], x[8 * l + j], t0);
+                t1 = fmaf(w[8 * l + 4 + j], x[8 * l + 4 + j], t1);
+            }
+        if constexpr (T == T_IQ1_S) return sa * fmaf(sb, S, t0 + t1);
+        else return sa * (t0 + t1);
+    }
+}
+
+struct IqbParams {
+    const uint8_t *w;
+    int64_t row_bytes, out_dim, in_dim;
+    const float *x;
+    float *y;
+    int n_vec, vb;   // vectors in all, vectors per group (<= kIqVB)
+    int rpw;         // rows per warp (<= kIqRowsPerWarp)
+};
+
+template <int T>
+__global__ void __launch_bounds__(kIqWarps * 32) k_matvec_iqb(const IqbParams P) {
+    extern __shared__ __align__(16) float xsm[];
+    const int nparts = (int)(P.in_dim / 32);
+    float *ssum = xsm + (size_t)P.vb * P.in_dim;
+    const int v0 = blockIdx.x * P.vb;
+    const int nv = min(P.vb, P.n_vec - v0);
+    const int64_t in4 = P.in_dim / 4;
+    for (int64_t i = threadIdx.x; i < nv * in4; i += blockDim.x) {
+        const int v = (int)(i / in4);
+        const int64_t c4 = i - v * in4;
+        const int64_t part = c4 >> 3;
+        const int c = (int)(c4 & 7);
+        const float4 f = __ldg(reinterpret_cast<const float4 *>(P.x + (int64_t)(v0 + v) * P.in_dim) + c4);
+        *reinterpret_cast<float4 *>(xsm + (size_t)v * P.in_dim + part * 32 + 4 * (c ^ (int)(part & 7))) = f;
+    }
+    __syncthreads();
+    if constexpr (T == T_IQ1_S) {
+        for (int i = threadIdx.x; i < nv * nparts; i += blockDim.x) {
+            const int v = i / nparts, part = i - v * nparts;
+            const float *xp = xsm + (size_t)v * P.in_dim + part * 32;
+            float a = 0.f, b = 0.f;
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                a += xp[4 * ((k >> 2) ^ (part & 7)) + (k & 3)];
+                b += xp[4 * (((k + 16) >> 2) ^ (part & 7)) + (k & 3)];
+            }
+            ssum[i] = a + b;
+        }
+        __syncthreads();
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bb = fmt_block_bytes(T);
+    const int64_t rbase = (int64_t)blockIdx.y * (kIqWarps * P.rpw);
+    for (int rr = 0; rr < P.rpw; rr++) {
+        const int64_t row = rbase + (int64_t)rr * kIqWarps + warp;
+        if (row >= P.out_dim) break;
+        const uint8_t *wr = P.w + row * P.row_bytes;
+        double acc[kIqVB];
+#pragma unroll
+        for (int v = 0; v < kIqVB; v++) acc[v] = 0.0;
+        for (int pc = lane; pc < nparts; pc += 32 * kIqPL) {
+            IqRaw raw[kIqPL];
+#pragma unroll
+            for (int i = 0; i < kIqPL; i++) {
+                const int part = pc + 32 * i;
+                if (part < nparts) raw[i] = iq_load<T>(wr + (int64_t)(part >> 3) * bb, part & 7);
+            }
+#pragma unroll
+            for (int i = 0; i < kIqPL; i++) {
+                const int part = pc + 32 * i;
+                if (part < nparts) {
+                    float wv[32], sa, sb;
+                    iq_decode<T>(raw[i], wv, sa, sb);
+#pragma unroll
+                    for (int v = 0; v < kIqVB; v++) {
+                        if (v < nv) {
+                            const float S = (T == T_IQ1_S) ? ssum[v * nparts + part] : 0.f;
+                            acc[v] += (double)iq_combine<T>(wv, xsm + (size_t)v * P.in_dim + part * 32, part & 7,
+                                                            sa, sb, S);
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int v = 0; v < kIqVB; v++) {
+            if (v < nv) {
+                double a = acc[v];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                if (lane == 0) P.y[(int64_t)(v0 + v) * P.out_dim + row] = (float)a;
+            }
+        }
+    }
+}
+
+static bool iqb_type(int t) { return t == T_IQ2_XXS || t == T_IQ2_XS || t == T_IQ3_XXS || t == T_IQ1_S; }
+
+static int launch_matvec_iqb(int t, const void *w, const float *x, float *y, int64_t out_dim, int64_t in_dim,
+                             int64_t rb, int64_t n_vec, cudaStream_t st) {
+    DevInfo &di = dev_info();
+    const int64_t nparts = in_dim / 32;
+    const int64_t per_vec = 4 * (in_dim + (t == T_IQ1_S ? nparts : 0));   // x (+ IQ1_S part sums)
+    const int vb = (int)std::min<int64_t>(kIqVB, std::min<int64_t>(n_vec, di.smem_optin / per_vec));
+    const size_t smem = (size_t)vb * per_vec;
+    const void *fn = nullptr;
+    switch (t) {
+    case T_IQ2_XXS: fn = (const void *)k_matvec_iqb<T_IQ2_XXS>; break;
+    case T_IQ2_XS: fn = (const void *)k_matvec_iqb<T_IQ2_XS>; break;
+    case T_IQ3_XXS: fn = (const void *)k_matvec_iqb<T_IQ3_XXS>; break;
+    default: fn = (const void *)k_matvec_iqb<T_IQ1_S>; break;
+    }
+    if (!ensure_smem(fn, (int)smem)) return 0;
+    IqbParams P;
+    P.w = reinterpret_cast<const uint8_t *>(w);
+    P.row_bytes = rb; P.out_dim = out_dim; P.in_dim = in_dim;
+    P.x = x; P.y = y; P.n_vec = (int)n_vec; P.vb = vb;
+    // rows per warp: as many as keep >= 2 CTAs per SM in the grid (each CTA
+    // stages its vectors once, so fewer, longer CTAs save L2 reads)
+    const int64_t groups = (n_vec + vb - 1) / vb;
+    P.rpw = (int)std::max<int64_t>(1, std::min<int64_t>(kIqRowsPerWarp,
+                                                        out_dim * groups / ((int64_t)kIqWarps * 2 * di.sm_count)));
+    const int64_t rows_per_cta = (int64_t)kIqWarps * P.rpw;
+    dim3 grid((unsigned)groups, (unsigned)((out_dim + rows_per_cta - 1) / rows_per_cta));
+    switch (t) {
+    case T_IQ2_XXS: k_matvec_iqb<T_IQ2_XXS><<<grid, kIqWarps * 32, smem, st>>>(P); break;
+    case T_IQ2_XS: k_matvec_iqb<T_IQ2_XS><<<grid, kIqWarps * 32, smem, st>>>(P); break;
+    case T_IQ3_XXS: k_matvec_iqb<T_IQ3_XXS><<<grid, kIqWarps * 32, smem, st>>>(P); break;
+    default: k_matvec_iqb<T_IQ1_S><<<grid, kIqWarps * 32, smem, st>>>(P); break;
+    }
+    return check(cudaGetLastError(), "matvec_q (batched IQ) launch");
+}
+
+// Can this call take the batched IQ path? Several vectors, whole
+// superblocks, 2-byte aligned weights and rows, 16-byte aligned x, and at
+// least one vector's x (plus part sums) fits in shared memory.
+static bool iqb_ok(int t, const void *w, const float *x, int64_t in_dim, int64_t rb, int64_t n_vec) {
+    return iqb_type(t) && n_vec > 1 && in_dim % kQK == 0 && rb % 2 == 0 &&
+           (reinterpret_cast<uintptr_t>(w) & 1) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+           4 * (in_dim + in_dim / 32) <= (int64_t)dev_info().smem_optin && (n_vec + kIqVB - 1) / kIqVB < 65536;
+}
+
 // ----------------------------------------------------------------- host side
 typedef void (*MvKernel)(const MvParams);
 
@@ -250,6 +530,7 @@ int launch_matvec_q(int t, const void *w, const float *x, float *y, int64_t out_
     if (!w || !x || !y) return fail("matvec_q: null pointer");
     // K-quants with aligned rows run on the integer tensor cores
     if (engine_ok(t, w, x, in_dim, rb, n_vec)) return launch_matvec_engine(t, w, x, y, out_dim, in_dim, rb, st);
+    if (iqb_ok(t, w, x, in_dim, rb, n_vec)) return launch_matvec_iqb(t, w, x, y, out_dim, in_dim, rb, n_vec, st);
     DevInfo &di = dev_info();
     const int nsb = (int)((in_dim + kQK - 1) / kQK);
     int c = 1, nwc = (nsb + 3) / 4;

@@ -98,20 +98,27 @@ def test_matvec_unaligned_base(torch_cuda, oracle, t, off):
     assert oracle.rel_err(got, want) <= TOL
 
 
-@pytest.mark.parametrize("t", [Q.IQ1_S, Q.IQ2_XXS, Q.Q2_K])
-@pytest.mark.parametrize("n_vec", [4, 16])
+@pytest.mark.parametrize("t", [Q.IQ1_S, Q.IQ2_XXS, Q.IQ2_XS, Q.IQ3_XXS, Q.Q2_K])
+@pytest.mark.parametrize("n_vec", [2, 4, 5, 16])
 def test_matvec_batched(torch_cuda, oracle, t, n_vec):
-    """BASELINE configuration 3 batches (smaller row count)."""
+    """BASELINE configuration 3 batches (smaller, ragged row count; n_vec 5
+    leaves a partial vector group). Every vector's row values also equal
+    the batch-1 call's bit for bit: the batched path keeps the per-part
+    accumulation order."""
     from sepia_b200 import ops
     torch = torch_cuda
     rng = np.random.default_rng(n_vec + t)
-    out_dim, in_dim = 96, 7168
+    out_dim, in_dim = 100, 7168
     w = synth.matrix_host(rng, t, out_dim, in_dim)
     X = rng.standard_normal((n_vec, in_dim)).astype(np.float32)
-    got = ops.matvec_q(t, _dev(torch, w), _dev(torch, X), out_dim, in_dim).cpu().numpy()
+    wd = _dev(torch, w)
+    got = ops.matvec_q(t, wd, _dev(torch, X), out_dim, in_dim).cpu().numpy()
     for v in range(n_vec):
         want = oracle.qlinear(t, w, out_dim, in_dim, X[v])
         assert oracle.rel_err(got[v], want) <= TOL
+        if t != Q.Q2_K:
+            one = ops.matvec_q(t, wd, _dev(torch, np.ascontiguousarray(X[v])), out_dim, in_dim).cpu().numpy()
+            assert np.array_equal(one, got[v])
 
 
 @pytest.mark.parametrize("rows", [2048, 7168, 16384])
