@@ -157,12 +157,50 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
 #pragma unroll
                 for (int j = 0; j < kHPT; j++) dd[j] = 0.0;
                 const KV *kr = sk + r * ldk;
-                for (int d = 0; d < Dh; d++) {
-                    const double kd = kv_d<KV>(kr + d);
+                if constexpr (VEC) {
+                    // one 16-byte shared load per granule: rows sit 16 bytes
+                    // past a multiple of 128, so 8 consecutive rows (one
+                    // quarter-warp phase) cover all 32 banks without conflict.
+                    // Accumulation order is unchanged (d ascending).
+                    constexpr int EPG = 16 / (int)sizeof(KV);
+                    for (int d0 = 0; d0 < Dh; d0 += EPG) {
+                        const uint4 raw = *reinterpret_cast<const uint4 *>(kr + d0);
+                        double kd[EPG];
+                        if constexpr (sizeof(KV) == 2) {
+                            const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
 #pragma unroll
-                    for (int j = 0; j < kHPT; j++) {
-                        const int g = g0 + gstep * j;
-                        if (g < G) dd[j] = fma(sq[g * ldq + d], kd, dd[j]);
+                            for (int e = 0; e < 4; e++) {
+                                const float2 f = __half22float2(h2[e]);
+                                kd[2 * e] = (double)f.x;
+                                kd[2 * e + 1] = (double)f.y;
+                            }
+                        } else {
+                            const float *f4 = reinterpret_cast<const float *>(&raw);
+#pragma unroll
+                            for (int e = 0; e < EPG; e++) kd[e] = (double)f4[e];
+                        }
+#pragma unroll
+                        for (int j = 0; j < kHPT; j++) {
+                            const int g = g0 + gstep * j;
+                            if (g < G) {
+                                const double *qg = sq + g * ldq + d0;
+#pragma unroll
+                                for (int e = 0; e < EPG; e += 2) {
+                                    const double2 q2 = *reinterpret_cast<const double2 *>(qg + e);
+                                    dd[j] = fma(q2.x, kd[e], dd[j]);
+                                    dd[j] = fma(q2.y, kd[e + 1], dd[j]);
+                                }
+                            }
+                        }
+                    }
+                } else {
+                    for (int d = 0; d < Dh; d++) {
+                        const double kd = kv_d<KV>(kr + d);
+#pragma unroll
+                        for (int j = 0; j < kHPT; j++) {
+                            const int g = g0 + gstep * j;
+                            if (g < G) dd[j] = fma(sq[g * ldq + d], kd, dd[j]);
+                        }
                     }
                 }
 #pragma unroll
@@ -210,14 +248,35 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
                 const int g = warp + kAttnWarps * a;
                 pr[a] = (g < G) ? (double)ss[g * kAttnKT + r] : 0.0;
             }
+            if constexpr (VEC) {
+                // lane owns dims 4*lane .. 4*lane+3: one 8- or 16-byte load
+                if (4 * lane < Dh) {
+                    double vd[4];
+                    if constexpr (sizeof(KV) == 2) {
+                        const uint2 raw = *reinterpret_cast<const uint2 *>(sv + r * ldk + 4 * lane);
+                        const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+                        const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+                        vd[0] = f0.x; vd[1] = f0.y; vd[2] = f1.x; vd[3] = f1.y;
+                    } else {
+                        const float4 f = *reinterpret_cast<const float4 *>(sv + r * ldk + 4 * lane);
+                        vd[0] = f.x; vd[1] = f.y; vd[2] = f.z; vd[3] = f.w;
+                    }
 #pragma unroll
-            for (int j = 0; j < kAttnMaxDh / 32; j++) {
-                const int d = lane + 32 * j;
-                if (d < Dh) {
-                    const double vd = kv_d<KV>(sv + r * ldk + d);
+                    for (int j = 0; j < 4; j++)
 #pragma unroll
-                    for (int a = 0; a < kHPW; a++)
-                        if (warp + kAttnWarps * a < G) acc[a][j] = fma(pr[a], vd, acc[a][j]);
+                        for (int a = 0; a < kHPW; a++)
+                            if (warp + kAttnWarps * a < G) acc[a][j] = fma(pr[a], vd[j], acc[a][j]);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < kAttnMaxDh / 32; j++) {
+                    const int d = lane + 32 * j;
+                    if (d < Dh) {
+                        const double vd = kv_d<KV>(sv + r * ldk + d);
+#pragma unroll
+                        for (int a = 0; a < kHPW; a++)
+                            if (warp + kAttnWarps * a < G) acc[a][j] = fma(pr[a], vd, acc[a][j]);
+                    }
                 }
             }
         }
@@ -233,7 +292,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
             if (lane == 0) { pp[0] = sml[2 * g]; pp[1] = sml[2 * g + 1]; }
 #pragma unroll
             for (int j = 0; j < kAttnMaxDh / 32; j++) {
-                const int d = lane + 32 * j;
+                const int d = VEC ? 4 * lane + j : lane + 32 * j;
                 if (d < Dh) pp[2 + d] = acc[a][j];
             }
         }
