@@ -161,8 +161,17 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
                     // one 16-byte shared load per granule: rows sit 16 bytes
                     // past a multiple of 128, so 8 consecutive rows (one
                     // quarter-warp phase) cover all 32 banks without conflict.
-                    // Accumulation order is unchanged (d ascending).
+                    // Each dot runs as 4 interleaved fp64 partial sums
+                    // (element pairs 2c, 2c+1 of every 8 go to chain c),
+                    // added pairwise at the end: 4x shorter dependent FMA
+                    // chains; the fp64 result moves by ~1e-16 relative,
+                    // far inside the float rounding that follows.
                     constexpr int EPG = 16 / (int)sizeof(KV);
+                    double dc[kHPT][4];
+#pragma unroll
+                    for (int j = 0; j < kHPT; j++)
+#pragma unroll
+                        for (int c = 0; c < 4; c++) dc[j][c] = 0.0;
                     for (int d0 = 0; d0 < Dh; d0 += EPG) {
                         const uint4 raw = *reinterpret_cast<const uint4 *>(kr + d0);
                         double kd[EPG];
@@ -187,12 +196,15 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
 #pragma unroll
                                 for (int e = 0; e < EPG; e += 2) {
                                     const double2 q2 = *reinterpret_cast<const double2 *>(qg + e);
-                                    dd[j] = fma(q2.x, kd[e], dd[j]);
-                                    dd[j] = fma(q2.y, kd[e + 1], dd[j]);
+                                    double &a = dc[j][(e >> 1) & 3];
+                                    a = fma(q2.x, kd[e], a);
+                                    a = fma(q2.y, kd[e + 1], a);
                                 }
                             }
                         }
                     }
+#pragma unroll
+                    for (int j = 0; j < kHPT; j++) dd[j] = (dc[j][0] + dc[j][1]) + (dc[j][2] + dc[j][3]);
                 } else {
                     for (int d = 0; d < Dh; d++) {
                         const double kd = kv_d<KV>(kr + d);
@@ -241,31 +253,40 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
         }
         __syncwarp();
         // ---- P.V: each v element is converted once for all of the warp's heads ----
+        // VEC: a tile's (<= 64) products are summed in fp32 (relative error
+        // ~64 * 2^-24 of the tile's magnitude) and added to the fp64 running
+        // accumulator once per tile, so the long chains stay fp64.
+        float tacc[kHPW][4];
+#pragma unroll
+        for (int a = 0; a < kHPW; a++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) tacc[a][j] = 0.0f;
         for (int r = 0; r < nt; r++) {
             double pr[kHPW];
+            float pf[kHPW];
 #pragma unroll
             for (int a = 0; a < kHPW; a++) {
                 const int g = warp + kAttnWarps * a;
-                pr[a] = (g < G) ? (double)ss[g * kAttnKT + r] : 0.0;
+                pf[a] = (g < G) ? ss[g * kAttnKT + r] : 0.0f;
+                pr[a] = (double)pf[a];
             }
             if constexpr (VEC) {
                 // lane owns dims 4*lane .. 4*lane+3: one 8- or 16-byte load
                 if (4 * lane < Dh) {
-                    double vd[4];
+                    float vf[4];
                     if constexpr (sizeof(KV) == 2) {
                         const uint2 raw = *reinterpret_cast<const uint2 *>(sv + r * ldk + 4 * lane);
                         const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
                         const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
-                        vd[0] = f0.x; vd[1] = f0.y; vd[2] = f1.x; vd[3] = f1.y;
+                        vf[0] = f0.x; vf[1] = f0.y; vf[2] = f1.x; vf[3] = f1.y;
                     } else {
                         const float4 f = *reinterpret_cast<const float4 *>(sv + r * ldk + 4 * lane);
-                        vd[0] = f.x; vd[1] = f.y; vd[2] = f.z; vd[3] = f.w;
+                        vf[0] = f.x; vf[1] = f.y; vf[2] = f.z; vf[3] = f.w;
                     }
 #pragma unroll
                     for (int j = 0; j < 4; j++)
 #pragma unroll
-                        for (int a = 0; a < kHPW; a++)
-                            if (warp + kAttnWarps * a < G) acc[a][j] = fma(pr[a], vd[j], acc[a][j]);
+                        for (int a = 0; a < kHPW; a++) tacc[a][j] = fmaf(pf[a], vf[j], tacc[a][j]);
                 }
             } else {
 #pragma unroll
@@ -279,6 +300,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
                     }
                 }
             }
+        }
+        if constexpr (VEC) {
+#pragma unroll
+            for (int a = 0; a < kHPW; a++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[a][j] += (double)tacc[a][j];
         }
         __syncthreads();
     }
