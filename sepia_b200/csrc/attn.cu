@@ -365,19 +365,31 @@ __global__ void k_attn_combine(const double *part, float *out, int64_t TH, int S
     const int64_t th = blockIdx.x;
     if (th >= TH) return;
     __shared__ double s_w[kAttnMaxSplits];
-    __shared__ double s_L;
+    __shared__ double s_M, s_L;
     const double *pp = part + th * S * (Dh + 2);
-    double M = -INFINITY;
-    for (int s = 0; s < S; s++) M = fmax(M, pp[s * (Dh + 2)]);
+    const int lane = threadIdx.x & 31;
+    // M and L by warp 0: lane-strided loads, then a fixed shuffle tree
+    // (deterministic; L's fp64 order differs from a serial sum by ~1e-16)
+    if (threadIdx.x < 32) {
+        double M = -INFINITY;
+        for (int s = lane; s < S; s += 32) M = fmax(M, pp[s * (Dh + 2)]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmax(M, __shfl_xor_sync(0xffffffffu, M, o));
+        if (lane == 0) s_M = M;
+    }
+    __syncthreads();
+    const double M = s_M;
     for (int s = threadIdx.x; s < S; s += blockDim.x) {
         const double m = pp[s * (Dh + 2)];
         s_w[s] = (m != -INFINITY) ? exp(m - M) : 0.0;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < 32) {
         double L = 0.0;
-        for (int s = 0; s < S; s++) L += pp[s * (Dh + 2) + 1] * s_w[s];
-        s_L = L;
+        for (int s = lane; s < S; s += 32) L += pp[s * (Dh + 2) + 1] * s_w[s];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        if (lane == 0) s_L = L;
     }
     __syncthreads();
     const double L = s_L;
