@@ -5,11 +5,15 @@ Inkling shape decoding one token (router f32 [258 x 7168] + sigmoid top-6 of
 experts), weights resident in HBM, experts sharded over the GPUs.
 
 A step is one token through one layer. Steps rotate over --layers distinct
-layer instances (default 4, 4 x 152.6 MB touched per rotation > 126 MB L2)
-and over hidden states seeds 1..64, so weights are never L2-resident.
+layer instances (default 4, 4 x 152.6 MB touched per rotation > 126 MB L2),
+so weights are never L2-resident. Each instance is replayed as one CUDA
+graph holding its own resident hidden state (instance l: seed l+1), so each
+instance selects the same 6 experts on every replay; the eager and e2e paths
+rotate over hidden states of seeds 1..64.
 
 value  = whole-job quantized-matvec HBM throughput: algorithmic bytes of
-         the steps (152.6 MB/token) / device time (max over ranks).
+         the steps (152.6 MB/token: router + 6 routed + 2 shared experts +
+         activations) / device time (max over ranks).
 e2e    = the same through the reference-facing C ABI (include/sepia_gpu.h:
          sepia_gpu_begin / sepia_gpu_moe_layer / sepia_gpu_end) with host
          buffers: x uploaded and the layer output read back every step.
@@ -114,41 +118,73 @@ class Clocks:
 
 
 # ------------------------------------------------------------------- CPU
-def cpu_token_seconds(shape, budget_s=12.0):
-    """Time the CPU oracle (a port of the reference's qlinear loop; the
-    reference has no Q2_K/Q3_K) on one token of the layer: router linear +
-    6 routed SwiGLU experts + 2 shared, all host threads. Returns
-    (seconds per token, threads, sample description)."""
-    import numpy as np
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+class CpuLayer:
+    """Host copy of one config-2 layer for the CPU baseline: the f32 router,
+    6 distinct routed experts (the ones a token selects) and 2 shared."""
+
+    def __init__(self, shape, seed=11):
+        import numpy as np
+        from sepia_b200 import synth
+        s = shape
+        rng = np.random.default_rng(seed)
+        self.s = s
+        self.routed = [tuple(synth.matrix_host(rng, t, r, c) for t, r, c in [
+            (s.gate_type, s.ff, s.hidden), (s.up_type, s.ff, s.hidden), (s.down_type, s.hidden, s.ff)])
+            for _ in range(s.topk)]
+        self.shared = [tuple(synth.matrix_host(rng, t, r, c) for t, r, c in [
+            (s.sh_gate_type, s.ff, s.hidden), (s.sh_up_type, s.ff, s.hidden), (s.sh_down_type, s.hidden, s.ff)])
+            for _ in range(s.n_shared)]
+        self.rw = (rng.standard_normal((s.n_routed + s.n_shared, s.hidden)) * 0.02).astype(np.float32)
+
+    def token(self, x, n):
+        """Router matvec + 6 routed + 2 shared SwiGLU experts, n threads (the
+        oracle port of the reference's qlinear loop: the reference itself has
+        no Q2_K/Q3_K)."""
+        from oracle import oracle as O
+        s = self.s
+        O.linear(self.rw, x, nthreads=n)
+        for g, u, d in self.routed:
+            O.expert_swiglu(s.gate_type, g, s.up_type, u, s.down_type, d, s.hidden, s.ff, x, nthreads=n)
+        for g, u, d in self.shared:
+            O.expert_swiglu(s.sh_gate_type, g, s.sh_up_type, u, s.sh_down_type, d, s.hidden, s.ff, x, 0.5,
+                            nthreads=n)
+
+
+def cpu_token_seconds(shape, budget_s=10.0):
+    """Time the CPU baseline on tokens of the layer, all host threads and
+    then one thread (the reference's own loop is single-threaded). Returns
+    (seconds per token at n threads, n, sample description, seconds per
+    token at 1 thread)."""
     from oracle import oracle as O
     from sepia_b200 import synth
     O.build()
     n = O.nproc()
-    rng = np.random.default_rng(11)
-    s = shape
-    g = synth.matrix_host(rng, s.gate_type, s.ff, s.hidden)
-    u = synth.matrix_host(rng, s.up_type, s.ff, s.hidden)
-    d = synth.matrix_host(rng, s.down_type, s.hidden, s.ff)
-    sg = synth.matrix_host(rng, s.sh_gate_type, s.ff, s.hidden)
-    su = synth.matrix_host(rng, s.sh_up_type, s.ff, s.hidden)
-    sd = synth.matrix_host(rng, s.sh_down_type, s.hidden, s.ff)
-    rw = (rng.standard_normal((s.n_routed + s.n_shared, s.hidden)) * 0.02).astype(np.float32)
-    x = synth.hidden_state(1, s.hidden)
-    reps = 0
-    t_tot = 0.0
-    while True:
-        t0 = time.perf_counter()
-        O.linear(rw, x, nthreads=n)
-        for _ in range(s.topk):
-            O.expert_swiglu(s.gate_type, g, s.up_type, u, s.down_type, d, s.hidden, s.ff, x, nthreads=n)
-        for _ in range(s.n_shared):
-            O.expert_swiglu(s.sh_gate_type, sg, s.sh_up_type, su, s.sh_down_type, sd, s.hidden, s.ff, x, 0.5,
-                            nthreads=n)
-        t_tot += time.perf_counter() - t0
-        reps += 1
-        if t_tot > budget_s or reps >= 50:
-            break
-    return t_tot / reps, n, f"{reps} token(s) of config 2 (router + 6 routed + 2 shared SwiGLU) on {n} threads"
+    C_ = CpuLayer(shape)
+
+    def timed(threads, budget, max_reps):
+        reps, t_tot = 0, 0.0
+        while True:
+            x = synth.hidden_state(1 + reps % 64, shape.hidden)
+            t0 = time.perf_counter()
+            C_.token(x, threads)
+            t_tot += time.perf_counter() - t0
+            reps += 1
+            if t_tot > budget or reps >= max_reps:
+                return t_tot / reps, reps
+    sec_n, reps_n = timed(n, budget_s, 50)
+    sec_1, reps_1 = timed(1, budget_s, 3)
+    return (sec_n, n, f"{reps_n} token(s) of config 2 (router + 6 distinct routed + 2 shared SwiGLU) on {n} "
+                      f"threads; {reps_1} token(s) on 1 thread", sec_1)
 
 
 def run_reference(args):
@@ -156,28 +192,16 @@ def run_reference(args):
     if rank != 0:
         return
     from sepia_b200.synth import MoeShape
-    shape = MoeShape()
-    import numpy as np
     from oracle import oracle as O
     from sepia_b200 import synth
+    shape = MoeShape()
     O.build()
     n = O.nproc()
     s = shape
-    rng = np.random.default_rng(11)
-    mats = [synth.matrix_host(rng, t, r, c) for t, r, c in [
-        (s.gate_type, s.ff, s.hidden), (s.up_type, s.ff, s.hidden), (s.down_type, s.hidden, s.ff),
-        (s.sh_gate_type, s.ff, s.hidden), (s.sh_up_type, s.ff, s.hidden), (s.sh_down_type, s.hidden, s.ff)]]
-    rw = (rng.standard_normal((s.n_routed + s.n_shared, s.hidden)) * 0.02).astype(np.float32)
+    C_ = CpuLayer(shape)
 
     def step(i):
-        x = synth.hidden_state(1 + i % 64, s.hidden)
-        O.linear(rw, x, nthreads=n)
-        for _ in range(s.topk):
-            O.expert_swiglu(s.gate_type, mats[0], s.up_type, mats[1], s.down_type, mats[2], s.hidden, s.ff, x,
-                            nthreads=n)
-        for _ in range(s.n_shared):
-            O.expert_swiglu(s.sh_gate_type, mats[3], s.sh_up_type, mats[4], s.sh_down_type, mats[5], s.hidden,
-                            s.ff, x, 0.5, nthreads=n)
+        C_.token(synth.hidden_state(1 + i % 64, s.hidden), n)
 
     for i in range(args.warmup):
         step(i)
@@ -193,10 +217,11 @@ def run_reference(args):
             "config": {"workload": "config2_moe_layer_decode_1tok", "hidden": 7168, "ff": 2048, "experts": 256,
                        "topk": 6, "shared": 2, "types": "Q2_K gate/up, Q3_K down, Q4_K shared"},
             "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": n, "kind": "port",
-                             "sample": f"{args.steps} tokens of config 2 on {n} threads (oracle port of the "
-                                       "reference qlinear loop; the reference lacks Q2_K/Q3_K)"},
+                             "cpu_model": cpu_model(),
+                             "sample": f"{args.steps} tokens of config 2 (6 distinct routed experts) on {n} threads "
+                                       "(oracle port of the reference qlinear loop; the reference lacks Q2_K/Q3_K)"},
             "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "decode_tok_s": round(args.steps / dt, 3)}
+            "layer_steps_per_s": round(args.steps / dt, 3)}
     print(json.dumps(line), flush=True)
 
 
@@ -414,9 +439,11 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        sec, n, sample = cpu_token_seconds(shape)
+        sec, n, sample, sec1 = cpu_token_seconds(shape)
         cpu = {"value": round(tok_bytes / sec / 1e9, 4), "unit": "GB/s", "cores": n, "kind": "port",
-               "sample": sample, "tok_s": round(1.0 / sec, 3)}
+               "cpu_model": cpu_model(), "sample": sample, "layer_steps_per_s": round(1.0 / sec, 3),
+               "one_thread": {"value": round(tok_bytes / sec1 / 1e9, 4), "unit": "GB/s", "cores": 1,
+                              "layer_steps_per_s": round(1.0 / sec1, 4)}}
 
     if rank == 0:
         line = {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -429,7 +456,7 @@ def main():
                            "l2": f"inputs larger than L2: {args.layers} rotating layer instances x "
                                  f"{tok_bytes / 1e6:.1f} MB/step", "bytes_per_token": tok_bytes},
                 "pct_of_8tbs": round(100 * gbs / 8000, 2), "pct_of_measured_peak": round(100 * gbs / peak, 2),
-                "decode_tok_s": round(args.steps / (ms / 1e3), 1),
+                "layer_steps_per_s": round(args.steps / (ms / 1e3), 1),
                 "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": launches_per_step * args.steps,
                 "clocks": clocks}
         print(json.dumps(line), flush=True)

@@ -71,7 +71,8 @@ int sepia_cuda_sconv_hist_roll(float *hist, const float *in, int64_t C, int64_t 
 typedef struct {
     int64_t hidden, ff;
     int32_t n_routed, n_shared, topk;
-    float route_scale, global_scale;
+    double route_scale;        /* double, as the reference reads it from the config (src/sepia.c:434) */
+    float global_scale;
     const float *router_w;     /* [n_routed + n_shared, hidden] */
     const float *router_bias;  /* [n_routed] selection-only bias */
     int32_t gate_type, up_type, down_type;
@@ -146,7 +147,10 @@ int sepia_cuda_banded_attn(int kv_f16, const float *q, const void *k, const void
  * (sepia_cuda_banded_attn_noalloc_max_bytes), held on every GPU that loads
  * the library until exit. Shapes whose partials exceed it return 0 with a
  * "needs N bytes" error. The first call on each device resolves the array's
- * address; make it before any stream capture begins. All calls on a device
+ * address and caches it; make it before any stream capture begins. A
+ * cudaDeviceReset makes the cached address stale and the library does not
+ * notice: do not call this entry point on a device after resetting it in
+ * the same process. All calls on a device
  * share the array: calls whose kernels overlap on the GPU (unordered
  * streams) race; calls on one stream are safe. */
 size_t sepia_cuda_banded_attn_noalloc_max_bytes(void);
@@ -155,6 +159,18 @@ int sepia_cuda_banded_attn_noalloc(int kv_f16, const float *q, const void *k, co
                                    const int64_t *kv_hi, const float *tau, int64_t T, int64_t H, int64_t Hkv,
                                    int64_t Dh, int64_t rel_extent, int64_t q_pos_base, int64_t kv_dim,
                                    float inv_head_dim, int64_t max_kv, void *stream);
+
+/* ---------------------------------------------------------- test hooks */
+/* The stream that the sepia_gpu_* batch API (sepia_gpu.h) enqueues on. */
+void *sepia_cuda_lib_stream(void);
+/* Failure detection without a GPU fault (no counterpart in the reference):
+ * runs the tensor-core matvec engine with its producer announcing 16 bytes
+ * more than it copies, so no stage ever completes. Every waiting role gives
+ * up after wait_cycles SM clock cycles (<= about 4e9), records error 1 in
+ * the device error word (read by sepia_cuda_device_error or sepia_gpu_end)
+ * and returns; y is left unwritten. The context stays usable. */
+int sepia_cuda_test_engine_timeout(int ggml_type, const void *w, const float *x, float *y,
+                                   int64_t out_dim, int64_t in_dim, long long wait_cycles, void *stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

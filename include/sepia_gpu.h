@@ -102,7 +102,8 @@ int sepia_gpu_sconv_hist_roll(SepiaGpuBuf *hist, SepiaGpuBuf *in, int64_t C, int
 typedef struct {
     int64_t hidden, ff;
     int32_t n_routed, n_shared, topk;
-    float route_scale, global_scale;
+    double route_scale;        /* double, as the reference reads it from the config (src/sepia.c:434) */
+    float global_scale;
     SepiaGpuBuf *router_w; size_t router_w_off;       /* f32 [n_routed+n_shared, hidden] */
     SepiaGpuBuf *router_bias; size_t router_bias_off; /* f32 [n_routed] */
     int32_t gate_type, up_type, down_type;

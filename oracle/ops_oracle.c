@@ -73,6 +73,31 @@ int or_qlinear(int type, const void *w, int64_t out_dim, int64_t in_dim, const f
     return c.ok;
 }
 
+/* Several vectors through one matrix: each row is dequantized once and
+ * dotted with every vector by the same per-row arithmetic as or_qlinear
+ * (src/sepia.c:748-753), so y[v] equals or_qlinear(x[v]) bit for bit. */
+typedef struct { int type; const uint8_t *w; size_t rb; int64_t in, out, nv; const float *x; float *y; int ok; } QlbCtx;
+
+static void qlb_rows(void *c, int64_t r0, int64_t r1) {
+    QlbCtx *q = (QlbCtx *)c;
+    float *row = (float *)malloc(sizeof(float) * (size_t)(q->in ? q->in : 1));
+    if (!row) { q->ok = 0; return; }
+    for (int64_t o = r0; o < r1; o++) {
+        if (!or_dequantize_row(q->type, q->w + (size_t)o * q->rb, row, q->in)) { q->ok = 0; break; }
+        for (int64_t v = 0; v < q->nv; v++) q->y[v * q->out + o] = dot_d(row, q->x + v * q->in, q->in);
+    }
+    free(row);
+}
+
+int or_qlinear_batch(int type, const void *w, int64_t out_dim, int64_t in_dim, int64_t n_vec,
+                     const float *x, float *y, int nthreads) {
+    size_t rb = or_row_bytes(type, in_dim);
+    if (!rb) return 0;
+    QlbCtx c = { type, (const uint8_t *)w, rb, in_dim, out_dim, n_vec, x, y, 1 };
+    parallel_rows(qlb_rows, &c, out_dim, nthreads);
+    return c.ok;
+}
+
 typedef struct { const float *w; int64_t in; const float *x; float *y; } LinCtx;
 static void lin_rows(void *c, int64_t r0, int64_t r1) {
     LinCtx *l = (LinCtx *)c;
@@ -270,8 +295,8 @@ void or_rel_project(const float *r_vec, const float *rel_proj, float *rel_logits
 }
 
 typedef struct {
-    const float *q, *k, *v, *rl; float *out; const int64_t *lo, *hi; const float *tau;
-    int64_t H, Hkv, Dh, E, base, kv_dim; float inv;
+    const float *q, *k, *v, *rl; float *out; const int64_t *lo, *hi; const float *tau; const double *tau64;
+    int64_t H, Hkv, Dh, E, base, kv_dim; double inv;
 } AttnCtx;
 
 static void attn_rows(void *c, int64_t r0, int64_t r1) {
@@ -281,14 +306,14 @@ static void attn_rows(void *c, int64_t r0, int64_t r1) {
     for (int64_t th = r0; th < r1; th++) {
         const int64_t t = th / a->H, h = th % a->H, hk = h / group;
         const int64_t q_pos = a->base + t, lo = a->lo[t], hi = a->hi[t], n = hi - lo + 1;
-        const double tau = (double)a->tau[t];
+        const double tau = a->tau64 ? a->tau64[t] : (double)a->tau[t];
         const float *qv = a->q + th * a->Dh;
         const float *rl = a->rl + th * a->E;
         float *sc = (float *)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
         float mx = -INFINITY;
         for (int64_t kv = lo; kv <= hi; kv++) {
             const float *kvv = a->k + kv * a->kv_dim + hk * a->Dh;
-            double content = (double)dot_d(qv, kvv, a->Dh) * (double)a->inv;
+            double content = (double)dot_d(qv, kvv, a->Dh) * a->inv;
             int64_t dist = q_pos - kv;
             double bias = (dist < a->E) ? (double)rl[dist] * tau : 0.0;
             float s = (float)(content + bias);
@@ -309,11 +334,32 @@ static void attn_rows(void *c, int64_t r0, int64_t r1) {
     free(acc);
 }
 
+static void banded_attn_any(const float *q, const float *k, const float *v, const float *rel_logits,
+                            float *out, const int64_t *kv_lo, const int64_t *kv_hi, const float *tau,
+                            const double *tau64, int64_t T, int64_t H, int64_t Hkv, int64_t Dh, int64_t rel_extent,
+                            int64_t q_pos_base, int64_t kv_dim, float inv_head_dim, int nthreads) {
+    /* the reference scales by 1.0/(double)Dh (src/sepia.c:1217); a float equal
+     * to that value rounded stands for it */
+    const double inv_exact = 1.0 / (double)Dh;
+    AttnCtx c = { q, k, v, rel_logits, out, kv_lo, kv_hi, tau, tau64, H, Hkv, Dh, rel_extent,
+                  q_pos_base, kv_dim, ((float)inv_exact == inv_head_dim) ? inv_exact : (double)inv_head_dim };
+    parallel_rows(attn_rows, &c, T * H, nthreads);
+}
+
 void or_banded_attn(const float *q, const float *k, const float *v, const float *rel_logits,
                     float *out, const int64_t *kv_lo, const int64_t *kv_hi, const float *tau,
                     int64_t T, int64_t H, int64_t Hkv, int64_t Dh, int64_t rel_extent,
                     int64_t q_pos_base, int64_t kv_dim, float inv_head_dim, int nthreads) {
-    AttnCtx c = { q, k, v, rel_logits, out, kv_lo, kv_hi, tau, H, Hkv, Dh, rel_extent,
-                  q_pos_base, kv_dim, inv_head_dim };
-    parallel_rows(attn_rows, &c, T * H, nthreads);
+    banded_attn_any(q, k, v, rel_logits, out, kv_lo, kv_hi, tau, NULL, T, H, Hkv, Dh, rel_extent, q_pos_base,
+                    kv_dim, inv_head_dim, nthreads);
+}
+
+/* The same with tau in double, as attn_forward_chunk holds it
+ * (src/sepia.c:1188-1194: the bias is rel_logits * tau in double). */
+void or_banded_attn64(const float *q, const float *k, const float *v, const float *rel_logits,
+                      float *out, const int64_t *kv_lo, const int64_t *kv_hi, const double *tau,
+                      int64_t T, int64_t H, int64_t Hkv, int64_t Dh, int64_t rel_extent,
+                      int64_t q_pos_base, int64_t kv_dim, float inv_head_dim, int nthreads) {
+    banded_attn_any(q, k, v, rel_logits, out, kv_lo, kv_hi, NULL, tau, T, H, Hkv, Dh, rel_extent, q_pos_base,
+                    kv_dim, inv_head_dim, nthreads);
 }

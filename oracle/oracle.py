@@ -58,6 +58,8 @@ def lib():
         L.or_dequantize_row.argtypes = [C.c_int, C.c_void_p, F32P, C.c_int64]
         L.or_qlinear.restype = C.c_int
         L.or_qlinear.argtypes = [C.c_int, C.c_void_p, C.c_int64, C.c_int64, F32P, F32P, C.c_int]
+        L.or_qlinear_batch.restype = C.c_int
+        L.or_qlinear_batch.argtypes = [C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_int64, F32P, F32P, C.c_int]
         L.or_linear.argtypes = [F32P, C.c_int64, C.c_int64, F32P, F32P, C.c_int]
         L.or_rmsnorm.argtypes = [F32P, F32P, C.c_int64, C.c_float, F32P]
         L.or_silu_mul.argtypes = [F32P, F32P, F32P, C.c_int64]
@@ -76,6 +78,9 @@ def lib():
             [C.c_int64] * 7 + [C.c_float, C.c_int]
         L.or_moe_layer.restype = C.c_int
         L.or_moe_layer.argtypes = [C.c_void_p, F32P, F32P, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+        L.or_banded_attn64.argtypes = [F32P, F32P, F32P, F32P, F32P, I64P, I64P,
+                                       np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")] + \
+            [C.c_int64] * 7 + [C.c_float, C.c_int]
         L.or_f16_to_f32.restype = C.c_float
         L.or_f16_to_f32.argtypes = [C.c_uint16]
         _LIB = L
@@ -136,6 +141,15 @@ def qlinear(t: int, w: np.ndarray, out_dim: int, in_dim: int, x: np.ndarray, nth
     x = np.ascontiguousarray(x, np.float32)
     if not lib().or_qlinear(t, _ptr(w), out_dim, in_dim, x, y, nthreads):
         raise ValueError("oracle: qlinear failed")
+    return y
+
+
+def qlinear_batch(t: int, w: np.ndarray, out_dim: int, in_dim: int, X: np.ndarray, nthreads: int = 1) -> np.ndarray:
+    """[n_vec, in_dim] vectors through one matrix; row v equals qlinear(X[v])."""
+    X = np.ascontiguousarray(X, np.float32)
+    y = np.empty((X.shape[0], out_dim), np.float32)
+    if not lib().or_qlinear_batch(t, _ptr(w), out_dim, in_dim, X.shape[0], X.reshape(-1), y.reshape(-1), nthreads):
+        raise ValueError("oracle: qlinear_batch failed")
     return y
 
 
@@ -222,6 +236,35 @@ def banded_attn(q, k, v, rel_logits, kv_lo, kv_hi, tau, T, H, Hkv, Dh, rel_exten
                          out, np.ascontiguousarray(kv_lo, np.int64), np.ascontiguousarray(kv_hi, np.int64),
                          np.ascontiguousarray(tau, np.float32), T, H, Hkv, Dh, rel_extent, q_pos_base, kv_dim,
                          inv_head_dim, nthreads)
+    return out
+
+
+def banded_attn64(q, k, v, rel_logits, kv_lo, kv_hi, tau64, T, H, Hkv, Dh, rel_extent, q_pos_base, kv_dim,
+                  inv_head_dim, nthreads=1):
+    """banded_attn with tau in double, as attn_forward_chunk holds it."""
+    out = np.empty(T * H * Dh, np.float32)
+    lib().or_banded_attn64(np.ascontiguousarray(q, np.float32), np.ascontiguousarray(k, np.float32),
+                           np.ascontiguousarray(v, np.float32), np.ascontiguousarray(rel_logits, np.float32),
+                           out, np.ascontiguousarray(kv_lo, np.int64), np.ascontiguousarray(kv_hi, np.int64),
+                           np.ascontiguousarray(tau64, np.float64), T, H, Hkv, Dh, rel_extent, q_pos_base, kv_dim,
+                           inv_head_dim, nthreads)
+    return out
+
+
+def rmsnorm(x, w, eps):
+    """src/sepia.c:720-729 on one row."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    lib().or_rmsnorm(x, np.ascontiguousarray(w, np.float32), x.size, np.float32(eps), out)
+    return out
+
+
+def sconv_apply(w, C_, K, hist, inp, T):
+    """src/sepia.c:801-816; hist ([K-1, C]) is updated in place."""
+    assert hist.dtype == np.float32 and hist.flags.c_contiguous
+    out = np.empty(T * C_, np.float32)
+    lib().or_sconv_apply(np.ascontiguousarray(w, np.float32), C_, K, hist, np.ascontiguousarray(inp, np.float32),
+                         T, out)
     return out
 
 

@@ -16,7 +16,7 @@
  *     (tests/golden/make_golden.py).
  *   - qlinear / router selection / sconv / rmsnorm / banded attention:
  *     pinned against the reference's static functions compiled from
- *     src/sepia.c (oracle/ref_shim.c) when /root/reference is present.
+ *     src/sepia.c (oracle/ref_shim.c) when the reference checkout is present.
  */
 #ifndef SEPIA_ORACLE_H
 #define SEPIA_ORACLE_H
@@ -49,6 +49,8 @@ int     or_dequantize_row(int type, const void *src, float *dst, int64_t n);
  * pthreads (nthreads <= 1: the reference's single-threaded loop). */
 int or_qlinear(int type, const void *w, int64_t out_dim, int64_t in_dim,
                const float *x, float *y, int nthreads);
+int or_qlinear_batch(int type, const void *w, int64_t out_dim, int64_t in_dim, int64_t n_vec,
+                     const float *x, float *y, int nthreads);
 /* f32 linear (src/sepia.c:731-740). */
 void or_linear(const float *w, int64_t out_dim, int64_t in_dim, const float *x, float *y, int nthreads);
 
@@ -108,6 +110,10 @@ void or_banded_attn(const float *q, const float *k, const float *v, const float 
                     float *out, const int64_t *kv_lo, const int64_t *kv_hi, const float *tau,
                     int64_t T, int64_t H, int64_t Hkv, int64_t Dh, int64_t rel_extent,
                     int64_t q_pos_base, int64_t kv_dim, float inv_head_dim, int nthreads);
+void or_banded_attn64(const float *q, const float *k, const float *v, const float *rel_logits,
+                      float *out, const int64_t *kv_lo, const int64_t *kv_hi, const double *tau,
+                      int64_t T, int64_t H, int64_t Hkv, int64_t Dh, int64_t rel_extent,
+                      int64_t q_pos_base, int64_t kv_dim, float inv_head_dim, int nthreads);
 
 #ifdef __cplusplus
 }

@@ -39,7 +39,7 @@ struct AttnParams {
     const float *tau;
     double *part;              // [T, H, S, Dh + 2]: m, l, acc[Dh] (fp64: no rounding before the combine)
     int64_t T, H, Hkv, Dh, E, q_pos_base, kv_dim;
-    float inv_head_dim;
+    double inv_head_dim;       // 1.0/(double)Dh when the caller passed that value rounded to float
     int S;
     int64_t max_chunk;         // kv positions per split (upper bound)
 };
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
                 for (int j = 0; j < kHPT; j++) {
                     const int g = g0 + gstep * j;
                     if (g < G) {
-                        double sc = (double)(float)dd[j] * (double)P.inv_head_dim;
+                        double sc = (double)(float)dd[j] * P.inv_head_dim;
                         if (dist < P.E && dist >= 0)
                             sc += (double)P.rel_logits[(t * P.H + (int64_t)hk * G + g) * P.E + dist] * (double)tau;
                         ss[g * kAttnKT + r] = (float)sc;
@@ -439,7 +439,11 @@ int launch_banded_attn(int kv_f16, const float *q, const void *k, const void *v,
     AttnParams P;
     P.q = q; P.k = k; P.v = v; P.rel_logits = rel_logits; P.kv_lo = kv_lo_d; P.kv_hi = kv_hi_d; P.tau = tau_d;
     P.part = part; P.T = T; P.H = H; P.Hkv = Hkv; P.Dh = Dh; P.E = E; P.q_pos_base = q_pos_base; P.kv_dim = kv_dim;
-    P.inv_head_dim = inv_head_dim; P.S = S; P.max_chunk = 0;
+    // The reference scales by 1.0/(double)Dh (src/sepia.c:1217); the ABI
+    // carries a float, so a float equal to that value rounded stands for it.
+    const double inv_exact = 1.0 / (double)Dh;
+    P.inv_head_dim = ((float)inv_exact == inv_head_dim) ? inv_exact : (double)inv_head_dim;
+    P.S = S; P.max_chunk = 0;
     const int G = (int)(H / Hkv);
     if (!(kv_f16 ? attn_launch_split<__half>(P, G, st) : attn_launch_split<float>(P, G, st))) return 0;
     k_attn_combine<<<(unsigned)(T * H), 128, 0, st>>>(part, out, T * H, S, Dh);

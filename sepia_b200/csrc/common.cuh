@@ -166,11 +166,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 
 // Bounded wait: returns false (and records kErrWaitTimeout) if the phase
 // does not complete within kWaitCycles.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err,
+                                          long long limit = kWaitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > limit) {
             set_error(err, kErrWaitTimeout);
             return false;
         }

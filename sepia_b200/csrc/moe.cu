@@ -44,7 +44,8 @@ constexpr int kDnMaxSlots = 8;     // topk + n_shared handled by the down kernel
 struct MoeDev {
     int64_t hidden, ff;
     int n_routed, n_shared, topk;
-    float route_scale, global_scale;
+    double route_scale;
+    float global_scale;
     const float *router_w, *router_bias;
     int gate_type, up_type, down_type, sh_gate_type, sh_up_type, sh_down_type;
     const uint8_t *gate, *up, *down, *sh_gate, *sh_up, *sh_down;

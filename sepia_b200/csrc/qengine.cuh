@@ -84,6 +84,8 @@ struct QeLayout {
     uint32_t slot_bytes, red_off, tab_off, stage_off;
     int n_tab, tab_nsb;    // tables x superblocks each
     int *err;
+    long long wait_cycles = kWaitCycles;   // bound of every mbarrier wait
+    uint32_t test_extra_tx = 0;            // test hook only: extra bytes the producer announces
 };
 
 // Programmatic dependent launch: a kernel launched with the programmatic
@@ -173,7 +175,7 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
         if (qe_block_mode(U)) {
             // whole rows with a bank-friendly stride: two copies of 8 rows
             const ByteRange rl{U.lo, (uint32_t)(U.nlo * U.rb)}, rh{U.hi, (uint32_t)(U.nhi * U.rb)};
-            mbar_arrive_expect_tx(&full[slot], range_copy_bytes(rl) + (U.nhi ? range_copy_bytes(rh) : 0u));
+            mbar_arrive_expect_tx(&full[slot], range_copy_bytes(rl) + (U.nhi ? range_copy_bytes(rh) : 0u) + P.test_extra_tx);
             range_issue(dst, rl, &full[slot]);
             if (U.nhi) range_issue(dst + qe_hi_off(U.rb), rh, &full[slot]);
             return;
@@ -183,7 +185,7 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
         uint32_t tx = 0;
         for (int i = 0; i < U.nlo; i++) tx += range_copy_bytes(ByteRange{U.lo + i * U.rb + off, bytes});
         for (int i = 0; i < U.nhi; i++) tx += range_copy_bytes(ByteRange{U.hi + i * U.rb + off, bytes});
-        mbar_arrive_expect_tx(&full[slot], tx);
+        mbar_arrive_expect_tx(&full[slot], tx + P.test_extra_tx);
         for (int i = 0; i < U.nlo; i++) range_issue(dst + i * pitch, ByteRange{U.lo + i * U.rb + off, bytes}, &full[slot]);
         for (int i = 0; i < U.nhi; i++)
             range_issue(dst + (8 + i) * pitch, ByteRange{U.hi + i * U.rb + off, bytes}, &full[slot]);
@@ -267,7 +269,7 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             while (pu < n_units) {
                 if (psp == 0) J.unit(jsm, pu, PU);
                 if (psp < PU.nsplit) {
-                    if (pk >= P.stages && !mbar_wait(&empty[pring.slot], pring.phase ^ 1u, P.err)) { ok = false; break; }
+                    if (pk >= P.stages && !mbar_wait(&empty[pring.slot], pring.phase ^ 1u, P.err, P.wait_cycles)) { ok = false; break; }
                     issue(PU, psp, pring.slot);
                     pk++;
                     pring.next(P.stages);
@@ -278,10 +280,12 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
                 }
             }
             QE_STAMP(6);
-            // no bulk copy may be in flight when the CTA exits
-            if (ok)
-                for (int64_t j = (pk > P.stages ? pk - P.stages : 0); j < pk; j++)
-                    mbar_wait(&full[j % P.stages], (uint32_t)((j / P.stages) & 1), nullptr);
+            // No bulk copy may be in flight when the CTA exits, on the error
+            // path too: the copies already issued complete on their "full"
+            // barriers whatever the consumers do, so wait for each (bounded).
+            (void)ok;
+            for (int64_t j = (pk > P.stages ? pk - P.stages : 0); j < pk; j++)
+                mbar_wait(&full[j % P.stages], (uint32_t)((j / P.stages) & 1), nullptr, P.wait_cycles);
         }
         return;
     }
@@ -295,7 +299,7 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             double acc = 0.0;
             bool ok = true;
             for (int sp = 0; sp < U.nsplit; sp++) {
-                if (!mbar_wait(&ready[ring.slot], ring.phase, P.err)) { ok = false; break; }
+                if (!mbar_wait(&ready[ring.slot], ring.phase, P.err, P.wait_cycles)) { ok = false; break; }
                 if (lane < 16) {
                     const double *rs = red + (size_t)ring.slot * P.cg * 16 + lane;
                     for (int c = 0; c < P.cg; c++) acc += rs[c * 16];
@@ -339,7 +343,7 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             const bool mine = (g == grp);
             if (++g == P.G) g = 0;
             if (!mine) continue;
-            if (!mbar_wait(&full[slot], phase, P.err)) return;
+            if (!mbar_wait(&full[slot], phase, P.err, P.wait_cycles)) return;
             if (first && warp == 0 && lane == 0) QE_STAMP(3);
             first = false;
             const int s0 = sp * U.sbs, s1 = min(U.nsb, s0 + U.sbs), n = s1 - s0;

@@ -166,7 +166,8 @@ struct MvJob {
 
 
 static int launch_matvec_engine(int t, const void *w, const float *x, float *y, int64_t out_dim, int64_t in_dim,
-                                int64_t rb, cudaStream_t st) {
+                                int64_t rb, cudaStream_t st, long long wait_cycles = kWaitCycles,
+                                uint32_t test_extra_tx = 0) {
     DevInfo &di = dev_info();
     MvJob J;
     J.w = reinterpret_cast<const uint8_t *>(w);
@@ -182,6 +183,8 @@ static int launch_matvec_engine(int t, const void *w, const float *x, float *y, 
     if (!qe_layout(P, G, cg, (uint32_t)J.sbs * qe_sb_bytes(t), 1, J.nsb, di.smem_optin, smem))
         return fail("matvec_q: tensor-core tile needs %lld B of shared memory", (long long)smem);
     P.err = di.err;
+    P.wait_cycles = wait_cycles;
+    P.test_extra_tx = test_extra_tx;
     const void *fn = (const void *)k_qengine<MvJob>;
     if (!ensure_smem(fn, (int)smem)) return 0;
     const int64_t units = (out_dim + 15) / 16;
@@ -590,3 +593,22 @@ extern "C" int sepia_cuda_matvec_q(int ggml_type, const void *w, const float *x,
 extern "C" int sepia_cuda_dequant(int ggml_type, const void *raw, float *out, int64_t n, void *stream) {
     return sepia::launch_dequant(ggml_type, raw, out, n, sepia::as_stream(stream));
 }
+
+// ------------------------------------------------------------ test hook
+// Failure detection without a GPU fault: the engine's producer announces 16
+// more bytes than it copies, so the first stage never completes; every
+// waiting role gives up after `wait_cycles` clock cycles, records
+// kErrWaitTimeout in the device error word and returns. The copies it did
+// issue all land before the CTA exits. Used only by the tests.
+extern "C" int sepia_cuda_test_engine_timeout(int ggml_type, const void *w, const float *x, float *y,
+                                              int64_t out_dim, int64_t in_dim, long long wait_cycles,
+                                              void *stream) {
+    using namespace sepia;
+    const int64_t rb = host_row_bytes(ggml_type, in_dim);
+    if (rb <= 0 || !engine_ok(ggml_type, w, x, in_dim, rb, 1))
+        return fail("test_engine_timeout: shape not on the tensor-core engine");
+    if (wait_cycles <= 0 || wait_cycles > kWaitCycles) return fail("test_engine_timeout: bad wait limit");
+    return launch_matvec_engine(ggml_type, w, x, y, out_dim, in_dim, rb, as_stream(stream), wait_cycles, 16u);
+}
+
+extern "C" void *sepia_cuda_lib_stream(void) { return (void *)sepia::lib_stream(); }

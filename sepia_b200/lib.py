@@ -24,7 +24,7 @@ i32 = C.c_int32
 
 class SepiaMoeLayer(C.Structure):
     _fields_ = [("hidden", i64), ("ff", i64), ("n_routed", i32), ("n_shared", i32), ("topk", i32),
-                ("route_scale", C.c_float), ("global_scale", C.c_float),
+                ("route_scale", C.c_double), ("global_scale", C.c_float),
                 ("router_w", vp), ("router_bias", vp),
                 ("gate_type", i32), ("up_type", i32), ("down_type", i32),
                 ("gate", vp), ("up", vp), ("down", vp),
@@ -41,7 +41,7 @@ class SepiaMoeWork(C.Structure):
 
 class SepiaGpuMoeDesc(C.Structure):
     _fields_ = [("hidden", i64), ("ff", i64), ("n_routed", i32), ("n_shared", i32), ("topk", i32),
-                ("route_scale", C.c_float), ("global_scale", C.c_float),
+                ("route_scale", C.c_double), ("global_scale", C.c_float),
                 ("router_w", vp), ("router_w_off", C.c_size_t), ("router_bias", vp), ("router_bias_off", C.c_size_t),
                 ("gate_type", i32), ("up_type", i32), ("down_type", i32),
                 ("experts", vp), ("gate_off", C.c_size_t), ("up_off", C.c_size_t), ("down_off", C.c_size_t),
@@ -112,6 +112,8 @@ _PROTOS = {
     "sepia_cuda_banded_attn_ws_bytes": (C.c_size_t, [i64, i64, i64, i64, i64]),
     "sepia_cuda_banded_attn": (C.c_int, [C.c_int, vp, vp, vp, vp, vp, vp, vp, vp] + [i64] * 7 + [C.c_float, i64, vp,
                                                                                                   C.c_size_t, vp]),
+    "sepia_cuda_lib_stream": (vp, []),
+    "sepia_cuda_test_engine_timeout": (C.c_int, [C.c_int, vp, vp, vp, i64, i64, C.c_longlong, vp]),
     "sepia_cuda_banded_attn_noalloc_max_bytes": (C.c_size_t, []),
     "sepia_cuda_banded_attn_noalloc": (C.c_int, [C.c_int, vp, vp, vp, vp, vp, vp, vp, vp] + [i64] * 7
                                        + [C.c_float, i64, vp]),

@@ -7,7 +7,8 @@ import pytest
 ROOT = Path(__file__).resolve().parent.parent
 sys.path.insert(0, str(ROOT))
 
-REFERENCE = Path(os.environ.get("SEPIA_REFERENCE", "/root/reference"))
+# the reference checkout: $SEPIA_REFERENCE, else a "reference" directory beside the repository
+REFERENCE = Path(os.environ.get("SEPIA_REFERENCE", str(ROOT.parent / "reference")))
 
 
 def pytest_configure(config):

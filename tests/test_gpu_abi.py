@@ -187,3 +187,36 @@ def test_copy_and_moe_extension(G, oracle):
     assert np.array_equal(get(G, bi, 6, np.int32), idx)
     assert oracle.rel_err(get(G, bo, 1024), want) <= 1e-4
     assert np.array_equal(get(G, bc, 1024), get(G, bo, 1024))
+
+
+def test_bounded_wait_timeout_reports_and_context_survives(lib):
+    """Failure detection without a GPU fault: the engine's producer
+    announces more bytes than it copies, every waiting role gives up after a
+    short bound (2e6 cycles, ~1 ms) and records error 1; the host reads it
+    through sepia_cuda_device_error and through sepia_gpu_end (which must
+    return 0); afterwards the same call without the hook computes normally."""
+    import torch
+    from sepia_b200 import ops
+    rng = np.random.default_rng(11)
+    t, out_dim, in_dim = Q.Q2_K, 64, 2048
+    w = torch.from_numpy(synth.matrix_host(rng, t, out_dim, in_dim)).cuda()
+    x = torch.from_numpy(rng.standard_normal(in_dim).astype(np.float32)).cuda()
+    y = torch.zeros(out_dim, dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib.sepia_cuda_device_error(st) == 0
+    assert lib.sepia_cuda_test_engine_timeout(t, w.data_ptr(), x.data_ptr(), y.data_ptr(), out_dim, in_dim,
+                                              2_000_000, st) == 1
+    assert lib.sepia_cuda_device_error(st) == 1
+    assert lib.sepia_cuda_device_error(st) == 0          # read-and-clear
+    # through the reference-shaped batch API: end() reports the failure
+    assert lib.sepia_gpu_init(b"metal") == 1
+    assert lib.sepia_gpu_begin() == 1
+    assert lib.sepia_cuda_test_engine_timeout(t, w.data_ptr(), x.data_ptr(), y.data_ptr(), out_dim, in_dim,
+                                              2_000_000, lib.sepia_cuda_lib_stream()) == 1
+    assert lib.sepia_gpu_end() == 0
+    assert b"device error" in lib.sepia_cuda_last_error()
+    # the context still works
+    good = ops.matvec_q(t, w, x, out_dim, in_dim)
+    torch.cuda.synchronize()
+    assert lib.sepia_cuda_device_error(st) == 0
+    assert torch.isfinite(good).all()

@@ -101,3 +101,18 @@ def test_abi_banded_attn_and_rel_project(lib, oracle):
     assert G.sepia_gpu_end() == 1
     assert oracle.rel_err(get(G, brl, T * H * E), rl_want) <= 1e-6
     assert oracle.rel_err(get(G, bo, T * H * c["Dh"]), run_oracle(oracle, c)) <= TOL
+
+
+@pytest.mark.parametrize("ctx,window,tau_v", [(32768, 0, 1.21), (4096, 4096, 1.0), (32768, 4096, 1.0)],
+                         ids=["global_32768_tau", "window_4096_ctx4096", "window_4096_ctx32768"])
+def test_config4_full_context(lib, oracle, ctx, window, tau_v):
+    """BASELINE configuration 4 at its stated contexts: 64 query heads, 8 KV
+    heads, Dh 128, fp16 K/V, rel_extent 256, decode (T = 1) at position
+    ctx - 1; the global case with tau != 1 (long fp64 chains over 32768
+    keys are where an fp32 score path loses the 1e-4 bar)."""
+    rng = np.random.default_rng(ctx + window)
+    c = make_case(rng, 1, 64, 8, 128, 256, ctx - 1, window, tau_v, f16=True)
+    want = oracle.banded_attn(c["q"], c["k"], c["v"], c["rl"], c["lo"], c["hi"], c["tau"], c["T"], c["H"],
+                              c["Hkv"], c["Dh"], c["E"], c["base"], c["kv_dim"], 1.0 / c["Dh"],
+                              nthreads=oracle.nproc())
+    assert oracle.rel_err(run_gpu(c, True), want) <= TOL

@@ -153,3 +153,58 @@ def test_router_selection_wide_and_ties(lib, oracle, n_routed, n_shared, dup):
         idx, wt = oracle.route_select(logits, bias, n_routed, n_shared, 6, shape.route_scale, shape.global_scale)
         assert np.array_equal(D.topk_idx.cpu().numpy(), idx), (seed, D.topk_idx.cpu().numpy(), idx)
         assert oracle.rel_err(D.weights.cpu().numpy(), wt) <= 1e-5, seed
+
+
+def _device_layer_oracle(oracle, D, x, host_cache):
+    """The oracle's mlp_moe_forward (src/sepia.c:1377-1470) for a layer whose
+    expert store lives on the GPU: the router runs on the host copy of the
+    f32 router, and only the selected experts' bytes are copied back."""
+    s = D.shape
+    if "router_w" not in host_cache:
+        host_cache["router_w"] = D.router_w.cpu().numpy()
+        host_cache["router_bias"] = D.router_bias.cpu().numpy()
+        sg, su, sd = D.strides[3:]
+        ng = Q.row_bytes(s.sh_gate_type, s.hidden) * s.ff
+        nu = Q.row_bytes(s.sh_up_type, s.hidden) * s.ff
+        nd = Q.row_bytes(s.sh_down_type, s.ff) * s.hidden
+        host_cache["shared"] = [(D.sh_gate[k * sg:k * sg + ng].cpu().numpy(), D.sh_up[k * su:k * su + nu].cpu().numpy(),
+                                 D.sh_down[k * sd:k * sd + nd].cpu().numpy()) for k in range(s.n_shared)]
+    nt = oracle.nproc()
+    logits = oracle.linear(host_cache["router_w"], x, nthreads=nt)
+    idx, w = oracle.route_select(logits, host_cache["router_bias"], s.n_routed, s.n_shared, s.topk,
+                                 s.route_scale, s.global_scale)
+    out = np.zeros(s.hidden, np.float32)
+    for j, e in enumerate(idx):
+        g, u, d = D.expert_bytes_host(int(e))
+        y = oracle.expert_swiglu(s.gate_type, g, s.up_type, u, s.down_type, d, s.hidden, s.ff, x, nthreads=nt)
+        out += y * w[j]        # routed weight applied after down (src/sepia.c:1425)
+    for k, (g, u, d) in enumerate(host_cache["shared"]):
+        out += oracle.expert_swiglu(s.sh_gate_type, g, s.sh_up_type, u, s.sh_down_type, d, s.hidden, s.ff, x,
+                                    w[s.topk + k], nthreads=nt)
+    return out, logits, idx, w
+
+
+def test_config2_full_layer_seeds_1_to_64(lib, oracle):
+    """BASELINE configuration 2 at full size: 256 routed experts (Q2_K
+    gate/up, Q3_K down), 2 shared Q4_K experts, the f32 [258 x 7168] router,
+    hidden states of seeds 1-64. Router ids exact, output within 1e-4."""
+    import torch
+    from sepia_b200.moe import MoeLayerDevice
+    from sepia_b200.synth import MoeShape as S
+    shape = S()
+    D = MoeLayerDevice.random(shape, seed=2)
+    cache = {}
+    out = torch.empty(shape.hidden, dtype=torch.float32, device="cuda")
+    worst = 0.0
+    for seed in range(1, 65):
+        x = hidden_state(seed, shape.hidden)
+        D.forward(torch.from_numpy(x).cuda(), out)
+        torch.cuda.synchronize()
+        want, logits, idx, w = _device_layer_oracle(oracle, D, x, cache)
+        assert np.array_equal(D.topk_idx.cpu().numpy(), idx), seed
+        assert oracle.rel_err(D.weights.cpu().numpy(), w) <= 1e-5, seed
+        err = oracle.rel_err(out.cpu().numpy(), want)
+        worst = max(worst, err)
+        assert err <= TOL, (seed, err)
+    del D
+    torch.cuda.empty_cache()

@@ -135,6 +135,23 @@ def test_config3_full_rows(torch_cuda, oracle, t, rows):
     assert oracle.rel_err(got, want) <= TOL
 
 
+@pytest.mark.parametrize("n_vec", [4, 16])
+@pytest.mark.parametrize("rows", [2048, 7168, 16384])
+@pytest.mark.parametrize("t", [Q.IQ1_S, Q.IQ2_XXS])
+def test_config3_full_rows_batched(torch_cuda, oracle, t, rows, n_vec):
+    """BASELINE configuration 3 at its full shapes for batches 4 and 16:
+    every vector within 1e-4 of the oracle's qlinear of that vector."""
+    from sepia_b200 import ops
+    torch = torch_cuda
+    rng = np.random.default_rng(rows * 31 + t * 7 + n_vec)
+    w = synth.matrix_host(rng, t, rows, 7168)
+    X = rng.standard_normal((n_vec, 7168)).astype(np.float32)
+    want = oracle.qlinear_batch(t, w, rows, 7168, X, nthreads=oracle.nproc())
+    got = ops.matvec_q(t, _dev(torch, w), _dev(torch, X), rows, 7168).cpu().numpy()
+    for v in range(n_vec):
+        assert oracle.rel_err(got[v], want[v]) <= TOL, v
+
+
 def test_config1_swiglu_slab(torch_cuda, oracle):
     """y = down(silu(gate x) * (up x)), Q2_K,
     2048x7168 / 7168x2048, x ~ N(0,1) seed 0."""
