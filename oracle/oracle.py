@@ -107,8 +107,28 @@ def ref_lib():
         R.ref_sconv_apply.argtypes = [F32P, C.c_int, C.c_int, F32P, F32P, C.c_int, F32P]
         R.ref_attn_chunk.argtypes = [C.c_int] * 7 + [C.c_int, C.c_int, C.c_float, C.c_int, C.c_double, C.c_long] + \
             [F32P] * 14 + [F32P, C.c_int, C.c_int, F32P]
+        R.ref_generate_ids.restype = C.c_int
+        R.ref_generate_ids.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, I32P, C.c_int, C.c_int, I32P, C.c_void_p]
         _REF = R
     return _REF
+
+
+def ref_generate(container_dir, prompt, n_gen, with_logits=True):
+    """The reference's own greedy loop on a container (oracle/_ref): returns
+    (ids [n_gen], logits [n_gen, unpadded] or None). None without _ref."""
+    R = ref_lib()
+    if R is None:
+        return None
+    import json
+    d = Path(container_dir)
+    tc = json.loads((d / "config.json").read_text())["text_config"]
+    prompt = np.ascontiguousarray(prompt, np.int32)
+    ids = np.zeros(n_gen, np.int32)
+    logits = np.zeros((n_gen, tc["unpadded_vocab_size"]), np.float32) if with_logits else None
+    R.ref_generate_ids(str(d / "config.json").encode(), str(d / "resident-manifest.json").encode(),
+                       str(d / "index.json").encode(), prompt, len(prompt), n_gen, ids,
+                       logits.ctypes.data if with_logits else None)
+    return ids, logits
 
 
 # ---------------------------------------------------------------- helpers

@@ -10,10 +10,39 @@
  *   rmsnorm            src/sepia.c:720-729
  *   sconv_apply        src/sepia.c:801-816
  *   attn_forward_chunk src/sepia.c:1077-1276
+ *   real_load + real_forward_chunk + real_generate's greedy loop
+ *                      src/sepia.c:2647, 3345, 4114 (token ids in and out:
+ *                      the tokenizer file real_load opens is not needed, so
+ *                      its loader is replaced by one that returns NULL)
  * Built by oracle/Makefile into oracle/_ref/libsepia_ref.so. */
+#include "src/tokenizer.h"
+#include "src/quants.h"
+static Tokenizer *shim_tokenizer_load(const char *path) { (void)path; return (Tokenizer *)0; }
+
+/* src/quants.c has no Q2_K, Q3_K, IQ2_XXS or IQ1_S (src/quants.h:6-10). For
+ * the decoder (sepia.c) only, rows of those four formats are dequantized by
+ * this directory's restatement, pinned bitwise to gguf-py 0.19.0
+ * (quants_oracle.c); every other format still goes through src/quants.c.
+ * The ref_dequantize_row / ref_qlinear exports below are not redirected. */
+int or_dequantize_row(int type, const void *src, float *dst, int64_t n);
+size_t or_row_bytes(int type, int64_t n);
+static int shim_extra_type(int t) { return t == 10 || t == 11 || t == 16 || t == 19; }
+static size_t shim_row_bytes(int t, int64_t ne) {
+    return shim_extra_type(t) ? or_row_bytes(t, ne) : quants_row_bytes(t, ne);
+}
+static void shim_dequantize_row(int t, const void *src, float *dst, int64_t n) {
+    if (shim_extra_type(t)) or_dequantize_row(t, src, dst, n);
+    else dequantize_row(t, src, dst, n);
+}
+#define tokenizer_load shim_tokenizer_load
+#define quants_row_bytes shim_row_bytes
+#define dequantize_row shim_dequantize_row
 #define main sepia_reference_main
 #include "src/sepia.c"
 #undef main
+#undef tokenizer_load
+#undef quants_row_bytes
+#undef dequantize_row
 
 #include <pthread.h>
 
@@ -115,4 +144,34 @@ void ref_attn_chunk(int hidden, int H, int Hkv, int Dh, int d_rel, int rel_exten
     lc.len = start_pos;
     lc.k = k_cache; lc.v = v_cache; lc.k_hist = k_hist; lc.v_hist = v_hist;
     attn_forward_chunk(&cfg, &lw, &lc, x_normed, T, start_pos, out);
+}
+
+/* Greedy generation on a container, token ids in and out: real_load
+ * (page-cache expert reads), real_forward_chunk over the prompt, then
+ * real_generate's loop (src/sepia.c:4131-4151): argmax of the current
+ * logits, forward that token, n_gen times (no eos stop). out_ids[n_gen];
+ * out_logits (optional) [n_gen, unpadded_vocab] = the logits each id was
+ * taken from. Returns unpadded_vocab_size. Dies (exits) on a bad container,
+ * as real_load does. */
+int ref_generate_ids(const char *config_path, const char *manifest_path, const char *index_path,
+                     const int *prompt, int n_prompt, int n_gen, int *out_ids, float *out_logits) {
+    RealModel m = real_load(config_path, manifest_path, index_path, "unused-tokenizer", 0, 0, 1);
+    const int unpadded = m.cfg.unpadded_vocab_size;
+    Cache *cache = cache_create_cfg(&m.cfg, n_prompt + n_gen + 8);
+    float *logits = xmalloc(sizeof(float) * (size_t)n_prompt * (size_t)unpadded);
+    real_forward_chunk(&m, cache, prompt, n_prompt, 0, logits);
+    float *cur = xmalloc(sizeof(float) * (size_t)unpadded);
+    memcpy(cur, logits + (size_t)(n_prompt - 1) * unpadded, sizeof(float) * (size_t)unpadded);
+    free(logits);
+    int pos = n_prompt;
+    for (int i = 0; i < n_gen; i++) {
+        int tok = argmax_f(cur, unpadded);
+        out_ids[i] = tok;
+        if (out_logits) memcpy(out_logits + (size_t)i * unpadded, cur, sizeof(float) * (size_t)unpadded);
+        real_forward_chunk(&m, cache, &tok, 1, pos, cur);
+        pos++;
+    }
+    cache_free(cache);
+    free(cur);
+    return unpadded;
 }

@@ -37,6 +37,8 @@ struct AttnParams {
     const float *rel_logits;   // [T, H, E]
     const int64_t *kv_lo, *kv_hi;
     const float *tau;
+    const double *tau64;       // tau in double (the reference's type); overrides tau when set
+    const int32_t *qpos_dev;   // q_pos_base read on the device (decode graphs); overrides q_pos_base
     double *part;              // [T, H, S, Dh + 2]: m, l, acc[Dh] (fp64: no rounding before the combine)
     int64_t T, H, Hkv, Dh, E, q_pos_base, kv_dim;
     double inv_head_dim;       // 1.0/(double)Dh when the caller passed that value rounded to float
@@ -79,8 +81,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
     const int64_t chunk = (n + P.S - 1) / P.S;
     const int64_t c0 = lo + (int64_t)s * chunk;
     const int64_t c1 = min(hi + 1, c0 + chunk);
-    const int64_t q_pos = P.q_pos_base + t;
-    const float tau = P.tau[t];
+    const int64_t q_pos = (P.qpos_dev ? (int64_t)*P.qpos_dev : P.q_pos_base) + t;
+    const double tau = P.tau64 ? P.tau64[t] : (double)P.tau[t];
     const KV *K = reinterpret_cast<const KV *>(P.k);
     const KV *V = reinterpret_cast<const KV *>(P.v);
 
@@ -117,11 +119,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
     // PV ownership: warp w owns heads g = w, w+8, ...; lane owns dims lane + 32j
     constexpr int kHPW = (GM + kAttnWarps - 1) / kAttnWarps;   // heads per warp (GM >= G)
     constexpr int kHPT = (GM + (kAttnThreads / kAttnKT) - 1) / (kAttnThreads / kAttnKT);   // score heads per thread
-    double acc[kHPW][kAttnMaxDh / 32];   // fp64: long kv chains stay at fp32 rounding
+    double acc[kHPW][kAttnMaxDh / 32];   // fp64, as the reference accumulates
+    double acc_b[kHPW][kAttnMaxDh / 32]; // VEC: the odd rows' accumulators
 #pragma unroll
     for (int a = 0; a < kHPW; a++)
 #pragma unroll
-        for (int j = 0; j < kAttnMaxDh / 32; j++) acc[a][j] = 0.0;
+        for (int j = 0; j < kAttnMaxDh / 32; j++) acc[a][j] = acc_b[a][j] = 0.0;
 
     if (c0 < c1) stage(c0, (int)min((int64_t)kAttnKT, c1 - c0), 0);
     int buf = 0;
@@ -221,7 +224,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
                     if (g < G) {
                         double sc = (double)(float)dd[j] * P.inv_head_dim;
                         if (dist < P.E && dist >= 0)
-                            sc += (double)P.rel_logits[(t * P.H + (int64_t)hk * G + g) * P.E + dist] * (double)tau;
+                            sc += (double)P.rel_logits[(t * P.H + (int64_t)hk * G + g) * P.E + dist] * tau;
                         ss[g * kAttnKT + r] = (float)sc;
                     }
                 }
@@ -248,64 +251,63 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
                 __syncwarp();
                 if (lane == 0) { sml[2 * g] = m_new; sml[2 * g + 1] = sml[2 * g + 1] * corr + psum; }
 #pragma unroll
-                for (int j = 0; j < kAttnMaxDh / 32; j++) acc[a][j] *= (double)corr;
+                for (int j = 0; j < kAttnMaxDh / 32; j++) {
+                    acc[a][j] *= (double)corr;
+                    acc_b[a][j] *= (double)corr;
+                }
             }
         }
         __syncwarp();
         // ---- P.V: each v element is converted once for all of the warp's heads ----
-        // VEC: a tile's (<= 64) products are summed in fp32 (relative error
-        // ~64 * 2^-24 of the tile's magnitude) and added to the fp64 running
-        // accumulator once per tile, so the long chains stay fp64.
-        float tacc[kHPW][4];
-#pragma unroll
-        for (int a = 0; a < kHPW; a++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) tacc[a][j] = 0.0f;
+        // Products accumulate in fp64 as in the reference (src/sepia.c:1247-
+        // 1252): an fp32 running sum over a tile loses ~1e-7 of its
+        // magnitude per tile, which at 32k keys puts outputs near zero past
+        // the 1e-4 bar. VEC: even and odd rows go to two accumulator sets
+        // (twice the independent fp64 chains), added when the split ends.
         for (int r = 0; r < nt; r++) {
             double pr[kHPW];
-            float pf[kHPW];
 #pragma unroll
             for (int a = 0; a < kHPW; a++) {
                 const int g = warp + kAttnWarps * a;
-                pf[a] = (g < G) ? ss[g * kAttnKT + r] : 0.0f;
-                pr[a] = (double)pf[a];
+                pr[a] = (g < G) ? (double)ss[g * kAttnKT + r] : 0.0;
             }
             if constexpr (VEC) {
                 // lane owns dims 4*lane .. 4*lane+3: one 8- or 16-byte load
                 if (4 * lane < Dh) {
-                    float vf[4];
+                    double vd[4];
                     if constexpr (sizeof(KV) == 2) {
                         const uint2 raw = *reinterpret_cast<const uint2 *>(sv + r * ldk + 4 * lane);
                         const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
                         const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
-                        vf[0] = f0.x; vf[1] = f0.y; vf[2] = f1.x; vf[3] = f1.y;
+                        vd[0] = f0.x; vd[1] = f0.y; vd[2] = f1.x; vd[3] = f1.y;
                     } else {
                         const float4 f = *reinterpret_cast<const float4 *>(sv + r * ldk + 4 * lane);
-                        vf[0] = f.x; vf[1] = f.y; vf[2] = f.z; vf[3] = f.w;
+                        vd[0] = f.x; vd[1] = f.y; vd[2] = f.z; vd[3] = f.w;
                     }
+                    if (r & 1) {
 #pragma unroll
-                    for (int j = 0; j < 4; j++)
+                        for (int jj = 0; jj < 4; jj++)
 #pragma unroll
-                        for (int a = 0; a < kHPW; a++) tacc[a][j] = fmaf(pf[a], vf[j], tacc[a][j]);
+                            for (int a = 0; a < kHPW; a++) acc_b[a][jj] = fma(pr[a], vd[jj], acc_b[a][jj]);
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 4; jj++)
+#pragma unroll
+                            for (int a = 0; a < kHPW; a++) acc[a][jj] = fma(pr[a], vd[jj], acc[a][jj]);
+                    }
                 }
             } else {
 #pragma unroll
-                for (int j = 0; j < kAttnMaxDh / 32; j++) {
-                    const int d = lane + 32 * j;
+                for (int jj = 0; jj < kAttnMaxDh / 32; jj++) {
+                    const int d = lane + 32 * jj;
                     if (d < Dh) {
-                        const double vd = kv_d<KV>(sv + r * ldk + d);
+                        const double vdd = kv_d<KV>(sv + r * ldk + d);
 #pragma unroll
                         for (int a = 0; a < kHPW; a++)
-                            if (warp + kAttnWarps * a < G) acc[a][j] = fma(pr[a], vd, acc[a][j]);
+                            if (warp + kAttnWarps * a < G) acc[a][jj] = fma(pr[a], vdd, acc[a][jj]);
                     }
                 }
             }
-        }
-        if constexpr (VEC) {
-#pragma unroll
-            for (int a = 0; a < kHPW; a++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) acc[a][j] += (double)tacc[a][j];
         }
         __syncthreads();
     }
@@ -320,7 +322,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
 #pragma unroll
             for (int j = 0; j < kAttnMaxDh / 32; j++) {
                 const int d = VEC ? 4 * lane + j : lane + 32 * j;
-                if (d < Dh) pp[2 + d] = acc[a][j];
+                if (d < Dh) pp[2 + d] = acc[a][j] + acc_b[a][j];
             }
         }
     }
@@ -424,20 +426,38 @@ size_t attn_part_bytes(int64_t T, int64_t H, int S, int64_t Dh) {
     return (size_t)T * (size_t)H * (size_t)S * (size_t)(Dh + 2) * sizeof(double);
 }
 
+int launch_banded_attn_ex(int kv_f16, const float *q, const void *k, const void *v, const float *rel_logits,
+                          float *out, const int64_t *kv_lo_d, const int64_t *kv_hi_d, const float *tau_d,
+                          const double *tau64_d, const int32_t *qpos_d, int64_t T, int64_t H, int64_t Hkv,
+                          int64_t Dh, int64_t E, int64_t q_pos_base, int64_t kv_dim, float inv_head_dim, int S,
+                          double *part, cudaStream_t st);
+
 int launch_banded_attn(int kv_f16, const float *q, const void *k, const void *v, const float *rel_logits, float *out,
                        const int64_t *kv_lo_d, const int64_t *kv_hi_d, const float *tau_d, int64_t T, int64_t H,
                        int64_t Hkv, int64_t Dh, int64_t E, int64_t q_pos_base, int64_t kv_dim, float inv_head_dim,
                        int S, double *part, cudaStream_t st) {
+    return launch_banded_attn_ex(kv_f16, q, k, v, rel_logits, out, kv_lo_d, kv_hi_d, tau_d, nullptr, nullptr, T, H,
+                                 Hkv, Dh, E, q_pos_base, kv_dim, inv_head_dim, S, part, st);
+}
+
+// tau64_d / qpos_d (either may be null): tau in double and the position of
+// token 0 read on the device, for decode steps replayed from a CUDA graph.
+int launch_banded_attn_ex(int kv_f16, const float *q, const void *k, const void *v, const float *rel_logits,
+                          float *out, const int64_t *kv_lo_d, const int64_t *kv_hi_d, const float *tau_d,
+                          const double *tau64_d, const int32_t *qpos_d, int64_t T, int64_t H, int64_t Hkv,
+                          int64_t Dh, int64_t E, int64_t q_pos_base, int64_t kv_dim, float inv_head_dim, int S,
+                          double *part, cudaStream_t st) {
     if (T <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || Dh <= 0 || E < 0 || kv_dim < Hkv * Dh)
         return fail("banded_attn: bad geometry T=%lld H=%lld Hkv=%lld Dh=%lld E=%lld kv_dim=%lld", (long long)T,
                     (long long)H, (long long)Hkv, (long long)Dh, (long long)E, (long long)kv_dim);
     if (Dh > kAttnMaxDh) return fail("banded_attn: Dh=%lld exceeds %d", (long long)Dh, kAttnMaxDh);
     if (H / Hkv > kAttnMaxG) return fail("banded_attn: %lld query heads per KV head exceeds %d", (long long)(H / Hkv), kAttnMaxG);
-    if (!q || !k || !v || !out || !kv_lo_d || !kv_hi_d || !tau_d || !part || (E > 0 && !rel_logits))
+    if (!q || !k || !v || !out || !kv_lo_d || !kv_hi_d || (!tau_d && !tau64_d) || !part || (E > 0 && !rel_logits))
         return fail("banded_attn: null pointer");
     if (S < 1) return fail("banded_attn: bad split count");
     AttnParams P;
     P.q = q; P.k = k; P.v = v; P.rel_logits = rel_logits; P.kv_lo = kv_lo_d; P.kv_hi = kv_hi_d; P.tau = tau_d;
+    P.tau64 = tau64_d; P.qpos_dev = qpos_d;
     P.part = part; P.T = T; P.H = H; P.Hkv = Hkv; P.Dh = Dh; P.E = E; P.q_pos_base = q_pos_base; P.kv_dim = kv_dim;
     // The reference scales by 1.0/(double)Dh (src/sepia.c:1217); the ABI
     // carries a float, so a float equal to that value rounded stands for it.

@@ -51,6 +51,30 @@ class SepiaGpuMoeDesc(C.Structure):
                 ("sh_gate_stride", i64), ("sh_up_stride", i64), ("sh_down_stride", i64)]
 
 
+class SepiaQTensor(C.Structure):
+    _fields_ = [("type", i32), ("reserved", i32), ("data", vp), ("rows", i64), ("cols", i64)]
+
+
+class SepiaModelLayer(C.Structure):
+    _fields_ = [("is_sliding", i32), ("is_sparse", i32), ("n_heads", i32), ("n_kv_heads", i32), ("head_dim", i32),
+                ("rel_extent", i32),
+                ("attn_norm", vp), ("mlp_norm", vp), ("q_norm", vp), ("k_norm", vp), ("rel_proj", vp),
+                ("k_sconv", vp), ("v_sconv", vp), ("attn_sconv", vp), ("mlp_sconv", vp),
+                ("wq", SepiaQTensor), ("wk", SepiaQTensor), ("wv", SepiaQTensor), ("wr", SepiaQTensor),
+                ("wo", SepiaQTensor),
+                ("dense_gate", SepiaQTensor), ("dense_up", SepiaQTensor), ("dense_down", SepiaQTensor),
+                ("dense_gscale", C.c_float),
+                ("moe", SepiaMoeLayer)]
+
+
+class SepiaModelDesc(C.Structure):
+    _fields_ = [("hidden", i64), ("n_layers", i32), ("vocab", i32), ("unpadded_vocab", i32), ("d_rel", i32),
+                ("conv_k", i32), ("window", i32), ("max_positions", i32), ("eps", C.c_float), ("mup", C.c_float),
+                ("has_log_scaling", i32), ("log_scaling_alpha", C.c_double), ("log_scaling_n_floor", i64),
+                ("embed", SepiaQTensor), ("unembed", SepiaQTensor), ("embed_norm", vp), ("final_norm", vp),
+                ("layers", C.POINTER(SepiaModelLayer))]
+
+
 # name -> (restype, argtypes)
 _PROTOS = {
     # ---- sepia_gpu.h (reference ABI) ----
@@ -113,6 +137,16 @@ _PROTOS = {
     "sepia_cuda_banded_attn": (C.c_int, [C.c_int, vp, vp, vp, vp, vp, vp, vp, vp] + [i64] * 7 + [C.c_float, i64, vp,
                                                                                                   C.c_size_t, vp]),
     "sepia_cuda_lib_stream": (vp, []),
+    # ---- sepia_model.h (whole-token decode engine) ----
+    "sepia_model_create": (C.c_int, [C.POINTER(SepiaModelDesc), C.POINTER(vp)]),
+    "sepia_model_destroy": (None, [vp]),
+    "sepia_model_device_bytes": (C.c_size_t, [vp]),
+    "sepia_model_reset": (C.c_int, [vp, vp]),
+    "sepia_model_prefill": (C.c_int, [vp, vp, i32, i32, vp]),
+    "sepia_model_decode": (C.c_int, [vp, i32, vp, vp]),
+    "sepia_model_logits": (vp, [vp]),
+    "sepia_model_copy_logits": (C.c_int, [vp, vp, vp]),
+    "sepia_model_position": (C.c_int, [vp, vp]),
     "sepia_cuda_test_engine_timeout": (C.c_int, [C.c_int, vp, vp, vp, i64, i64, C.c_longlong, vp]),
     "sepia_cuda_banded_attn_noalloc_max_bytes": (C.c_size_t, []),
     "sepia_cuda_banded_attn_noalloc": (C.c_int, [C.c_int, vp, vp, vp, vp, vp, vp, vp, vp] + [i64] * 7
@@ -125,7 +159,7 @@ def header_symbols() -> list[str]:
     names = []
     for h in sorted(INCLUDE.glob("*.h")):
         text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
-        names += re.findall(r"\b(sepia_(?:gpu|cuda)_[a-z0-9_]+)\s*\(", text)
+        names += re.findall(r"\b(sepia_(?:gpu|cuda|model)_[a-z0-9_]+)\s*\(", text)
     return sorted(set(names))
 
 
