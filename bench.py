@@ -50,7 +50,11 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--parity", action="store_true", help="check one step against the CPU oracle")
     ap.add_argument("--only", default="", help="kernels workload: run only the lines whose name contains this")
-    ap.add_argument("--workload", default="moe_layer", choices=["moe_layer", "kernels"],
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-5 decode measurement")
+    ap.add_argument("--decode-layers", type=int, default=0, help="config-5 depth (default 24 at N=1, 66 at N>1)")
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--gen", type=int, default=256)
+    ap.add_argument("--workload", default="moe_layer", choices=["moe_layer", "kernels", "decode"],
                     help="moe_layer: the headline line (config 2); kernels: one line per BASELINE config-1/3/4 "
                          "kernel (device time, 1 GPU)")
     return ap.parse_args()
@@ -236,6 +240,67 @@ def committed_traffic():
         return None
 
 
+# ------------------------------------------------------------------ decode
+def decode_measure(args, world, rank, group):
+    """a random-init Inkling-shape model generated
+    in HBM (24-layer truncation on one GPU, all 66 layers when experts are
+    sharded), a 512-token prefill of random ids (seed 7), then 256 greedy
+    decode steps replayed from one CUDA graph per step. Returns a dict (rank
+    0) with decode tok/s, prefill tok/s and the decode HBM roofline."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from sepia_b200 import container as CT
+    from sepia_b200.model import DeviceModel
+    n_layers = args.decode_layers or (24 if world == 1 else 66)
+    tc = CT.config5_text_config(n_layers)
+    cfg = CT.ModelConfig.from_text_config(tc)
+    types = CT.ModelTypes()
+    t0 = time.perf_counter()
+    m = DeviceModel.synthetic(cfg, types, seed=7, max_positions=args.prompt + args.gen + 8, rank=rank, world=world)
+    build_s = time.perf_counter() - t0
+    prompt = np.random.default_rng(7).integers(0, cfg.vocab_size, args.prompt).astype(np.int32)
+    ids = torch.as_tensor(prompt, device="cuda")
+    out = torch.empty(args.gen, dtype=torch.int32, device="cuda")
+    # warm-up: a short sequence (sets kernel attributes, captures the graph)
+    m.reset()
+    m.prefill(ids[:8], True)
+    m.decode(out, 4)
+    torch.cuda.synchronize()
+    m.reset()
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    if world > 1:
+        dist.barrier()
+    clk = Clocks(int(os.environ.get("LOCAL_RANK", "0"))) if rank == 0 else None
+    torch.cuda.synchronize()
+    e0.record()
+    m.prefill(ids, True)
+    e1.record()
+    m.decode(out, args.gen)
+    e2.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop() if clk else None
+    pre_ms, dec_ms = e0.elapsed_time(e1), e1.elapsed_time(e2)
+    if world > 1:
+        t = torch.tensor([pre_ms, dec_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        pre_ms, dec_ms = float(t[0]), float(t[1])
+    tb = CT.token_bytes(cfg, types, args.prompt + args.gen // 2)
+    peak, kind = peak_hbm()
+    dec_tok_s = args.gen / (dec_ms / 1e3)
+    gbs = tb["total"] * dec_tok_s / 1e9
+    res = {"metric": "synthetic Inkling-shape decode tok/s", "value": round(dec_tok_s, 2), "unit": "tok/s",
+           "prefill_tok_s": round(args.prompt / (pre_ms / 1e3), 2), "ms_per_token": round(dec_ms / args.gen, 4),
+           "layers": n_layers, "prompt": args.prompt, "generated": args.gen, "n_gpus": world,
+           "bytes_per_token": tb, "hbm_gbs": round(gbs, 1), "frac_of_measured_peak": round(gbs / peak, 4),
+           "peak_kind": kind, "weights_gb_per_gpu": round(m.weight_bytes() / 1e9, 2), "build_s": round(build_s, 1),
+           "first_ids": out[:8].cpu().tolist(), "graph": "one CUDA graph per decode step",
+           "clocks": clocks}
+    del m
+    torch.cuda.empty_cache()
+    return res
+
+
 # ------------------------------------------------------------------- main
 def kernel_lines(args):
     """Device-timed bandwidth of the other BASELINE kernels on one GPU:
@@ -351,6 +416,14 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     L = LIB.load()
+    if args.workload == "decode":
+        res = decode_measure(args, world, rank, group)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     shape = MoeShape()
     layers = [MoeLayerDevice.random(shape, seed=100 + l, rank=rank, world=world) for l in range(args.layers)]
     X = torch.stack([torch.from_numpy(hidden_state(s, shape.hidden)) for s in range(1, 65)]).cuda()
@@ -437,6 +510,14 @@ def main():
     elif world > 1:
         e2e = sharded_e2e(layers, args, shape, group)
 
+    # ---- config 5: whole-model decode (the layers above are freed first) ----
+    decode = None
+    if not args.no_decode and world == 1:
+        del layers, graphs
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        decode = decode_measure(args, world, rank, group)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         sec, n, sample, sec1 = cpu_token_seconds(shape)
@@ -458,7 +539,7 @@ def main():
                 "pct_of_8tbs": round(100 * gbs / 8000, 2), "pct_of_measured_peak": round(100 * gbs / peak, 2),
                 "layer_steps_per_s": round(args.steps / (ms / 1e3), 1),
                 "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": launches_per_step * args.steps,
-                "clocks": clocks}
+                "clocks": clocks, "decode": decode}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

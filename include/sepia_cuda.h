@@ -160,6 +160,18 @@ int sepia_cuda_banded_attn_noalloc(int kv_f16, const float *q, const void *k, co
                                    int64_t Dh, int64_t rel_extent, int64_t q_pos_base, int64_t kv_dim,
                                    float inv_head_dim, int64_t max_kv, void *stream);
 
+/* ------------------------------------------------------ synthetic weights */
+/* Fills n_units units (unit u at dst + u*unit_stride, blocks_per_unit
+ * blocks of ggml_type each) with seeded random blocks: bytes uniform, every
+ * fp16 scale field (d, dmin) uniform in [d_lo, d_hi]. Unit u's bytes depend
+ * only on (seed, unit_id0 + u*unit_id_step), so a shard holding every
+ * world-th expert gets exactly the bytes those experts have unsharded.
+ * No counterpart in the reference (its models are real checkpoints); used
+ * to build the random-init benchmark models in HBM. */
+int sepia_cuda_fill_blocks(int ggml_type, void *dst, int64_t n_units, int64_t unit_stride, int64_t blocks_per_unit,
+                           uint64_t seed, int64_t unit_id0, int64_t unit_id_step, float d_lo, float d_hi,
+                           void *stream);
+
 /* ---------------------------------------------------------- test hooks */
 /* The stream that the sepia_gpu_* batch API (sepia_gpu.h) enqueues on. */
 void *sepia_cuda_lib_stream(void);

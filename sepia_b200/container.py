@@ -350,6 +350,55 @@ def synth_text_config(hidden=512, n_layers=4, vocab=512, unpadded=500, heads=4, 
         "rms_norm_eps": eps, "log_scaling_alpha": log_alpha, "log_scaling_n_floor": log_floor}
 
 
+def config5_text_config(n_layers: int = 66) -> dict:
+    """the Inkling shape with hidden 7168, 256
+    experts (top 6, 2 shared, ff 2048), 64 query / 8 KV heads of 128 in
+    every layer, sliding window 4096 (every 6th layer global, rel_extent
+    256), the first 2 layers dense, vocabulary 200k. n_layers truncates the
+    66-layer stack (24 on one GPU). Fields the configuration leaves open take
+    the real model's values (d_rel 16, kernel 4, mup 24, eps 1e-6, log
+    scaling alpha 0.1 / floor 128000); the dense width is 4 x 4608."""
+    return {
+        "hidden_size": 7168, "num_hidden_layers": n_layers, "vocab_size": 200064, "unpadded_vocab_size": 200000,
+        "num_attention_heads": 64, "num_key_value_heads": 8, "head_dim": 128,
+        "swa_num_attention_heads": 64, "swa_num_key_value_heads": 8, "swa_head_dim": 128,
+        "sliding_window_size": 4096,
+        "layer_types": ["hybrid" if (i + 1) % 6 == 0 else "hybrid_sliding" for i in range(n_layers)],
+        "mlp_layer_types": ["dense" if i < 2 else "sparse" for i in range(n_layers)],
+        "d_rel": 16, "rel_extent": 256, "conv_kernel_size": 4, "dense_intermediate_size": 18432,
+        "moe_intermediate_size": 2048, "n_routed_experts": 256, "num_experts_per_tok": 6, "n_shared_experts": 2,
+        "route_scale": 8.0, "logits_mup_width_multiplier": 24.0, "rms_norm_eps": 1e-6,
+        "log_scaling_alpha": 0.1, "log_scaling_n_floor": 128000}
+
+
+def token_bytes(cfg: ModelConfig, types: ModelTypes, ctx: int) -> dict:
+    """Algorithmic HBM bytes of one decode token at context ctx, per part:
+    every weight the token reads once (attention projections, router, the
+    top-k routed and all shared experts, dense MLPs, one embedding row, the
+    unpadded logits head) plus the fp32 K/V cache rows attention reads."""
+    H = cfg.hidden_size
+    rb = Q.row_bytes
+    attn = kv = moe = dense = 0
+    for l in range(cfg.num_hidden_layers):
+        nh, nkv, dh = cfg.heads(l)
+        attn += (rb(types.attn, H) * (nh * dh + 2 * nkv * dh + nh * cfg.d_rel) + rb(types.attn, nh * dh) * H
+                 + 4 * cfg.d_rel * cfg.layer_rel_extent(l))
+        span = min(ctx, cfg.sliding_window_size) if cfg.layer_is_sliding[l] else ctx
+        kv += 2 * 4 * nkv * dh * span
+        if cfg.layer_is_sparse[l]:
+            ff = cfg.moe_intermediate_size
+            e = rb(types.gate, H) * ff + rb(types.up, H) * ff + rb(types.down, ff) * H
+            sh = 2 * rb(types.shared, H) * ff + rb(types.shared, ff) * H
+            moe += 4 * (cfg.n_routed_experts + cfg.n_shared_experts) * H + cfg.num_experts_per_tok * e \
+                + cfg.n_shared_experts * sh
+        else:
+            ff = cfg.dense_intermediate_size
+            dense += 2 * rb(types.dense, H) * ff + rb(types.dense, ff) * H
+    head = rb(types.unembed, H) * cfg.unpadded_vocab_size + rb(types.embed, H)
+    return {"attention": attn, "kv_cache": kv, "moe": moe, "dense": dense, "head": head,
+            "total": attn + kv + moe + dense + head}
+
+
 def synth_resident(cfg: ModelConfig, types: ModelTypes, seed: int):
     """name -> (type, shape, uint8 array), seeded. Quantized blocks follow
     BASELINE's distributions (uniform bytes, fp16 scales in [1e-3, 4e-3]);

@@ -137,6 +137,7 @@ _PROTOS = {
     "sepia_cuda_banded_attn": (C.c_int, [C.c_int, vp, vp, vp, vp, vp, vp, vp, vp] + [i64] * 7 + [C.c_float, i64, vp,
                                                                                                   C.c_size_t, vp]),
     "sepia_cuda_lib_stream": (vp, []),
+    "sepia_cuda_fill_blocks": (C.c_int, [C.c_int, vp, i64, i64, i64, C.c_uint64, i64, i64, C.c_float, C.c_float, vp]),
     # ---- sepia_model.h (whole-token decode engine) ----
     "sepia_model_create": (C.c_int, [C.POINTER(SepiaModelDesc), C.POINTER(vp)]),
     "sepia_model_destroy": (None, [vp]),

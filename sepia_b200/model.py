@@ -68,15 +68,19 @@ class DeviceModel:
     @classmethod
     def synthetic(cls, cfg: ModelConfig, types: ModelTypes | None = None, seed: int = 7, max_positions: int = 1024,
                   rank: int = 0, world: int = 1, device="cuda"):
-        """Seeded random weights generated on the GPU in BASELINE's
-        distributions. Every tensor (and every routed expert) has its own
-        generator seed, so a rank's shard does not depend on the world size."""
+        """Seeded random weights generated in HBM in BASELINE's
+        distributions (sepia_cuda_fill_blocks for the quantized tensors).
+        Every tensor and every routed expert has its own unit id, so a rank's
+        shard holds the bytes those experts have on one GPU."""
         types = types or ModelTypes()
         m = cls(cfg, max_positions, rank, world, device)
+        L = load()
+        st = torch.cuda.current_stream(m.device).cuda_stream
         gen = torch.Generator(device=m.device)
-        for i, (name, t, shape) in enumerate(resident_specs(cfg, types)):
-            gen.manual_seed(seed * 1000003 + i)
+        specs = resident_specs(cfg, types)
+        for i, (name, t, shape) in enumerate(specs):
             if t == Q.F32:
+                gen.manual_seed(seed * 1000003 + i)
                 n = int(np.prod(shape))
                 if name.endswith("norm.weight"):
                     v = 1.0 + torch.randn(n, generator=gen, device=m.device) * 0.1
@@ -92,9 +96,13 @@ class DeviceModel:
                     v = torch.randn(n, generator=gen, device=m.device) * 0.1
                 m.t[name] = (t, shape, v.float().contiguous().view(torch.uint8))
             else:
-                nb = tensor_nbytes(t, shape) // Q.block_bytes(t)
-                m.t[name] = (t, shape, synth.blocks_device(gen, t, nb, m.device).contiguous())
-        H, ff = cfg.hidden_size, cfg.moe_intermediate_size
+                nbytes = tensor_nbytes(t, shape)
+                buf = torch.empty(nbytes, dtype=torch.uint8, device=m.device)
+                ok(L.sepia_cuda_fill_blocks(t, buf.data_ptr(), 1, nbytes, nbytes // Q.block_bytes(t), seed, i, 1,
+                                            synth.D_LO, synth.D_HI, st), "fill_blocks")
+                m.t[name] = (t, shape, buf)
+        H, ff, n_e = cfg.hidden_size, cfg.moe_intermediate_size, cfg.n_routed_experts
+        mine = m.owned()
         for l in range(cfg.num_hidden_layers):
             if not cfg.layer_is_sparse[l]:
                 continue
@@ -103,12 +111,13 @@ class DeviceModel:
                                                         ("down", types.down, H, ff)]):
                 nb = Q.row_bytes(t, cols) * rows
                 stride = _pad256(nb)
-                mine = m.owned()
                 buf = torch.zeros(max(1, len(mine)) * stride, dtype=torch.uint8, device=m.device)
-                for i, e in enumerate(mine):
-                    gen.manual_seed(seed * 7919 + (l * 3 + k) * 65537 + e)
-                    buf[i * stride:i * stride + nb] = synth.blocks_device(gen, t, nb // Q.block_bytes(t), m.device)
+                if mine:
+                    base = (1 << 40) + (l * 3 + k) * n_e
+                    ok(L.sepia_cuda_fill_blocks(t, buf.data_ptr(), len(mine), stride, nb // Q.block_bytes(t), seed,
+                                                base + rank, world, synth.D_LO, synth.D_HI, st), "fill_blocks")
                 m.experts[l][slot] = (t, stride, buf)
+        torch.cuda.synchronize(m.device)
         m._build()
         return m
 
