@@ -76,6 +76,9 @@ typedef struct {
     SepiaQTensor embed, unembed;            /* token_embd.weight, output.weight */
     const float *embed_norm, *final_norm;   /* [hidden] */
     const SepiaModelLayer *layers;          /* host array of n_layers */
+    /* expert sharding over the GPUs of one box: this process is rank `rank`
+     * of `world`; every sparse layer's moe must be that rank's shard */
+    int32_t rank, world;
 } SepiaModelDesc;
 
 typedef struct SepiaModel SepiaModel;
@@ -104,6 +107,18 @@ int sepia_model_decode(SepiaModel *m, int32_t n, int32_t *out_ids, void *stream)
 const float *sepia_model_logits(const SepiaModel *m);
 /* Copies the last logits into dst (device, unpadded_vocab floats). */
 int sepia_model_copy_logits(const SepiaModel *m, float *dst, void *stream);
+/* Expert sharding (world > 1). Every rank exports the IPC handle of its
+ * exchange buffers (64 bytes, cudaIpcMemHandle_t) and passes all ranks'
+ * handles, in rank order, to sepia_model_connect before its first token.
+ * Each sparse layer then ends with a one-kernel exchange instead of a
+ * collective: owned slot rows are stored into every rank's buffers over
+ * NVLink, a per-source arrival counter is bumped, and each rank waits
+ * (bounded, ~2 s; on timeout the device error word is set and the layer's
+ * output is left unwritten) before summing the slots in the reference's
+ * order -- bit-identical to one GPU. No counterpart in the reference (its
+ * expert store is one process on one GPU, src/sepia.c:2216-2470). */
+int sepia_model_exchange_handle(SepiaModel *m, void *handle);
+int sepia_model_connect(SepiaModel *m, const void *handles);
 /* Position of the next token (synchronises `stream`). */
 int sepia_model_position(SepiaModel *m, void *stream);
 

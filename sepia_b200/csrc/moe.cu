@@ -921,7 +921,7 @@ static int launch_gateup_engine(const MoeDev &L, const float *x, const SepiaMoeW
                  "moe gate/up (tensor cores) launch");
 }
 
-static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *out, float *slots_out,
+static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *out, float *slots_out, bool clear,
                               cudaStream_t st) {
     DevInfo &di = dev_info();
     DnJob J;
@@ -948,7 +948,7 @@ static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *ou
     P.err = di.err;
     const void *fn = (const void *)k_qengine<DnJob>;
     if (!ensure_smem(fn, (int)smem)) return 0;
-    if (slots_out &&
+    if (slots_out && clear &&
         !check(cudaMemsetAsync(slots_out, 0, (size_t)J.n_slots * L.hidden * sizeof(float), st), "moe slot clear"))
         return 0;
     // the down projections (each CTA builds the h tables it reads), then
@@ -1007,8 +1007,11 @@ int launch_gateup(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaS
 }
 
 // The down engine reads the h tables that only the gate/up engine builds.
-int launch_down(const MoeDev &L, const SepiaMoeWork *ws, float *out, float *slots_out, cudaStream_t st) {
-    if (engine_gateup_ok(L, ws) && engine_down_ok(L, ws)) return launch_down_engine(L, ws, out, slots_out, st);
+// clear: zero the slot buffer first (slots other ranks own stay zero, as a
+// sum all-reduce of the buffer needs); an owner-only exchange skips it.
+int launch_down(const MoeDev &L, const SepiaMoeWork *ws, float *out, float *slots_out, cudaStream_t st,
+                bool clear = true) {
+    if (engine_gateup_ok(L, ws) && engine_down_ok(L, ws)) return launch_down_engine(L, ws, out, slots_out, clear, st);
     DevInfo &di = dev_info();
     const int n_slots = L.topk + L.n_shared;
     DnParams D;
@@ -1086,6 +1089,18 @@ extern "C" int sepia_cuda_moe_router(const SepiaMoeLayer *Lh, const float *x, co
     if (!x || !ws) return fail("moe_router: null argument");
     return launch_router(L, x, ws, as_stream(stream));
 }
+
+namespace sepia {
+// Router already run: every slot this rank owns gets its term in ws->slots
+// (other slots are left as they are); for an exchange that moves owned rows
+// only (csrc/model.cu).
+int moe_experts_owned_slots(const SepiaMoeLayer *Lh, const float *x, const SepiaMoeWork *ws, cudaStream_t st) {
+    MoeDev L;
+    if (!to_dev(Lh, L)) return 0;
+    if (!x || !ws) return fail("moe_experts: null argument");
+    return launch_gateup(L, x, ws, st) && launch_down(L, ws, nullptr, ws->slots, st, false);
+}
+}  // namespace sepia
 
 extern "C" int sepia_cuda_moe_experts(const SepiaMoeLayer *Lh, const float *x, const SepiaMoeWork *ws, float *out,
                                       int write_slots, void *stream) {

@@ -72,7 +72,7 @@ class SepiaModelDesc(C.Structure):
                 ("conv_k", i32), ("window", i32), ("max_positions", i32), ("eps", C.c_float), ("mup", C.c_float),
                 ("has_log_scaling", i32), ("log_scaling_alpha", C.c_double), ("log_scaling_n_floor", i64),
                 ("embed", SepiaQTensor), ("unembed", SepiaQTensor), ("embed_norm", vp), ("final_norm", vp),
-                ("layers", C.POINTER(SepiaModelLayer))]
+                ("layers", C.POINTER(SepiaModelLayer)), ("rank", i32), ("world", i32)]
 
 
 # name -> (restype, argtypes)
@@ -147,6 +147,8 @@ _PROTOS = {
     "sepia_model_decode": (C.c_int, [vp, i32, vp, vp]),
     "sepia_model_logits": (vp, [vp]),
     "sepia_model_copy_logits": (C.c_int, [vp, vp, vp]),
+    "sepia_model_exchange_handle": (C.c_int, [vp, vp]),
+    "sepia_model_connect": (C.c_int, [vp, vp]),
     "sepia_model_position": (C.c_int, [vp, vp]),
     "sepia_cuda_test_engine_timeout": (C.c_int, [C.c_int, vp, vp, vp, i64, i64, C.c_longlong, vp]),
     "sepia_cuda_banded_attn_noalloc_max_bytes": (C.c_size_t, []),

@@ -200,6 +200,7 @@ class DeviceModel:
         d.embed, d.unembed = self._q("token_embd.weight"), self._q("output.weight")
         d.embed_norm, d.final_norm = self._f("token_embd_norm.weight"), self._f("output_norm.weight")
         d.layers = self._layers
+        d.rank, d.world = self.rank, self.world
         self._desc = d
         h = C.c_void_p()
         ok(L.sepia_model_create(C.byref(d), C.byref(h)), "model_create")
@@ -212,6 +213,20 @@ class DeviceModel:
             except Exception:
                 pass
             self._h = None
+
+    def connect(self, group=None):
+        """Expert sharding: all-gathers every rank's exchange-buffer IPC
+        handle over torch.distributed (host objects only) and opens the
+        peers' buffers. Call once on every rank before the first token."""
+        if self.world == 1:
+            return
+        import torch.distributed as dist
+        h = (C.c_char * 64)()
+        ok(load().sepia_model_exchange_handle(self._h, h), "model_exchange_handle")
+        allh = [None] * self.world
+        dist.all_gather_object(allh, bytes(h), group=group)
+        buf = (C.c_char * (64 * self.world)).from_buffer_copy(b"".join(allh))
+        ok(load().sepia_model_connect(self._h, buf), "model_connect")
 
     # --------------------------------------------------------------- run
     def _st(self, stream=None) -> int:
