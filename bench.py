@@ -258,6 +258,7 @@ def decode_measure(args, world, rank, group):
     types = CT.ModelTypes()
     t0 = time.perf_counter()
     m = DeviceModel.synthetic(cfg, types, seed=7, max_positions=args.prompt + args.gen + 8, rank=rank, world=world)
+    m.connect(group)
     build_s = time.perf_counter() - t0
     prompt = np.random.default_rng(7).integers(0, cfg.vocab_size, args.prompt).astype(np.int32)
     ids = torch.as_tensor(prompt, device="cuda")
@@ -426,6 +427,13 @@ def main():
         return
     shape = MoeShape()
     layers = [MoeLayerDevice.random(shape, seed=100 + l, rank=rank, world=world) for l in range(args.layers)]
+    if world > 1:
+        # one NVLink slot exchange per rank, shared by the layer instances
+        from sepia_b200.moe import Exchange
+        xchg = Exchange(shape.topk + shape.n_shared, shape.hidden, rank, world)
+        xchg.connect(group)
+        for D in layers:
+            D.exchange = xchg
     X = torch.stack([torch.from_numpy(hidden_state(s, shape.hidden)) for s in range(1, 65)]).cuda()
     out = torch.empty(shape.hidden, dtype=torch.float32, device="cuda")
     torch.cuda.synchronize()
@@ -434,10 +442,11 @@ def main():
         layers[i % len(layers)].forward(X[i % 64], out, group=group)
 
     # Decode runs a layer as one CUDA graph (router, gate/up, down, combine
-    # replayed without host launch gaps). One graph per layer instance, each
-    # with its own resident input; eager launches for the sharded path.
+    # -- or, sharded, the NVLink slot exchange -- replayed without host
+    # launch gaps). One graph per layer instance, each with its own resident
+    # input.
     graphs = []
-    if world == 1 and not args.no_graph:
+    if not args.no_graph:
         xin = X[:len(layers)].clone()
         outs = torch.empty(len(layers), shape.hidden, dtype=torch.float32, device="cuda")
         for l, D in enumerate(layers):      # warm: kernel attributes set before capture
@@ -479,7 +488,7 @@ def main():
         ms = float(t.item())
     tok_bytes = shape.token_bytes()
     gbs = args.steps * tok_bytes / (ms / 1e3) / 1e9
-    launches_per_step = 4   # router, gate/up, down, combine (N > 1: the all-reduce is NCCL's)
+    launches_per_step = 4   # router, gate/up, down, then combine (N = 1) or the NVLink slot exchange (N > 1)
 
     # ---- per-kernel live timing (same workload, events between launches) ----
     kt = per_kernel_times(layers, X, args, world, group)
@@ -512,7 +521,7 @@ def main():
 
     # ---- config 5: whole-model decode (the layers above are freed first) ----
     decode = None
-    if not args.no_decode and world == 1:
+    if not args.no_decode:
         del layers, graphs
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
@@ -659,8 +668,8 @@ def abi_e2e(layers, args, shape):
 
 def sharded_e2e(layers, args, shape, group):
     """N > 1: pinned host x -> device, the sharded layer (router, own experts,
-    NCCL all-reduce of slot terms, combine), device -> pinned host output;
-    wall clock per step, max over ranks."""
+    NVLink slot exchange + combine), device -> pinned host output; wall clock
+    per step, max over ranks."""
     import torch
     import torch.distributed as dist
     from sepia_b200.synth import hidden_state
@@ -688,7 +697,7 @@ def sharded_e2e(layers, args, shape, group):
     return {"value": round(args.steps * s.token_bytes() / dt / 1e9, 1), "unit": "GB/s",
             "h2d_bytes_per_step": s.hidden * 4, "d2h_bytes_per_step": s.hidden * 4,
             "ms_per_step": round(1e3 * dt / args.steps, 4), "tok_s": round(args.steps / dt, 1),
-            "path": "raw entry points + torch.distributed NCCL all-reduce"}
+            "path": "sepia_cuda_moe_layer_sharded (router, owned experts, one-kernel NVLink slot exchange)"}
 
 
 def parity_check(D, x):

@@ -122,6 +122,35 @@ int sepia_cuda_moe_layer(const SepiaMoeLayer *L, const float *x, const SepiaMoeW
  * (src/sepia.c:1336-1347; lowest index wins ties). */
 int sepia_cuda_topk_select(const float *scores, int32_t n, int32_t topk, int32_t *idx, void *stream);
 
+/* ------------------------------------------- expert-sharded exchange */
+/* With experts sharded by index over the GPUs of one box (one process per
+ * GPU, routed expert e on rank e % world, shared expert s on rank
+ * s % world), every rank computes the same router and only the slot terms
+ * it owns. The exchange replaces the collective with one kernel: owned slot
+ * rows are stored into every rank's receive buffer through peer mappings
+ * (NVLink), a per-source arrival counter is bumped on every rank, each rank
+ * waits until all sources arrived (bounded, about 2 s; on timeout the device
+ * error word is set and `out` is left unwritten) and sums the slots in the
+ * reference's combine order, so the result is bit-identical to one GPU.
+ * No counterpart in the reference (its expert store is one process on one
+ * GPU, src/sepia.c:2216-2470; combine order src/sepia.c:1420-1466).
+ * Setup: create on every rank, export the 64-byte IPC handle
+ * (cudaIpcMemHandle_t), gather all ranks' handles in rank order by any host
+ * channel, connect. Every rank must then run the same sequence of
+ * exchanges; calls are stream-ordered and may be captured in CUDA graphs. */
+typedef struct SepiaExchange SepiaExchange;
+int sepia_cuda_exchange_create(int32_t n_slots, int64_t hidden, int32_t rank, int32_t world, SepiaExchange **out);
+void sepia_cuda_exchange_destroy(SepiaExchange *x);
+int sepia_cuda_exchange_handle(SepiaExchange *x, void *handle);
+int sepia_cuda_exchange_connect(SepiaExchange *x, const void *handles);
+/* out = combine of every rank's owned slot terms in ws->slots (after
+ * sepia_cuda_moe_router + the owned-slot experts). */
+int sepia_cuda_moe_exchange(SepiaExchange *x, const SepiaMoeLayer *L, const SepiaMoeWork *ws, float *out,
+                            void *stream);
+/* Router + this rank's experts + exchange: one sharded MoE layer. */
+int sepia_cuda_moe_layer_sharded(SepiaExchange *x, const SepiaMoeLayer *L, const float *xin, const SepiaMoeWork *ws,
+                                 float *out, void *stream);
+
 /* ------------------------------------------------- banded attention */
 /* rel_logits[t,h,r] = sum_d r_vec[t,h,d] * rel_proj[d,r] (src/sepia.c:1201-1208) */
 int sepia_cuda_rel_project(const float *r_vec, const float *rel_proj, float *rel_logits,

@@ -38,7 +38,6 @@ int launch_banded_attn_ex(int kv_f16, const float *q, const void *k, const void 
 int attn_splits(int64_t T, int64_t Hkv, int64_t max_n);
 size_t attn_part_bytes(int64_t T, int64_t H, int S, int64_t Dh);
 int op_silu_mul(const float *g, const float *u, float *z, int64_t n, cudaStream_t st);
-int moe_experts_owned_slots(const SepiaMoeLayer *Lh, const float *x, const SepiaMoeWork *ws, cudaStream_t st);
 
 constexpr int kMaxConvK = 16;
 constexpr int kResThreads = 1024;
@@ -50,7 +49,6 @@ struct ModelState {
     int32_t fed;               // teacher-forced tokens consumed by the current prefill
     int32_t gen;               // generated tokens written by decode steps
     int32_t bad_token;         // set when an input token id is out of range
-    int32_t xchg;              // expert-sharded exchanges completed (same on every rank)
     int64_t kv_lo, kv_hi;      // attention range of the current token (this layer)
     double tau;                // tau of the current token (this layer)
 };
@@ -230,7 +228,6 @@ struct ResArgs {
     float *xn;
     ModelState *st;
     int advance;                // pos += 1 at the end
-    int bump_xchg;              // st->xchg += 1 at the end (after a sharded MoE layer)
 };
 
 // x += sconv(in) (src/sepia.c:1506-1519, 1535-1549) then xn = rmsnorm(x)
@@ -252,10 +249,7 @@ __global__ void __launch_bounds__(kResThreads) k_residual(const ResArgs A) {
         if (A.mup > 0.0f) v = __fdiv_rn(v, A.mup);
         A.xn[c] = v;
     }
-    if (threadIdx.x == 0) {
-        if (A.advance) A.st->pos += 1;
-        if (A.bump_xchg) A.st->xchg += 1;
-    }
+    if (A.advance && threadIdx.x == 0) A.st->pos += 1;
 }
 
 // ---------------------------------------------------------------- argmax
@@ -290,104 +284,6 @@ __global__ void __launch_bounds__(256) k_argmax(const float *logits, int32_t n, 
         for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = sh[w] > best ? sh[w] : best;
         atomicMax(&st->best, best);
         if (advance && blockIdx.x == 0) st->pos += 1;
-    }
-}
-
-// ---------------------------------------------- expert-sharded exchange
-// After each rank computed the terms of the MoE slots it owns (routed slot
-// j: expert idx[j] on rank idx[j] % world; shared slot s on rank
-// s % world), every rank stores its owned rows into every rank's receive
-// buffer (plain stores through peer mappings over NVLink; no TMA, no
-// multicast), bumps a per-source arrival counter on each rank, waits until
-// every source has arrived for this exchange (bounded), and sums the slots
-// in the reference's order (routed j = 0..k-1, then shared): the same bits
-// as one GPU, since each slot has exactly one writer and x + 0 is never
-// formed. Exchange e (1-based, the same sequence on every rank) uses
-// buffer e & 1: a rank can only write buffer e & 1 again at exchange e + 2,
-// after every rank arrived at e + 1, i.e. after it finished reading e.
-constexpr int kXchgCtas = 16;
-constexpr int kXchgThreads = 256;
-
-struct XchgArgs {
-    const float *slots;                  // this rank's slot terms [n_slots, hidden]
-    const int32_t *topk_idx;
-    int topk, n_shared, n_routed;
-    int64_t hidden;
-    int rank, world;
-    float *const *peer_recv;             // [world] receive bases (2 buffers each)
-    unsigned long long *const *peer_cnt; // [world] counter arrays ([world] each)
-    const float *my_recv;
-    unsigned long long *my_cnt;
-    ModelState *st;
-    float *out;
-    int *err;
-    long long spin_limit;
-};
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsigned long long v) {
-    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__global__ void __launch_bounds__(kXchgThreads) k_exchange(const XchgArgs A) {
-    __shared__ int owned[32];
-    __shared__ int n_owned, ok_sh;
-    const unsigned long long e = (unsigned long long)A.st->xchg + 1ull;
-    const int buf = (int)(e & 1ull);
-    const int n_slots = A.topk + A.n_shared;
-    if (threadIdx.x == 0) {
-        int n = 0;
-        for (int j = 0; j < A.topk; j++) {
-            const int ex = A.topk_idx[j];
-            if (ex >= 0 && ex < A.n_routed && ex % A.world == A.rank) owned[n++] = j;
-        }
-        for (int s2 = 0; s2 < A.n_shared; s2++)
-            if (s2 % A.world == A.rank) owned[n++] = A.topk + s2;
-        n_owned = n;
-        ok_sh = 1;
-    }
-    __syncthreads();
-    // this CTA's columns of every owned row, to every rank
-    const int64_t per = (A.hidden + gridDim.x - 1) / gridDim.x;
-    const int64_t c0 = (int64_t)blockIdx.x * per, c1 = imin64(A.hidden, c0 + per);
-    for (int k = 0; k < n_owned; k++) {
-        const int sl = owned[k];
-        const float *src = A.slots + (int64_t)sl * A.hidden;
-        for (int p = 0; p < A.world; p++) {
-            float *dst = A.peer_recv[p] + ((int64_t)buf * n_slots + sl) * A.hidden;
-            for (int64_t c = c0 + threadIdx.x; c < c1; c += blockDim.x) dst[c] = src[c];
-        }
-    }
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0)
-        for (int p = 0; p < A.world; p++) red_release_sys_add(A.peer_cnt[p] + A.rank, 1ull);
-    // wait for every source's CTAs of this exchange
-    if (threadIdx.x == 0) {
-        const unsigned long long want = e * (unsigned long long)gridDim.x;
-        for (int src = 0; src < A.world && ok_sh; src++) {
-            long long spins = 0;
-            while (ld_acquire_sys(A.my_cnt + src) < want) {
-                if (++spins > A.spin_limit) {
-                    set_error(A.err, kErrWaitTimeout);
-                    ok_sh = 0;
-                    break;
-                }
-                __nanosleep(200);
-            }
-        }
-    }
-    __syncthreads();
-    if (!ok_sh) return;
-    const float *rb = A.my_recv + (int64_t)buf * n_slots * A.hidden;
-    for (int64_t c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
-        float o = 0.0f;
-        for (int sl = 0; sl < n_slots; sl++) o = __fadd_rn(o, __ldcg(rb + (int64_t)sl * A.hidden + c));
-        A.out[c] = o;
     }
 }
 
@@ -432,14 +328,7 @@ struct SepiaModel {
     int32_t *graph_out = nullptr;    // out_ids array baked into the graph
     // expert sharding (world > 1)
     int rank = 0, world = 1;
-    void *xchg_mem = nullptr;        // recv[2][n_slots][hidden] floats, then counters[world]
-    float *recv = nullptr;
-    unsigned long long *cnt = nullptr;
-    float **peer_recv = nullptr;     // device arrays [world]
-    unsigned long long **peer_cnt = nullptr;
-    std::vector<void *> opened;      // peer mappings to close
-    bool connected = false;
-    int n_slots = 0;
+    SepiaExchange *xchg = nullptr;   // the sharded MoE layers' exchange
 };
 
 namespace {
@@ -490,21 +379,11 @@ int run_layers(SepiaModel *m, bool want_logits, cudaStream_t st) {
         ResArgs R;
         R.x = m->x; R.in = m->blk; R.scale = 1.0f; R.use_scale = 0; R.w = L.attn_sconv; R.hist = m->ah[l];
         R.C = hidden; R.K = K; R.norm_w = L.mlp_norm; R.eps = d.eps; R.mup = 0.0f; R.xn = m->xn; R.st = m->st;
-        R.advance = 0; R.bump_xchg = 0;
+        R.advance = 0;
         k_residual<<<1, kResThreads, hidden * sizeof(float), st>>>(R);
         if (!check(cudaGetLastError(), "model: residual launch")) return 0;
         if (L.is_sparse && m->world > 1) {
-            if (!m->connected) return fail("model: world %d needs sepia_model_connect first", m->world);
-            if (!sepia_cuda_moe_router(&L.moe, m->xn, &m->ws, (void *)st)) return 0;
-            if (!moe_experts_owned_slots(&L.moe, m->xn, &m->ws, st)) return 0;
-            XchgArgs X;
-            X.slots = m->ws.slots; X.topk_idx = m->ws.topk_idx;
-            X.topk = L.moe.topk; X.n_shared = L.moe.n_shared; X.n_routed = L.moe.n_routed; X.hidden = hidden;
-            X.rank = m->rank; X.world = m->world; X.peer_recv = m->peer_recv; X.peer_cnt = m->peer_cnt;
-            X.my_recv = m->recv; X.my_cnt = m->cnt; X.st = m->st; X.out = m->blk; X.err = dev_info().err;
-            X.spin_limit = 10000000;
-            k_exchange<<<kXchgCtas, kXchgThreads, 0, st>>>(X);
-            if (!check(cudaGetLastError(), "model: exchange launch")) return 0;
+            if (!sepia_cuda_moe_layer_sharded(m->xchg, &L.moe, m->xn, &m->ws, m->blk, (void *)st)) return 0;
         } else if (L.is_sparse) {
             if (!sepia_cuda_moe_layer(&L.moe, m->xn, &m->ws, m->blk, (void *)st)) return 0;
         } else {
@@ -519,7 +398,6 @@ int run_layers(SepiaModel *m, bool want_logits, cudaStream_t st) {
         R.norm_w = last ? d.final_norm : m->layers[l + 1].attn_norm;
         R.mup = last ? d.mup : 0.0f;
         R.advance = (last && !want_logits) ? 1 : 0;
-        R.bump_xchg = (L.is_sparse && m->world > 1) ? 1 : 0;
         k_residual<<<1, kResThreads, hidden * sizeof(float), st>>>(R);
         if (!check(cudaGetLastError(), "model: residual launch")) return 0;
     }
@@ -620,17 +498,10 @@ extern "C" int sepia_model_create(const SepiaModelDesc *d, SepiaModel **out) {
                 delete m;
                 return 0;
             }
-        m->n_slots = moe0->topk + moe0->n_shared;
-        const size_t rb = align256(sizeof(float) * 2 * (size_t)m->n_slots * (size_t)hidden);
-        const size_t bytes = rb + align256(sizeof(unsigned long long) * m->world);
-        if (!check(cudaMalloc(&m->xchg_mem, bytes), "model: exchange buffers") ||
-            !check(cudaMemset(m->xchg_mem, 0, bytes), "model: exchange clear")) {
-            if (m->xchg_mem) cudaFree(m->xchg_mem);
+        if (!sepia_cuda_exchange_create(moe0->topk + moe0->n_shared, hidden, m->rank, m->world, &m->xchg)) {
             delete m;
             return 0;
         }
-        m->recv = (float *)m->xchg_mem;
-        m->cnt = (unsigned long long *)((char *)m->xchg_mem + rb);
     }
     // carve one allocation
     const int64_t cap = d->max_positions;
@@ -667,7 +538,7 @@ extern "C" int sepia_model_create(const SepiaModelDesc *d, SepiaModel **out) {
     }
     size_t total = 0;
     for (auto &p : plan) total += p.second;
-    if (!check(cudaMalloc(&m->mem, total), "model: cudaMalloc")) { delete m; return 0; }
+    if (!check(cudaMalloc(&m->mem, total), "model: cudaMalloc")) { sepia_model_destroy(m); return 0; }
     m->mem_bytes = total;
     size_t off = 0;
     for (auto &p : plan) { *p.first = (char *)m->mem + off; off += p.second; }
@@ -696,52 +567,18 @@ extern "C" void sepia_model_destroy(SepiaModel *m) {
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
     if (m->mem) cudaFree(m->mem);
-    for (void *p : m->opened) cudaIpcCloseMemHandle(p);
-    if (m->peer_recv) cudaFree(m->peer_recv);
-    if (m->xchg_mem) cudaFree(m->xchg_mem);
+    if (m->xchg) sepia_cuda_exchange_destroy(m->xchg);
     delete m;
 }
 
 extern "C" int sepia_model_exchange_handle(SepiaModel *m, void *handle) {
-    if (!m || !handle) return fail("model: exchange_handle needs a model and an output");
-    if (!m->xchg_mem) return fail("model: no exchange buffers (world 1 or no MoE layer)");
-    cudaIpcMemHandle_t h;
-    if (!check(cudaIpcGetMemHandle(&h, m->xchg_mem), "model: cudaIpcGetMemHandle")) return 0;
-    memcpy(handle, &h, sizeof h);
-    return 1;
+    if (!m || !m->xchg) return fail("model: no exchange (world 1 or no MoE layer)");
+    return sepia_cuda_exchange_handle(m->xchg, handle);
 }
 
 extern "C" int sepia_model_connect(SepiaModel *m, const void *handles) {
-    if (!m || !handles) return fail("model: connect needs handles");
-    if (!m->xchg_mem) return fail("model: no exchange buffers (world 1 or no MoE layer)");
-    if (m->connected) return 1;
-    const size_t rb = align256(sizeof(float) * 2 * (size_t)m->n_slots * (size_t)m->d.hidden);
-    std::vector<float *> recv(m->world);
-    std::vector<unsigned long long *> cnt(m->world);
-    for (int p = 0; p < m->world; p++) {
-        void *base = nullptr;
-        if (p == m->rank) {
-            base = m->xchg_mem;
-        } else {
-            cudaIpcMemHandle_t h;
-            memcpy(&h, (const char *)handles + (size_t)p * sizeof h, sizeof h);
-            if (!check(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess), "model: cudaIpcOpenMemHandle"))
-                return 0;
-            m->opened.push_back(base);
-        }
-        recv[p] = (float *)base;
-        cnt[p] = (unsigned long long *)((char *)base + rb);
-    }
-    void *arr = nullptr;
-    const size_t n = sizeof(void *) * (size_t)m->world;
-    if (!check(cudaMalloc(&arr, 2 * n), "model: peer tables")) return 0;
-    m->peer_recv = (float **)arr;
-    m->peer_cnt = (unsigned long long **)((char *)arr + n);
-    if (!check(cudaMemcpy(m->peer_recv, recv.data(), n, cudaMemcpyHostToDevice), "model: peer table upload") ||
-        !check(cudaMemcpy(m->peer_cnt, cnt.data(), n, cudaMemcpyHostToDevice), "model: peer table upload"))
-        return 0;
-    m->connected = true;
-    return 1;
+    if (!m || !m->xchg) return fail("model: no exchange (world 1 or no MoE layer)");
+    return sepia_cuda_exchange_connect(m->xchg, handles);
 }
 
 extern "C" size_t sepia_model_device_bytes(const SepiaModel *m) { return m ? m->mem_bytes : 0; }

@@ -137,6 +137,12 @@ _PROTOS = {
     "sepia_cuda_banded_attn": (C.c_int, [C.c_int, vp, vp, vp, vp, vp, vp, vp, vp] + [i64] * 7 + [C.c_float, i64, vp,
                                                                                                   C.c_size_t, vp]),
     "sepia_cuda_lib_stream": (vp, []),
+    "sepia_cuda_exchange_create": (C.c_int, [i32, i64, i32, i32, C.POINTER(vp)]),
+    "sepia_cuda_exchange_destroy": (None, [vp]),
+    "sepia_cuda_exchange_handle": (C.c_int, [vp, vp]),
+    "sepia_cuda_exchange_connect": (C.c_int, [vp, vp]),
+    "sepia_cuda_moe_exchange": (C.c_int, [vp, C.POINTER(SepiaMoeLayer), C.POINTER(SepiaMoeWork), vp, vp]),
+    "sepia_cuda_moe_layer_sharded": (C.c_int, [vp, C.POINTER(SepiaMoeLayer), vp, C.POINTER(SepiaMoeWork), vp, vp]),
     "sepia_cuda_fill_blocks": (C.c_int, [C.c_int, vp, i64, i64, i64, C.c_uint64, i64, i64, C.c_float, C.c_float, vp]),
     # ---- sepia_model.h (whole-token decode engine) ----
     "sepia_model_create": (C.c_int, [C.POINTER(SepiaModelDesc), C.POINTER(vp)]),

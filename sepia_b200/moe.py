@@ -30,6 +30,37 @@ def owned_shared(n_shared: int, rank: int, world: int) -> list[int]:
     return [s for s in range(n_shared) if s % world == rank]
 
 
+class Exchange:
+    """The expert-sharded exchange of one rank (sepia_cuda_exchange_*): one
+    kernel stores this rank's slot terms into every rank's buffers over
+    NVLink and combines them; replaces the NCCL all-reduce of the slots."""
+
+    def __init__(self, n_slots: int, hidden: int, rank: int, world: int):
+        self.rank, self.world = rank, world
+        h = C.c_void_p()
+        ok(load().sepia_cuda_exchange_create(n_slots, hidden, rank, world, C.byref(h)), "exchange_create")
+        self.h = h
+
+    def connect(self, group=None):
+        """Gathers every rank's 64-byte IPC handle over torch.distributed (a
+        host object all-gather) and opens the peers' buffers."""
+        import torch.distributed as dist
+        mine = (C.c_char * 64)()
+        ok(load().sepia_cuda_exchange_handle(self.h, mine), "exchange_handle")
+        allh = [None] * self.world
+        dist.all_gather_object(allh, bytes(mine), group=group)
+        buf = (C.c_char * (64 * self.world)).from_buffer_copy(b"".join(allh))
+        ok(load().sepia_cuda_exchange_connect(self.h, buf), "exchange_connect")
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            try:
+                load().sepia_cuda_exchange_destroy(self.h)
+            except Exception:
+                pass
+            self.h = None
+
+
 class MoeLayerDevice:
     """One layer's weights on this GPU (this rank's shard) plus scratch."""
 
@@ -148,13 +179,18 @@ class MoeLayerDevice:
         return self._struct
 
     def forward(self, x: torch.Tensor, out: torch.Tensor, stream=None, group=None) -> torch.Tensor:
-        """out[hidden] = MoE(x[hidden]) on this rank; for world > 1 the slot
-        terms are all-reduced over `group` (torch.distributed, NCCL)."""
+        """out[hidden] = MoE(x[hidden]) on this rank. For world > 1 the slot
+        terms are combined through self.exchange (an Exchange, set by the
+        caller) when present, else all-reduced over `group` with NCCL."""
         L = load()
         st = (stream or torch.cuda.current_stream()).cuda_stream
         Ls, ws = C.byref(self._struct), C.byref(self.ws)
         if self.world == 1:
             ok(L.sepia_cuda_moe_layer(Ls, x.data_ptr(), ws, out.data_ptr(), st), "moe_layer")
+            return out
+        if getattr(self, "exchange", None) is not None:
+            ok(L.sepia_cuda_moe_layer_sharded(self.exchange.h, Ls, x.data_ptr(), ws, out.data_ptr(), st),
+               "moe_layer_sharded")
             return out
         import torch.distributed as dist
         ok(L.sepia_cuda_moe_router(Ls, x.data_ptr(), ws, st), "moe_router")
