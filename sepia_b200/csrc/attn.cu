@@ -76,6 +76,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(const AttnParams P)
     float *sml = ss + G * kAttnKT;                               // [G][2] running m, l
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    griddep_wait();
+    griddep_launch();
     const int64_t lo = P.kv_lo[t], hi = P.kv_hi[t];
     const int64_t n = hi - lo + 1;
     const int64_t chunk = (n + P.S - 1) / P.S;
@@ -339,8 +341,7 @@ static int attn_launch_g(const AttnParams &P, size_t smem, cudaStream_t st) {
     const void *fn = (const void *)k_attn_split<KV, VEC, GM>;
     if (!ensure_smem(fn, (int)smem)) return 0;
     dim3 grid((unsigned)P.S, (unsigned)P.Hkv, (unsigned)P.T);
-    k_attn_split<KV, VEC, GM><<<grid, kAttnThreads, smem, st>>>(P);
-    return check(cudaGetLastError(), "banded_attn launch");
+    return check(launch_pdl(k_attn_split<KV, VEC, GM>, grid, dim3(kAttnThreads), smem, st, P), "banded_attn launch");
 }
 
 template <typename KV, bool VEC>
@@ -365,6 +366,8 @@ static int attn_launch_split(const AttnParams &P, int G, cudaStream_t st) {
 constexpr int kAttnMaxSplits = 256;
 __global__ void k_attn_combine(const double *part, float *out, int64_t TH, int S, int64_t Dh) {
     const int64_t th = blockIdx.x;
+    griddep_wait();
+    griddep_launch();
     if (th >= TH) return;
     __shared__ double s_w[kAttnMaxSplits];
     __shared__ double s_M, s_L;
@@ -406,6 +409,8 @@ __global__ void k_attn_combine(const double *part, float *out, int64_t TH, int S
 __global__ void k_rel_project(const float *r_vec, const float *rel_proj, float *rel_logits, int64_t TH,
                               int64_t d_rel, int64_t E) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    griddep_wait();
+    griddep_launch();
     if (i >= TH * E) return;
     const int64_t th = i / E, r = i % E;
     const float *rv = r_vec + th * d_rel;
@@ -466,7 +471,9 @@ int launch_banded_attn_ex(int kv_f16, const float *q, const void *k, const void 
     P.S = S; P.max_chunk = 0;
     const int G = (int)(H / Hkv);
     if (!(kv_f16 ? attn_launch_split<__half>(P, G, st) : attn_launch_split<float>(P, G, st))) return 0;
-    k_attn_combine<<<(unsigned)(T * H), 128, 0, st>>>(part, out, T * H, S, Dh);
+    if (!check(launch_pdl(k_attn_combine, (unsigned)(T * H), 128, 0, st, (const double *)part, out, T * H, S, Dh),
+               "banded_attn combine launch"))
+        return 0;
     return check(cudaGetLastError(), "banded_attn combine launch");
 }
 
@@ -475,7 +482,9 @@ int launch_rel_project(const float *r_vec, const float *rel_proj, float *rel_log
     if (T <= 0 || H <= 0 || d_rel <= 0 || E <= 0 || !r_vec || !rel_proj || !rel_logits)
         return fail("rel_project: bad arguments");
     const int64_t n = T * H * E;
-    k_rel_project<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(r_vec, rel_proj, rel_logits, T * H, d_rel, E);
+    if (!check(launch_pdl(k_rel_project, (unsigned)((n + 255) / 256), 256, 0, st, r_vec, rel_proj, rel_logits, T * H,
+                          d_rel, E), "rel_project launch"))
+        return 0;
     return check(cudaGetLastError(), "rel_project launch");
 }
 

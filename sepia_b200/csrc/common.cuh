@@ -222,4 +222,31 @@ __device__ __forceinline__ uint32_t lds_u32_any(const uint8_t *p) {
     return __funnelshift_r(w[0], w[1], sh);
 }
 
+// ------------------------------------------- programmatic dependent launch
+// A kernel launched with the programmatic stream serialization attribute
+// (launch_pdl) may start while its predecessor in the stream still runs:
+// griddep_wait() blocks until the predecessor grid completed and its writes
+// are visible (a no-op for a normal launch), griddep_launch() lets the
+// successor start launching. Every kernel launched by launch_pdl calls
+// griddep_wait() in every CTA before it reads its inputs or writes anything
+// a predecessor may still read, so completion stays transitive along the
+// stream.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename Kern, typename... Args>
+static cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 }  // namespace sepia

@@ -61,6 +61,8 @@ __device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsig
 __global__ void __launch_bounds__(kXchgThreads) k_exchange(const XchgArgs A) {
     __shared__ int owned[32];
     __shared__ int n_owned, ok_sh;
+    griddep_wait();
+    griddep_launch();
     const unsigned long long e = *(volatile unsigned long long *)A.epoch + 1ull;
     const int buf = (int)(e & 1ull);
     const int n_slots = A.topk + A.n_shared;
@@ -230,7 +232,8 @@ extern "C" int sepia_cuda_moe_exchange(SepiaExchange *x, const SepiaMoeLayer *L,
     A.peer_cnt = (unsigned long long *const *)((char *)x->tables + sizeof(void *) * x->world);
     A.my_recv = x->recv; A.my_cnt = x->cnt; A.epoch = x->epoch; A.done = x->done;
     A.out = out; A.err = dev_info().err; A.spin_limit = kXchgSpinLimit;
-    k_exchange<<<kXchgCtas, kXchgThreads, 0, as_stream(stream)>>>(A);
+    if (!check(launch_pdl(k_exchange, kXchgCtas, kXchgThreads, 0, as_stream(stream), A), "moe_exchange launch"))
+        return 0;
     return check(cudaGetLastError(), "moe_exchange launch");
 }
 

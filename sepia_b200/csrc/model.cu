@@ -28,6 +28,8 @@ namespace sepia {
 
 int launch_matvec_q(int t, const void *w, const float *x, float *y, int64_t out_dim, int64_t in_dim, int64_t n_vec,
                     cudaStream_t st);
+int launch_matvec_q_multi(int n, int t, const void *const *w, const int64_t *rows, int64_t in_dim, const float *x,
+                          float *const *y, cudaStream_t st);
 int launch_rel_project(const float *r_vec, const float *rel_proj, float *rel_logits, int64_t T, int64_t H,
                        int64_t d_rel, int64_t E, cudaStream_t st);
 int launch_banded_attn_ex(int kv_f16, const float *q, const void *k, const void *v, const float *rel_logits,
@@ -104,6 +106,8 @@ __global__ void __launch_bounds__(kResThreads) k_embed(const EmbedArgs A) {
     extern __shared__ float e_sm[];
     __shared__ double sh[33];
     __shared__ int tok_sh;
+    griddep_wait();
+    griddep_launch();
     if (threadIdx.x == 0) {
         ModelState *st = A.st;
         int tok;
@@ -179,6 +183,8 @@ __global__ void __launch_bounds__(128) k_attn_prep(const PrepArgs A) {
     __shared__ double sh[33];
     __shared__ float v_sm[128];
     const int d = threadIdx.x;
+    griddep_wait();
+    griddep_launch();
     const int64_t pos = A.st->pos;
     const double tau = (A.is_sliding || !A.tau_table) ? 1.0 : A.tau_table[pos];
     if ((int)blockIdx.x < A.H) {
@@ -235,6 +241,8 @@ struct ResArgs {
 __global__ void __launch_bounds__(kResThreads) k_residual(const ResArgs A) {
     extern __shared__ float x_sm[];
     __shared__ double sh[33];
+    griddep_wait();
+    griddep_launch();
     for (int64_t c = threadIdx.x; c < A.C; c += blockDim.x) {
         const float v = A.use_scale ? __fmul_rn(A.in[c], A.scale) : A.in[c];
         const float o = sconv1(A.w, A.hist, A.C, A.K, c, v);
@@ -266,6 +274,8 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
 __global__ void __launch_bounds__(256) k_argmax(const float *logits, int32_t n, ModelState *st, int advance) {
     __shared__ unsigned long long sh[8];
     unsigned long long best = 0ull;
+    griddep_wait();
+    griddep_launch();
     for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float v = logits[i];
         if (v == v) {
@@ -358,9 +368,15 @@ int run_layers(SepiaModel *m, bool want_logits, cudaStream_t st) {
         const SepiaModelLayer &L = m->layers[l];
         const int H = L.n_heads, Hkv = L.n_kv_heads, Dh = L.head_dim;
         const int64_t q_dim = (int64_t)H * Dh, kv_dim = (int64_t)Hkv * Dh, r_dim = (int64_t)H * d.d_rel;
-        if (!mv(L.wq, m->xn, m->q, q_dim, st) || !mv(L.wk, m->xn, m->k, kv_dim, st) ||
-            !mv(L.wv, m->xn, m->v, kv_dim, st) || !mv(L.wr, m->xn, m->r, r_dim, st))
+        if (L.wq.type == L.wk.type && L.wq.type == L.wv.type && L.wq.type == L.wr.type) {
+            const void *w4[4] = {L.wq.data, L.wk.data, L.wv.data, L.wr.data};
+            const int64_t r4[4] = {q_dim, kv_dim, kv_dim, r_dim};
+            float *y4[4] = {m->q, m->k, m->v, m->r};
+            if (!launch_matvec_q_multi(4, L.wq.type, w4, r4, hidden, m->xn, y4, st)) return 0;
+        } else if (!mv(L.wq, m->xn, m->q, q_dim, st) || !mv(L.wk, m->xn, m->k, kv_dim, st) ||
+                   !mv(L.wv, m->xn, m->v, kv_dim, st) || !mv(L.wr, m->xn, m->r, r_dim, st)) {
             return 0;
+        }
         PrepArgs P;
         P.q_raw = m->q; P.k_raw = m->k; P.v_raw = m->v; P.q_out = m->qs;
         P.k_cache = m->kc[l]; P.v_cache = m->vc[l]; P.k_hist = m->kh[l]; P.v_hist = m->vh[l];
@@ -368,7 +384,7 @@ int run_layers(SepiaModel *m, bool want_logits, cudaStream_t st) {
         P.H = H; P.Hkv = Hkv; P.Dh = Dh; P.K = K; P.kv_dim = kv_dim; P.eps = d.eps;
         P.is_sliding = L.is_sliding; P.window = d.window; P.tau_table = d.has_log_scaling ? m->tau : nullptr;
         P.st = m->st;
-        k_attn_prep<<<(unsigned)(H + Hkv), 128, 0, st>>>(P);
+        launch_pdl(k_attn_prep, (unsigned)(H + Hkv), 128, 0, st, P);
         if (!check(cudaGetLastError(), "model: attn_prep launch")) return 0;
         if (!launch_rel_project(m->r, L.rel_proj, m->rl, 1, H, d.d_rel, L.rel_extent, st)) return 0;
         if (!launch_banded_attn_ex(0, m->qs, m->kc[l], m->vc[l], m->rl, m->att, &m->st->kv_lo, &m->st->kv_hi,
@@ -380,7 +396,7 @@ int run_layers(SepiaModel *m, bool want_logits, cudaStream_t st) {
         R.x = m->x; R.in = m->blk; R.scale = 1.0f; R.use_scale = 0; R.w = L.attn_sconv; R.hist = m->ah[l];
         R.C = hidden; R.K = K; R.norm_w = L.mlp_norm; R.eps = d.eps; R.mup = 0.0f; R.xn = m->xn; R.st = m->st;
         R.advance = 0;
-        k_residual<<<1, kResThreads, hidden * sizeof(float), st>>>(R);
+        launch_pdl(k_residual, 1, kResThreads, hidden * sizeof(float), st, R);
         if (!check(cudaGetLastError(), "model: residual launch")) return 0;
         if (L.is_sparse && m->world > 1) {
             if (!sepia_cuda_moe_layer_sharded(m->xchg, &L.moe, m->xn, &m->ws, m->blk, (void *)st)) return 0;
@@ -398,14 +414,14 @@ int run_layers(SepiaModel *m, bool want_logits, cudaStream_t st) {
         R.norm_w = last ? d.final_norm : m->layers[l + 1].attn_norm;
         R.mup = last ? d.mup : 0.0f;
         R.advance = (last && !want_logits) ? 1 : 0;
-        k_residual<<<1, kResThreads, hidden * sizeof(float), st>>>(R);
+        launch_pdl(k_residual, 1, kResThreads, hidden * sizeof(float), st, R);
         if (!check(cudaGetLastError(), "model: residual launch")) return 0;
     }
     if (want_logits) {
         if (!launch_matvec_q(d.unembed.type, d.unembed.data, m->xn, m->logits, d.unpadded_vocab, hidden, 1, st))
             return 0;
         const int sms = dev_info().sm_count > 0 ? dev_info().sm_count : 148;
-        k_argmax<<<(unsigned)sms, 256, 0, st>>>(m->logits, d.unpadded_vocab, m->st, 1);
+        launch_pdl(k_argmax, (unsigned)sms, 256, 0, st, (const float *)m->logits, d.unpadded_vocab, m->st, 1);
         if (!check(cudaGetLastError(), "model: argmax launch")) return 0;
     }
     return 1;
@@ -418,7 +434,7 @@ int embed(SepiaModel *m, int mode, const int32_t *ids, int32_t *out_ids, cudaStr
     E.hidden = d.hidden; E.vocab = d.vocab; E.ids = ids; E.mode = mode; E.out_ids = out_ids; E.st = m->st;
     E.embed_norm = d.embed_norm; E.norm0 = m->layers[0].attn_norm; E.eps = d.eps; E.x = m->x; E.xn = m->xn;
     E.err = dev_info().err;
-    k_embed<<<1, kResThreads, d.hidden * sizeof(float), st>>>(E);
+    launch_pdl(k_embed, 1, kResThreads, d.hidden * sizeof(float), st, E);
     return check(cudaGetLastError(), "model: embed launch");
 }
 

@@ -757,21 +757,6 @@ struct DnJob {
     }
 };
 
-template <typename Kern, typename... Args>
-static cudaError_t launch_pdl(Kern kern, unsigned grid, unsigned block, size_t smem, cudaStream_t st, Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(block);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, args...);
-}
-
 // ============================================================== host side
 static int to_dev(const SepiaMoeLayer *in, MoeDev &L) {
     if (!in) return fail("moe: null layer");

@@ -69,6 +69,8 @@ __global__ void k_matvec_f32(const float *w, const float *x, float *y, int64_t o
 // z = silu(g) * u with silu(v) = v * (1/(1+expf(-v)))   (src/sepia.c:755-756)
 __global__ void k_silu_mul(const float *g, const float *u, float *z, int64_t n) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    griddep_wait();
+    griddep_launch();
     if (i >= n) return;
     const float gv = g[i];
     const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, (float)exp(-(double)gv)));
@@ -162,7 +164,7 @@ int op_matvec_f32(const float *w, const float *x, float *y, int64_t out_dim, int
 }
 int op_silu_mul(const float *g, const float *u, float *z, int64_t n, cudaStream_t st) {
     if (n <= 0 || !g || !u || !z) return fail("silu_mul: bad arguments");
-    k_silu_mul<<<blocks_for(n, 256), 256, 0, st>>>(g, u, z, n);
+    if (!check(launch_pdl(k_silu_mul, blocks_for(n, 256), 256, 0, st, g, u, z, n), "silu_mul launch")) return 0;
     return check(cudaGetLastError(), "silu_mul launch");
 }
 int op_add(const float *a, const float *b, float *o, int64_t n, cudaStream_t st) {

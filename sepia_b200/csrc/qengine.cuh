@@ -88,14 +88,6 @@ struct QeLayout {
     uint32_t test_extra_tx = 0;            // test hook only: extra bytes the producer announces
 };
 
-// Programmatic dependent launch: a kernel launched with the programmatic
-// stream serialization attribute may start while its predecessor runs;
-// griddep_wait() blocks until the predecessor grid completed and its writes
-// are visible (a no-op for a normal launch), griddep_launch() lets the
-// successor start launching.
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
 // u / n for 0 <= u < 2^22 without an integer division: (u + 0.5) / n lies
 // at least 0.5/n from an integer, more than the float product's error
 // ((u + 0.5) / n * 2^-23) for such u; inv_n = 1/n rounded to float.

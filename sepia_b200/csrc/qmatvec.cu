@@ -55,6 +55,8 @@ __global__ void __launch_bounds__(17 * 32) k_matvec(const MvParams P) {
     __syncthreads();
 
     const int sbb = fmt_sb_bytes(T);
+    griddep_wait();
+    griddep_launch();
 
     if (warp == n_cons) {
         // ---------------- producer ----------------
@@ -189,9 +191,54 @@ static int launch_matvec_engine(int t, const void *w, const float *x, float *y, 
     if (!ensure_smem(fn, (int)smem)) return 0;
     const int64_t units = (out_dim + 15) / 16;
     const int64_t grid = std::min<int64_t>(units, (int64_t)di.sm_count);
-    k_qengine<MvJob><<<(unsigned)grid, (P.G * P.cg + 2) * 32, (size_t)smem, st>>>(J, P);
-    return check(cudaGetLastError(), "matvec_q (tensor cores) launch");
+    return check(launch_pdl(k_qengine<MvJob>, (unsigned)grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, J, P),
+                 "matvec_q (tensor cores) launch");
 }
+
+// Up to kMvMulti matrices of one format and input width sharing one input x
+// (the q/k/v/r projections of an attention layer) in one engine launch: the
+// matrices' 16-row tiles are numbered consecutively, so small matrices do
+// not leave SMs idle and the launch count drops.
+constexpr int kMvMulti = 4;
+struct MvNJob {
+    const uint8_t *w[kMvMulti];
+    float *y[kMvMulti];
+    int64_t rows[kMvMulti];
+    int64_t u0[kMvMulti + 1];          // first unit of each matrix
+    int n;
+    int64_t rb;
+    int type, nsb, sbs, nsplit;
+    const float *x;
+    __device__ void init() {}
+    __device__ void setup(uint8_t *, int, bool) {}
+    __device__ int64_t n_units() const { return u0[n]; }
+    __device__ bool needs_dep(int64_t) const { return false; }
+    __device__ uint32_t tab_mask(const uint8_t *) const { return 1u; }
+    __device__ int splits(const uint8_t *, int64_t) const { return nsplit; }
+    __device__ int which(int64_t u) const {
+        int m = 0;
+#pragma unroll
+        for (int i = 1; i < kMvMulti; i++) m += (i < n && u >= u0[i]) ? 1 : 0;
+        return m;
+    }
+    __device__ void unit(const uint8_t *, int64_t u, QUnit &U) const {
+        const int m = which(u);
+        const int64_t r0 = (u - u0[m]) * 16;
+        const int nr = (int)imin64(16, rows[m] - r0);
+        U.type = type; U.nsb = nsb; U.sbs = sbs; U.nsplit = nsplit; U.rb = rb; U.tab = 0;
+        U.nlo = min(8, nr);
+        U.nhi = max(0, nr - 8);
+        U.lo = w[m] + r0 * rb;
+        U.hi = U.lo + 8 * rb;
+    }
+    __device__ int n_tab() const { return 1; }
+    __device__ const float *tab_src(int) const { return x; }
+    __device__ void finish(const uint8_t *, int64_t u, const QUnit &, double v, int lane) const {
+        const int m = which(u);
+        const int64_t r = (u - u0[m]) * 16 + lane;
+        if (lane < 16 && r < rows[m]) y[m][r] = (float)v;
+    }
+};
 
 // Can this call run on the engine? in_dim whole superblocks, x 16-byte
 // aligned (float4 table loads), every row at the same address mod 4 with
@@ -380,6 +427,8 @@ __global__ void __launch_bounds__(kIqWarps * 32) k_matvec_iqb(const IqbParams P)
     const int v0 = blockIdx.x * P.vb;
     const int nv = min(P.vb, P.n_vec - v0);
     const int64_t in4 = P.in_dim / 4;
+    griddep_wait();
+    griddep_launch();
     for (int64_t i = threadIdx.x; i < nv * in4; i += blockDim.x) {
         const int v = (int)(i / in4);
         const int64_t c4 = i - v * in4;
@@ -568,8 +617,47 @@ int launch_matvec_q(int t, const void *w, const float *x, float *y, int64_t out_
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (n_cons + 1) * 32, (size_t)smem);
     if (per_sm < 1) per_sm = 1;
     const int64_t grid = std::min<int64_t>(P.num_units, (int64_t)di.sm_count * per_sm);
-    kern<<<(unsigned)grid, (n_cons + 1) * 32, (size_t)smem, st>>>(P);
+    if (!check(launch_pdl(kern, (unsigned)grid, (n_cons + 1) * 32, (size_t)smem, st, P), "matvec_q launch")) return 0;
     return check(cudaGetLastError(), "matvec_q launch");
+}
+
+// y_i = W_i x for n <= 4 matrices of one format and input width: one engine
+// launch when every matrix can run on it, else one launch per matrix.
+int launch_matvec_q_multi(int n, int t, const void *const *w, const int64_t *rows, int64_t in_dim, const float *x,
+                          float *const *y, cudaStream_t st) {
+    if (n < 1 || n > kMvMulti) return fail("matvec_q_multi: %d matrices (1..%d)", n, kMvMulti);
+    const int64_t rb = host_row_bytes(t, in_dim);
+    bool eng = rb > 0;
+    for (int i = 0; i < n && eng; i++) eng = rows[i] > 0 && engine_ok(t, w[i], x, in_dim, rb, 1);
+    if (!eng) {
+        for (int i = 0; i < n; i++)
+            if (!launch_matvec_q(t, w[i], x, y[i], rows[i], in_dim, 1, st)) return 0;
+        return 1;
+    }
+    DevInfo &di = dev_info();
+    MvNJob J;
+    J.n = n; J.rb = rb; J.type = t; J.nsb = (int)(in_dim / kQK); J.x = x;
+    J.u0[0] = 0;
+    for (int i = 0; i < kMvMulti; i++) {
+        J.w[i] = i < n ? reinterpret_cast<const uint8_t *>(w[i]) : nullptr;
+        J.y[i] = i < n ? y[i] : nullptr;
+        J.rows[i] = i < n ? rows[i] : 0;
+        J.u0[i + 1] = J.u0[i] + (i < n ? (rows[i] + 15) / 16 : 0);
+    }
+    J.sbs = qe_sbs(t, J.nsb, qe_row_budget(di.smem_optin, (int64_t)J.nsb * kTabSB), J.nsplit);
+    if (!J.sbs) return fail("matvec_q_multi: no tensor-core split for type %d", t);
+    QeLayout P;
+    int cg, G;
+    qe_groups(J.sbs, cg, G);
+    int64_t smem = 0;
+    if (!qe_layout(P, G, cg, (uint32_t)J.sbs * qe_sb_bytes(t), 1, J.nsb, di.smem_optin, smem))
+        return fail("matvec_q_multi: tensor-core tile needs %lld B of shared memory", (long long)smem);
+    P.err = di.err;
+    const void *fn = (const void *)k_qengine<MvNJob>;
+    if (!ensure_smem(fn, (int)smem)) return 0;
+    const int64_t grid = std::min<int64_t>(J.u0[n], (int64_t)di.sm_count);
+    return check(launch_pdl(k_qengine<MvNJob>, (unsigned)grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, J, P),
+                 "matvec_q_multi launch");
 }
 
 int launch_dequant(int t, const void *raw, float *out, int64_t n, cudaStream_t st) {
