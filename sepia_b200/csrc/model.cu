@@ -20,9 +20,12 @@
 #include "common.cuh"
 #include "quant_formats.cuh"
 
+#include <cooperative_groups.h>
 #include <cmath>
 #include <cstring>
 #include <vector>
+
+namespace cg = cooperative_groups;
 
 namespace sepia {
 
@@ -42,7 +45,6 @@ size_t attn_part_bytes(int64_t T, int64_t H, int S, int64_t Dh);
 int op_silu_mul(const float *g, const float *u, float *z, int64_t n, cudaStream_t st);
 
 constexpr int kMaxConvK = 16;
-constexpr int kResThreads = 1024;
 
 // Device-resident decode state.
 struct ModelState {
@@ -83,6 +85,29 @@ __device__ float rms_inv(const float *v, int64_t n, float eps, double *sh) {
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
 }
 
+// The residual stream's kernels run as one cluster of kClusterCtas CTAs
+// (each owns hidden/kClusterCtas channels); a norm's sum of squares is a
+// block reduction per CTA, then every CTA adds the partials of the whole
+// cluster through distributed shared memory in rank order (deterministic).
+constexpr int kClusterCtas = 8;
+constexpr int kClThreads = 1024;
+
+__device__ double cluster_sum_d(double v, double *sh, double *part) {
+    cg::cluster_group cl = cg::this_cluster();
+    v = block_sum_d2(v, sh);
+    if (threadIdx.x == 0) part[0] = v;
+    cl.sync();
+    double t = 0.0;
+    for (unsigned r = 0; r < cl.num_blocks(); r++) t += *cl.map_shared_rank(part, r);
+    cl.sync();       // no CTA leaves (or reuses part) while another still reads it
+    return t;
+}
+
+__device__ __forceinline__ float rms_inv_from(double sumsq, int64_t n, float eps) {
+    const float var = (float)(sumsq / (double)n);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+}
+
 // ------------------------------------------------------------ embedding
 struct EmbedArgs {
     int type;
@@ -99,23 +124,32 @@ struct EmbedArgs {
     int *err;
 };
 
-// One CTA: token id -> dequantized row (qrow, src/sepia.c:742-746) ->
-// rmsnorm(embed_norm) = x (src/sepia.c:3352-3355) -> rmsnorm(attn_norm of
-// layer 0) = xn.
-__global__ void __launch_bounds__(kResThreads) k_embed(const EmbedArgs A) {
-    extern __shared__ float e_sm[];
+// Token id -> dequantized row (qrow, src/sepia.c:742-746) -> rmsnorm with
+// embed_norm = x (src/sepia.c:3352-3355) -> rmsnorm with layer 0's
+// attention norm = xn. One cluster; CTA rank r owns a contiguous run of
+// 32-element parts. Every CTA reads the pending token before rank 0
+// updates the decode state.
+__global__ void __launch_bounds__(kClThreads) k_embed(const EmbedArgs A) {
+    cg::cluster_group cl = cg::this_cluster();
     __shared__ double sh[33];
+    __shared__ double part;
     __shared__ int tok_sh;
+    __shared__ float e_sm[32 * 32];
     griddep_wait();
     griddep_launch();
+    const unsigned rank = cl.block_rank(), nr = cl.num_blocks();
     if (threadIdx.x == 0) {
+        const ModelState *st = A.st;
+        int tok = A.mode == 0 ? A.ids[st->fed] : (int)(0xFFFFFFFFu - (uint32_t)(st->best & 0xFFFFFFFFull));
+        tok_sh = tok;
+    }
+    cl.sync();
+    int tok = tok_sh;
+    if (rank == 0 && threadIdx.x == 0) {
         ModelState *st = A.st;
-        int tok;
         if (A.mode == 0) {
-            tok = A.ids[st->fed];
             st->fed += 1;
         } else {
-            tok = (int)(0xFFFFFFFFu - (uint32_t)(st->best & 0xFFFFFFFFull));
             A.out_ids[st->gen] = tok;
             st->gen += 1;
         }
@@ -123,30 +157,31 @@ __global__ void __launch_bounds__(kResThreads) k_embed(const EmbedArgs A) {
         if (tok < 0 || tok >= A.vocab) {
             st->bad_token = 1;
             set_error(A.err, kErrBadArgs);
-            tok = 0;
         }
-        tok_sh = tok;
     }
-    __syncthreads();
-    const uint8_t *row = A.w + (int64_t)tok_sh * A.rb;
+    if (tok < 0 || tok >= A.vocab) tok = 0;
+    const int64_t nparts = (A.hidden + 31) / 32;
+    const int64_t pp = (nparts + nr - 1) / nr;             // parts per CTA (<= 32)
+    const int64_t p0 = rank * pp, p1 = imin64(nparts, p0 + pp);
+    const int64_t e0 = p0 * 32, e1 = imin64(A.hidden, p1 * 32);
+    const uint8_t *row = A.w + (int64_t)tok * A.rb;
     const int sbB = fmt_sb_bytes(A.type);
-    for (int64_t first = (int64_t)threadIdx.x * 32; first < A.hidden; first += (int64_t)blockDim.x * 32) {
+    if (threadIdx.x < p1 - p0) {
+        const int64_t first = (p0 + threadIdx.x) * 32;
         float y[32];
         const int nvalid = (int)imin64(32, A.hidden - first);
         decode_part_exact(A.type, row + (first / kQK) * sbB, (int)((first % kQK) / 32), y, nvalid);
-        for (int i = 0; i < nvalid; i++) e_sm[first + i] = y[i];
+        for (int i = 0; i < nvalid; i++) e_sm[first - e0 + i] = y[i];
     }
     __syncthreads();
-    const float inv = rms_inv(e_sm, A.hidden, A.eps, sh);
-    for (int64_t i = threadIdx.x; i < A.hidden; i += blockDim.x) {
-        const float v = __fmul_rn(A.embed_norm[i], __fmul_rn(e_sm[i], inv));
-        e_sm[i] = v;
-        A.x[i] = v;
-    }
-    __syncthreads();
-    const float inv2 = rms_inv(e_sm, A.hidden, A.eps, sh);
-    for (int64_t i = threadIdx.x; i < A.hidden; i += blockDim.x)
-        A.xn[i] = __fmul_rn(A.norm0[i], __fmul_rn(e_sm[i], inv2));
+    const int64_t c = e0 + threadIdx.x;
+    const bool mine = c < e1;
+    const float ev = mine ? e_sm[threadIdx.x] : 0.0f;
+    const float inv = rms_inv_from(cluster_sum_d(mine ? (double)__fmul_rn(ev, ev) : 0.0, sh, &part), A.hidden, A.eps);
+    const float xv = mine ? __fmul_rn(A.embed_norm[c], __fmul_rn(ev, inv)) : 0.0f;
+    if (mine) A.x[c] = xv;
+    const float inv2 = rms_inv_from(cluster_sum_d(mine ? (double)__fmul_rn(xv, xv) : 0.0, sh, &part), A.hidden, A.eps);
+    if (mine) A.xn[c] = __fmul_rn(A.norm0[c], __fmul_rn(xv, inv2));
 }
 
 // ------------------------------------------------------- attention prep
@@ -167,12 +202,17 @@ struct PrepArgs {
 // Depthwise causal convolution of one channel at T = 1 with its history,
 // plus the history roll (sconv_apply, src/sepia.c:801-816).
 __device__ __forceinline__ float sconv1(const float *w, float *hist, int64_t C, int K, int64_t c, float in) {
+    // window = hist[0..K-2] then `in`; the history moves one frame down
+    // (no local array: K is a runtime value)
     double acc = 0.0;
-    float win[kMaxConvK];
-    for (int j = 0; j < K - 1; j++) win[j] = hist[(int64_t)j * C + c];
-    win[K - 1] = in;
-    for (int k = 0; k < K; k++) acc += (double)w[c * K + k] * (double)win[k];
-    for (int j = 0; j < K - 1; j++) hist[(int64_t)j * C + c] = win[j + 1];
+    const float *wc = w + c * K;
+    for (int j = 0; j < K - 1; j++) {
+        const float h = hist[(int64_t)j * C + c];
+        acc += (double)wc[j] * (double)h;
+        if (j > 0) hist[(int64_t)(j - 1) * C + c] = h;
+    }
+    acc += (double)wc[K - 1] * (double)in;
+    if (K > 1) hist[(int64_t)(K - 2) * C + c] = in;
     return __fadd_rn(in, (float)acc);
 }
 
@@ -236,28 +276,44 @@ struct ResArgs {
     int advance;                // pos += 1 at the end
 };
 
-// x += sconv(in) (src/sepia.c:1506-1519, 1535-1549) then xn = rmsnorm(x)
-// for the next block. One CTA (the residual stream is 28 KB).
-__global__ void __launch_bounds__(kResThreads) k_residual(const ResArgs A) {
-    extern __shared__ float x_sm[];
+// x += sconv(in) (src/sepia.c:1506-1519, 1535-1549), then xn = rmsnorm(x)
+// for the next block. One cluster; each thread owns one channel per pass.
+__global__ void __launch_bounds__(kClThreads) k_residual(const ResArgs A) {
+    cg::cluster_group cl = cg::this_cluster();
     __shared__ double sh[33];
+    __shared__ double part;
     griddep_wait();
     griddep_launch();
-    for (int64_t c = threadIdx.x; c < A.C; c += blockDim.x) {
-        const float v = A.use_scale ? __fmul_rn(A.in[c], A.scale) : A.in[c];
-        const float o = sconv1(A.w, A.hist, A.C, A.K, c, v);
-        const float xv = __fadd_rn(A.x[c], o);
-        A.x[c] = xv;
-        x_sm[c] = xv;
+    const unsigned rank = cl.block_rank(), nr = cl.num_blocks();
+    const int64_t per = (A.C + nr - 1) / nr;
+    const int64_t c0 = rank * per, c1 = imin64(A.C, c0 + per);
+    constexpr int kMaxPer = 8;          // channels per thread (hidden <= 8 * 1024 * kClusterCtas)
+    float xs[kMaxPer];
+    double sq = 0.0;
+#pragma unroll
+    for (int k = 0; k < kMaxPer; k++) {
+        const int64_t c = c0 + threadIdx.x + (int64_t)k * blockDim.x;
+        xs[k] = 0.0f;
+        if (c < c1) {
+            const float v = A.use_scale ? __fmul_rn(A.in[c], A.scale) : A.in[c];
+            const float o = sconv1(A.w, A.hist, A.C, A.K, c, v);
+            const float xv = __fadd_rn(A.x[c], o);
+            A.x[c] = xv;
+            xs[k] = xv;
+            sq += (double)__fmul_rn(xv, xv);
+        }
     }
-    __syncthreads();
-    const float inv = rms_inv(x_sm, A.C, A.eps, sh);
-    for (int64_t c = threadIdx.x; c < A.C; c += blockDim.x) {
-        float v = __fmul_rn(A.norm_w[c], __fmul_rn(x_sm[c], inv));
-        if (A.mup > 0.0f) v = __fdiv_rn(v, A.mup);
-        A.xn[c] = v;
+    const float inv = rms_inv_from(cluster_sum_d(sq, sh, &part), A.C, A.eps);
+#pragma unroll
+    for (int k = 0; k < kMaxPer; k++) {
+        const int64_t c = c0 + threadIdx.x + (int64_t)k * blockDim.x;
+        if (c < c1) {
+            float v = __fmul_rn(A.norm_w[c], __fmul_rn(xs[k], inv));
+            if (A.mup > 0.0f) v = __fdiv_rn(v, A.mup);
+            A.xn[c] = v;
+        }
     }
-    if (A.advance && threadIdx.x == 0) A.st->pos += 1;
+    if (A.advance && rank == 0 && threadIdx.x == 0) A.st->pos += 1;
 }
 
 // ---------------------------------------------------------------- argmax
@@ -354,6 +410,27 @@ int check_q(const SepiaQTensor &t, int64_t rows, int64_t cols, const char *what,
     return 1;
 }
 
+// One cluster of kClusterCtas CTAs, launched with programmatic dependent
+// launch like the rest of the chain.
+template <typename Args>
+int launch_cluster(void (*kern)(const Args), cudaStream_t st, const Args &a) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kClusterCtas);
+    cfg.blockDim = dim3(kClThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = kClusterCtas;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    return check(cudaLaunchKernelEx(&cfg, kern, a), "model: cluster kernel launch");
+}
+
 int mv(const SepiaQTensor &t, const float *x, float *y, int64_t rows, cudaStream_t st) {
     return launch_matvec_q(t.type, t.data, x, y, rows, t.cols, 1, st);
 }
@@ -396,8 +473,7 @@ int run_layers(SepiaModel *m, bool want_logits, cudaStream_t st) {
         R.x = m->x; R.in = m->blk; R.scale = 1.0f; R.use_scale = 0; R.w = L.attn_sconv; R.hist = m->ah[l];
         R.C = hidden; R.K = K; R.norm_w = L.mlp_norm; R.eps = d.eps; R.mup = 0.0f; R.xn = m->xn; R.st = m->st;
         R.advance = 0;
-        launch_pdl(k_residual, 1, kResThreads, hidden * sizeof(float), st, R);
-        if (!check(cudaGetLastError(), "model: residual launch")) return 0;
+        if (!launch_cluster(k_residual, st, R)) return 0;
         if (L.is_sparse && m->world > 1) {
             if (!sepia_cuda_moe_layer_sharded(m->xchg, &L.moe, m->xn, &m->ws, m->blk, (void *)st)) return 0;
         } else if (L.is_sparse) {
@@ -414,8 +490,7 @@ int run_layers(SepiaModel *m, bool want_logits, cudaStream_t st) {
         R.norm_w = last ? d.final_norm : m->layers[l + 1].attn_norm;
         R.mup = last ? d.mup : 0.0f;
         R.advance = (last && !want_logits) ? 1 : 0;
-        launch_pdl(k_residual, 1, kResThreads, hidden * sizeof(float), st, R);
-        if (!check(cudaGetLastError(), "model: residual launch")) return 0;
+        if (!launch_cluster(k_residual, st, R)) return 0;
     }
     if (want_logits) {
         if (!launch_matvec_q(d.unembed.type, d.unembed.data, m->xn, m->logits, d.unpadded_vocab, hidden, 1, st))
@@ -434,14 +509,11 @@ int embed(SepiaModel *m, int mode, const int32_t *ids, int32_t *out_ids, cudaStr
     E.hidden = d.hidden; E.vocab = d.vocab; E.ids = ids; E.mode = mode; E.out_ids = out_ids; E.st = m->st;
     E.embed_norm = d.embed_norm; E.norm0 = m->layers[0].attn_norm; E.eps = d.eps; E.x = m->x; E.xn = m->xn;
     E.err = dev_info().err;
-    launch_pdl(k_embed, 1, kResThreads, d.hidden * sizeof(float), st, E);
-    return check(cudaGetLastError(), "model: embed launch");
+    return launch_cluster(k_embed, st, E);
 }
 
 int setup_kernels(const SepiaModelDesc &d) {
-    const int sm = (int)(d.hidden * sizeof(float));
-    if (!ensure_smem((const void *)k_embed, sm)) return 0;
-    if (!ensure_smem((const void *)k_residual, sm)) return 0;
+    (void)d;
     return 1;
 }
 
@@ -451,8 +523,10 @@ extern "C" int sepia_model_create(const SepiaModelDesc *d, SepiaModel **out) {
     if (!d || !out) return fail("model: null argument");
     *out = nullptr;
     if (d->n_layers <= 0 || !d->layers) return fail("model: no layers");
-    if (d->hidden <= 0 || d->hidden % 32 || d->hidden * 4 > 200 * 1024)
-        return fail("model: hidden %lld unsupported (a multiple of 32, at most 51200)", (long long)d->hidden);
+    if (d->hidden <= 0 || d->hidden % 32 || d->hidden > 8 * kClThreads * kClusterCtas ||
+        (d->hidden + kClusterCtas - 1) / kClusterCtas > kClThreads)
+        return fail("model: hidden %lld unsupported (a multiple of 32, at most %d)", (long long)d->hidden,
+                    kClThreads * kClusterCtas);
     if (d->conv_k < 1 || d->conv_k > kMaxConvK) return fail("model: conv kernel %d outside 1..%d", d->conv_k, kMaxConvK);
     if (d->max_positions <= 0) return fail("model: max_positions must be positive");
     if (d->unpadded_vocab <= 0 || d->unpadded_vocab > d->vocab) return fail("model: bad vocab sizes");

@@ -245,7 +245,7 @@ struct MvNJob {
 // 4-byte aligned superblocks (2-byte for Q3_K).
 static bool engine_ok(int t, const void *w, const float *x, int64_t in_dim, int64_t rb, int64_t n_vec) {
     const uintptr_t wa = reinterpret_cast<uintptr_t>(w);
-    return mma_format(t) && n_vec == 1 && in_dim % kQK == 0 && in_dim / kQK <= 64 && rb % 4 == 0 &&
+    return mma_format(t) && n_vec == 1 && in_dim % kQK == 0 && in_dim / kQK <= 80 && rb % 4 == 0 &&
            (wa & (t == T_Q3_K ? 1 : 3)) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
 }
 

@@ -64,7 +64,7 @@ def test_matvec_golden_sqlx(torch_cuda, oracle, path):
     assert oracle.rel_err(got, y) <= TOL
 
 
-SHAPES = [(1, 256), (3, 512), (17, 768), (64, 2048), (130, 7168), (33, 9216)]
+SHAPES = [(1, 256), (3, 512), (17, 768), (64, 2048), (130, 7168), (33, 9216), (40, 18432), (24, 20480)]
 
 
 @pytest.mark.parametrize("t", Q.ALL_TYPES, ids=lambda t: Q.NAMES[t])
