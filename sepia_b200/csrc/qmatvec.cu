@@ -16,6 +16,8 @@
 
 namespace sepia {
 
+int op_matvec_f32(const float *w, const float *x, float *y, int64_t out_dim, int64_t in_dim, cudaStream_t st);
+
 constexpr int kMvStagesMax = 6;
 
 struct MvParams {
@@ -594,6 +596,14 @@ int launch_matvec_q(int t, const void *w, const float *x, float *y, int64_t out_
     if ((int64_t)trw * G * rb > 80 * 1024) trw = 2;
     while (G > 1 && (int64_t)trw * G * rb > 80 * 1024) G /= 2;
     if ((int64_t)trw * G * rb > 160 * 1024) return fail("matvec_q: rows of %lld bytes too large", (long long)rb);
+    if (t == T_F32 && 2 * (int64_t)slot_bytes_for((uint64_t)trw * G * rb) + 4096 > (int64_t)di.smem_optin) {
+        // f32 rows too long to double-buffer: one warp per row straight from
+        // global memory (same double-accumulated dot)
+        for (int64_t v = 0; v < n_vec; v++)
+            if (!op_matvec_f32(reinterpret_cast<const float *>(w), x + v * in_dim, y + v * out_dim, out_dim, in_dim, st))
+                return 0;
+        return 1;
+    }
     const int TR = trw * G;
     const uint32_t slot = slot_bytes_for((uint64_t)TR * rb);
     const int n_cons = nwc * G;
