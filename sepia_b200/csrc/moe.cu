@@ -218,6 +218,87 @@ __global__ void __launch_bounds__(kRouterMaxChunks * 32) k_router(const MoeDev L
     }
 }
 
+// Router GEMV, bulk-copy form: each CTA owns `rpc` consecutive rows of the
+// [n_total, hidden] f32 matrix (contiguous bytes), fetched with one 1-D
+// cp.async.bulk (TMA engine, no multicast) into shared memory before the
+// dependency wait -- the weights do not depend on the previous kernel. A
+// single request per CTA keeps the whole matrix in flight without the
+// per-load queueing of thousands of 16-byte loads. Thread t then dots
+// elements t, t + T, ... of each row with x (held in registers) in fp64,
+// the warps' partials are summed in warp order, and the last CTA selects.
+constexpr int kRouter2Threads = 256;
+constexpr int kRouter2MaxPerThread = 64;       // hidden <= 64 * 256
+__global__ void __launch_bounds__(kRouter2Threads) k_router2(const MoeDev L, const float *x, float *logits,
+                                                              int32_t *topk_idx, float *weights,
+                                                              unsigned int *counter, float2 *row_out, int rpc) {
+    extern __shared__ __align__(128) float w_sm[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ double s_w[kRouter2Threads / 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_total = L.n_routed + L.n_shared;
+    const int r0 = blockIdx.x * rpc;
+    const int nr = min(rpc, n_total - r0);
+    const int64_t H = L.hidden;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+        const uint32_t bytes = (uint32_t)(nr * H * 4);
+        mbar_arrive_expect_tx(&bar, bytes);
+        bulk_g2s(w_sm, L.router_w + (int64_t)r0 * H, bytes, &bar);
+    }
+    griddep_launch();
+    griddep_wait();
+    float xv[kRouter2MaxPerThread];
+    const int per = (int)((H + kRouter2Threads - 1) / kRouter2Threads);
+#pragma unroll
+    for (int j = 0; j < kRouter2MaxPerThread; j++) {
+        const int64_t i = threadIdx.x + (int64_t)j * kRouter2Threads;
+        xv[j] = (j < per && i < H) ? __ldg(x + i) : 0.0f;
+    }
+    __syncthreads();                       // the barrier's init is visible
+    const bool ok = mbar_wait(&bar, 0, L.err);
+    const float bias0 = 0.0f;
+    (void)bias0;
+    for (int r = 0; r < nr; r++) {
+        double acc = 0.0;
+        if (ok) {
+            const float *wr = w_sm + (int64_t)r * H;
+#pragma unroll
+            for (int j = 0; j < kRouter2MaxPerThread; j++) {
+                const int64_t i = threadIdx.x + (int64_t)j * kRouter2Threads;
+                if (j < per && i < H) acc = fma((double)wr[i], (double)xv[j], acc);
+            }
+        }
+        acc = warp_sum_d(acc);
+        if (lane == 0) s_w[warp] = acc;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double t = 0.0;
+            for (int w = 0; w < kRouter2Threads / 32; w++) t += s_w[w];       // warp order
+            const int row = r0 + r;
+            const float l = (float)t;
+            logits[row] = l;
+            const float score = row < L.n_routed ? __fadd_rn(sigmoid_ref(l), L.router_bias[row]) : 0.0f;
+            row_out[row] = make_float2(score, logsigmoid_ref(l));
+        }
+        __syncthreads();
+    }
+    if (warp != 0) return;
+    unsigned int last = 0;
+    if (lane == 0) {
+        __threadfence();     // release this CTA's writes before counting it
+        last = (atomicAdd(counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+    }
+    if (!__shfl_sync(0xffffffffu, last, 0)) return;
+    __threadfence();
+    if (L.n_routed <= 8 * 32) router_select<8>(L, row_out, topk_idx, weights, lane);
+    else router_select<kRouterMaxExperts / 32>(L, row_out, topk_idx, weights, lane);
+    if (lane == 0) {
+        *counter = 0u;   // ready for the next launch
+        __threadfence();
+    }
+}
+
 // Selection only (bit-exact part of the router): top-k of given scores.
 __global__ void k_topk(const float *scores, int n, int topk, int32_t *idx) {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
@@ -955,6 +1036,20 @@ int launch_router(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaS
     if (router_chunks(L.hidden) > kRouterMaxChunks)
         return fail("moe: hidden %lld exceeds the router's %d", (long long)L.hidden, kRouterMaxChunks * kRouterChunk);
     if (!ws->router_part) return fail("moe: work area has no router scratch (carve it with moe_work_carve)");
+    // bulk-copy form: ~one CTA per SM, each fetching its rows in one request
+    const DevInfo &di = dev_info();
+    const int sms = di.sm_count > 0 ? di.sm_count : 148;
+    const int rpc = (n_total + sms - 1) / sms;
+    const int64_t smem = (int64_t)rpc * L.hidden * 4;
+    if ((L.hidden * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(L.router_w) & 15) == 0 &&
+        L.hidden <= (int64_t)kRouter2MaxPerThread * kRouter2Threads && smem <= di.smem_optin - 2048 &&
+        smem < (1 << 20)) {
+        if (!ensure_smem((const void *)k_router2, (int)smem)) return 0;
+        const unsigned grid = (unsigned)((n_total + rpc - 1) / rpc);
+        return check(launch_pdl(k_router2, grid, kRouter2Threads, (size_t)smem, st, L, x, ws->logits, ws->topk_idx,
+                                ws->weights, ws->counter, reinterpret_cast<float2 *>(ws->router_part), rpc),
+                     "moe router launch");
+    }
     // one CTA per logit row, a warp per 1024-element chunk
     const int nw = std::max(kRouterWarps, router_chunks(L.hidden));
     return check(launch_pdl(k_router, (unsigned)n_total, nw * 32, 0, st, L, x, ws->logits, ws->topk_idx, ws->weights,
