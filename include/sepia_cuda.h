@@ -94,6 +94,9 @@ typedef struct {
     float *slots;           /* [topk + n_shared, hidden] per-slot terms (sharded mode) */
     unsigned int *counter;  /* router completion counter; zero before first use */
     double *router_part;    /* [n_routed + n_shared, ceil(hidden/1024)] router scratch (per-row scores) */
+    unsigned int *sync;     /* single-launch layer: progress counters; zero before first use, every
+                               completed launch leaves them zero (re-zero after a device error) */
+    void *htab;             /* single-launch layer: tensor-core activation tables of h */
 } SepiaMoeWork;
 
 size_t sepia_cuda_moe_work_bytes(const SepiaMoeLayer *L);
@@ -118,6 +121,19 @@ int sepia_cuda_moe_combine(const SepiaMoeLayer *L, const SepiaMoeWork *ws, float
 /* router + experts (world must be 1 or the layer already sharded with
  * write_slots handled by the caller). */
 int sepia_cuda_moe_layer(const SepiaMoeLayer *L, const float *x, const SepiaMoeWork *ws, float *out, void *stream);
+/* The same layer as ONE persistent cooperative kernel (router, top-k,
+ * gate/up, down and combine; no kernel boundary). Opt-in: on B200 it
+ * measured slower than the kernel chain of sepia_cuda_moe_layer (96 us
+ * against 72 us for BASELINE configuration 2), because under a saturated
+ * memory system each of its cross-CTA dependencies costs 2-4 us. Same
+ * results as the chain (ids and weights equal, outputs within 1e-6).
+ * eligible: 1 when the fused kernel takes this layer (world = 1,
+ * tensor-core expert formats, hidden <= 8192, a shared-memory plan that
+ * fits). No reference counterpart: the reference synchronises the host
+ * inside every MoE layer (src/sepia.c:3831-3974). */
+int sepia_cuda_moe_fused_eligible(const SepiaMoeLayer *L, const SepiaMoeWork *ws);
+int sepia_cuda_moe_layer_fused(const SepiaMoeLayer *L, const float *x, const SepiaMoeWork *ws, float *out,
+                               void *stream);
 /* Selection only: top-k of given scores by the reference's strict-'>' scan
  * (src/sepia.c:1336-1347; lowest index wins ties). */
 int sepia_cuda_topk_select(const float *scores, int32_t n, int32_t topk, int32_t *idx, void *stream);

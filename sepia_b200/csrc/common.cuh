@@ -145,6 +145,13 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
                  : "memory");
 }
 
+// Arrival counted `count` times (count >= 1).
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t *bar, uint32_t count) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+                 "r"(count)
+                 : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
                      smem_u32(bar)),

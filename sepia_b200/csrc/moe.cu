@@ -19,126 +19,12 @@
 //                 sharding, writes each slot's term separately so an
 //                 all-reduce plus k_combine reproduces the same sums bit for
 //                 bit on any number of GPUs.
-#include "../../include/sepia_cuda.h"
-#include "runtime.h"
+#include "moe_dev.cuh"
 #include "stream.cuh"
-#include "qengine.cuh"
 
 #include <algorithm>
 
 namespace sepia {
-
-constexpr int kMaxSlots = 16;      // topk + n_shared
-constexpr int kRouterWarps = 8;
-constexpr int kRouterChunk = 1024;       // router row elements per warp
-constexpr int kRouterMaxExperts = 1024;  // n_routed + n_shared
-constexpr int kRouterMaxChunks = 16;     // hidden <= 16384
-__host__ __device__ inline int router_chunks(int64_t hidden) { return (int)((hidden + kRouterChunk - 1) / kRouterChunk); }
-constexpr int kGuStagesMax = 8;
-constexpr int kDnStagesMax = 8;
-constexpr int kTRG = 8;            // max rows per gate/up unit
-constexpr int kTRD = 4;            // rows per down unit
-constexpr int kDnMaxSlots = 8;     // topk + n_shared handled by the down kernel
-
-// --------------------------------------------------------------- device-side layer
-struct MoeDev {
-    int64_t hidden, ff;
-    int n_routed, n_shared, topk;
-    double route_scale;
-    float global_scale;
-    const float *router_w, *router_bias;
-    int gate_type, up_type, down_type, sh_gate_type, sh_up_type, sh_down_type;
-    const uint8_t *gate, *up, *down, *sh_gate, *sh_up, *sh_down;
-    int64_t gate_stride, up_stride, down_stride, sh_gate_stride, sh_up_stride, sh_down_stride;
-    int64_t rb_gate, rb_up, rb_down, rb_sh_gate, rb_sh_up, rb_sh_down;
-    int rank, world;
-    const int32_t *expert_slot;
-    int *err;
-};
-
-// Active slots of this rank, in the reference's combine order.
-// slot j < topk: routed expert idx[j]; slot topk+s: shared expert s.
-__device__ __forceinline__ int active_slots(const MoeDev &L, const int32_t *idx, int (&slots)[kMaxSlots]) {
-    int n = 0;
-    for (int j = 0; j < L.topk; j++) {
-        const int e = idx[j];
-        if (e >= 0 && e < L.n_routed && (e % L.world) == L.rank) slots[n++] = j;
-    }
-    for (int s = 0; s < L.n_shared; s++)
-        if ((s % L.world) == L.rank) slots[n++] = L.topk + s;
-    return n;
-}
-
-__device__ __forceinline__ int64_t local_expert(const MoeDev &L, int e) {
-    if (L.expert_slot) return L.expert_slot[e];
-    return L.world > 1 ? e / L.world : e;
-}
-
-// ============================================================== router
-// sigmoid as the reference computes it (1/(1+expf(-x)) in float), with
-// expf taken as the correctly rounded float of the double exponential.
-__device__ __forceinline__ float sigmoid_ref(float x) {
-    const float e = (float)exp(-(double)x);
-    return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
-}
-__device__ __forceinline__ float logsigmoid_ref(float x) {
-    if (x >= 0.0f) return -log1pf((float)exp(-(double)x));
-    return x - log1pf((float)exp((double)x));
-}
-
-// Order-preserving 32-bit key of a score: larger key = larger score, +0 and
-// -0 equal (they compare equal in the reference's scan). 0 is below every
-// score's key and marks a taken or absent entry.
-__device__ __forceinline__ uint32_t score_key(float f) {
-    const uint32_t u = __float_as_uint(f == 0.0f ? 0.0f : f);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-// moe_route_select (src/sepia.c:1329-1375) on one warp. Expert e's key sits
-// in lane e % 32, register e / 32. The reference's repeated strict-'>' scan
-// picks, at each step, the highest remaining score and the lowest index
-// among equal ones: per step a warp max of the keys (redux.sync), then a
-// warp min of the indices holding that key. Weights: log-sigmoid softmax
-// over the k raw logits and the shared-sink logits, in slot order.
-template <int KPL>
-__device__ __forceinline__ void router_select(const MoeDev &L, const float2 *row_out, int32_t *topk_idx,
-                                              float *weights, int lane) {
-    uint32_t key[KPL];
-#pragma unroll
-    for (int j = 0; j < KPL; j++) {
-        const int e = lane + 32 * j;
-        key[j] = e < L.n_routed ? score_key(__ldcg(&row_out[e].x)) : 0u;
-    }
-    int my_sel = -1;        // lane j < topk: the j-th pick
-    for (int k = 0; k < L.topk; k++) {
-        uint32_t m = 0;
-#pragma unroll
-        for (int j = 0; j < KPL; j++) m = max(m, key[j]);
-        m = __reduce_max_sync(0xffffffffu, m);
-        uint32_t cand = 0xFFFFFFFFu;
-#pragma unroll
-        for (int j = KPL - 1; j >= 0; j--)
-            if (key[j] == m) cand = (uint32_t)(lane + 32 * j);
-        const int e = (int)__reduce_min_sync(0xffffffffu, cand);
-#pragma unroll
-        for (int j = 0; j < KPL; j++)
-            if (lane + 32 * j == e) key[j] = 0u;
-        if (lane == k) my_sel = e;
-    }
-    const int n_sel = L.topk + L.n_shared;
-    float lp = -INFINITY;
-    if (lane < n_sel) lp = __ldcg(&row_out[lane < L.topk ? my_sel : L.n_routed + (lane - L.topk)].y);
-    float lmax = lp;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
-    const double ex = (lane < n_sel) ? exp((double)(lp - lmax)) : 0.0;
-    double se = 0.0;
-    for (int j = 0; j < n_sel; j++) se += __shfl_sync(0xffffffffu, ex, j);   // slot order
-    const double lse = (double)lmax + log(se);
-    const double scl = (double)L.route_scale * (double)L.global_scale;
-    if (lane < n_sel) weights[lane] = (float)(exp((double)lp - lse) * scl);
-    if (lane < L.topk) topk_idx[lane] = my_sel;
-}
 
 // Router GEMV: the [n_total, hidden] f32 matrix is cut into chunks of
 // kRouterChunk consecutive elements of one row; one warp per chunk, every
@@ -679,17 +565,6 @@ __global__ void k_combine(const float *slots, int n_slots, int64_t hidden, float
 // (shared experts for gate/up, every down matrix) while the predecessor
 // finishes.
 
-// Per-slot row sources of one launch, kept in the engine's shared job
-// scratch: matrix bases (gate/up, or down), row bytes, format and splits;
-// nsplit = 0 for slots this rank does not own; w = the slot's combine
-// weight (down kernel: routed slots' router weights, 1 for shared ones).
-struct MoeSlot {
-    const uint8_t *a, *b;
-    int64_t rb;
-    int type, sbs, nsplit;
-    float w;
-};
-static_assert(kMaxSlots * sizeof(MoeSlot) <= (size_t)kQeJobSmem, "slot table exceeds the job scratch");
 
 // Units: (slot, 8-row block of ff): MMA rows 0-7 are the gate rows, 8-15 the
 // matching up rows. Shared slots come first: they do not depend on the router.
@@ -839,7 +714,7 @@ struct DnJob {
 };
 
 // ============================================================== host side
-static int to_dev(const SepiaMoeLayer *in, MoeDev &L) {
+int to_dev(const SepiaMoeLayer *in, MoeDev &L) {
     if (!in) return fail("moe: null layer");
     L.hidden = in->hidden; L.ff = in->ff;
     L.n_routed = in->n_routed; L.n_shared = in->n_shared; L.topk = in->topk;
@@ -933,7 +808,7 @@ static int pick_tr(int64_t rb_pair, int64_t budget) {
 static bool rows_ok(const void *base, int64_t stride, int64_t rb) {
     return ((reinterpret_cast<uintptr_t>(base) | (uintptr_t)stride | (uintptr_t)rb) & 3) == 0;
 }
-static bool engine_gateup_ok(const MoeDev &L, const SepiaMoeWork *ws) {
+bool engine_gateup_ok(const MoeDev &L, const SepiaMoeWork *ws) {
     if (L.hidden % kQK || L.ff % kQK || L.hidden / kQK > 64 || L.ff / kQK > 16) return false;
     if (!mma_format(L.gate_type) || L.up_type != L.gate_type) return false;
     if (!rows_ok(L.gate, L.gate_stride, L.rb_gate) || !rows_ok(L.up, L.up_stride, L.rb_up) ||
@@ -947,7 +822,7 @@ static bool engine_gateup_ok(const MoeDev &L, const SepiaMoeWork *ws) {
     }
     return true;
 }
-static bool engine_down_ok(const MoeDev &L, const SepiaMoeWork *ws) {
+bool engine_down_ok(const MoeDev &L, const SepiaMoeWork *ws) {
     if (L.ff % kQK || L.ff / kQK > 16) return false;
     if (!mma_format(L.down_type) || !rows_ok(L.down, L.down_stride, L.rb_down)) return false;
     if (L.n_shared > 0 && (!mma_format(L.sh_down_type) || !rows_ok(L.sh_down, L.sh_down_stride, L.rb_sh_down)))
@@ -1141,6 +1016,8 @@ extern "C" size_t sepia_cuda_moe_work_bytes(const SepiaMoeLayer *L) {
     add(n_slots * (size_t)L->hidden * 4);  // slots
     add(256);                         // counter
     add(n_total * (size_t)router_chunks(L->hidden) * 8);  // router_part
+    add(moe_fused_sync_bytes(L));     // sync
+    add(moe_fused_htab_bytes(L));     // htab
     return b;
 }
 
@@ -1160,6 +1037,8 @@ extern "C" int sepia_cuda_moe_work_carve(const SepiaMoeLayer *L, void *base, siz
     ws->slots = (float *)take(n_slots * (size_t)L->hidden * 4);
     ws->counter = (unsigned int *)take(256);
     ws->router_part = (double *)take(n_total * (size_t)router_chunks(L->hidden) * 8);
+    ws->sync = (unsigned int *)take(moe_fused_sync_bytes(L));
+    ws->htab = take(moe_fused_htab_bytes(L));
     return 1;
 }
 

@@ -56,16 +56,6 @@ constexpr int kTabSB = 1296;     // activation-table bytes per superblock (16-by
 // MMA; columns 5-7 are zero).
 constexpr int kTabG16 = 1024, kTabG32 = 1152, kTabUnit = 1280;
 
-// Balanced base-256 digits of v (|v| <= 2^30): v = d0 + 256 d1 + 65536 d2 + 2^24 d3.
-__device__ __forceinline__ void limbs4(int v, int (&d)[4]) {
-#pragma unroll
-    for (int j = 0; j < 3; j++) {
-        const int lo = ((v + 128) & 255) - 128;
-        d[j] = lo;
-        v = (v - lo) >> 8;
-    }
-    d[3] = v;
-}
 // Five balanced base-256 digits of v (|v| < 2^38).
 __device__ __forceinline__ void limbs5(long long v, int (&d)[5]) {
 #pragma unroll
@@ -105,22 +95,32 @@ __device__ inline void xtab_emit(uint8_t *te, const float (&v)[8], int lane) {
     int e = (m > 0.f) ? ((__float_as_int(m) >> 23) & 0xFF) - 127 : 0;
     e = max(-90, min(e, 90));
     const float scale = __int_as_float((127 + kXShift - e) << 23);
+    // Balanced base-256 digits by one biased add: u = xi + 0x808080 has
+    // bytes 0-2 equal to d_j + 128 (each digit in [-128, 127]) and byte 3
+    // equal to d3 (|xi| <= 2^30), so each limb byte is a byte of u, the low
+    // three with the bias bit flipped (d + 128 -> d as a signed byte). A
+    // 4 x 4 byte transpose (8 prmt) turns the u of 4 elements into the 4
+    // limb words of those elements.
     int xi[8];
-    uint32_t w0[4] = {0, 0, 0, 0}, w1[4] = {0, 0, 0, 0};
+    uint32_t wl[2][4];
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        xi[j] = __float2int_rn(v[j] * scale);
-        int d[4];
-        limbs4(xi[j], d);
+    for (int hq = 0; hq < 2; hq++) {
+        uint32_t u[4];
 #pragma unroll
-        for (int l = 0; l < 4; l++) {
-            if (j < 4) w0[l] |= (uint32_t)(d[l] & 255) << (8 * j);
-            else w1[l] |= (uint32_t)(d[l] & 255) << (8 * (j - 4));
+        for (int j = 0; j < 4; j++) {
+            xi[4 * hq + j] = __float2int_rn(v[4 * hq + j] * scale);
+            u[j] = (uint32_t)xi[4 * hq + j] + 0x808080u;
         }
+        const uint32_t t01l = __byte_perm(u[0], u[1], 0x5140), t01h = __byte_perm(u[0], u[1], 0x7362);
+        const uint32_t t23l = __byte_perm(u[2], u[3], 0x5140), t23h = __byte_perm(u[2], u[3], 0x7362);
+        wl[hq][0] = __byte_perm(t01l, t23l, 0x5410) ^ 0x80808080u;
+        wl[hq][1] = __byte_perm(t01l, t23l, 0x7632) ^ 0x80808080u;
+        wl[hq][2] = __byte_perm(t01h, t23h, 0x5410) ^ 0x80808080u;
+        wl[hq][3] = __byte_perm(t01h, t23h, 0x7632);
     }
     uint2 *bd = reinterpret_cast<uint2 *>(te) + part * 16 + tig * 4;
 #pragma unroll
-    for (int l = 0; l < 4; l++) bd[l] = make_uint2(w0[l], w1[l]);
+    for (int l = 0; l < 4; l++) bd[l] = make_uint2(wl[0][l], wl[1][l]);
     // group sums: group 2*part = elements 0-15 of the part (lanes tig
     // 0,1), group 2*part+1 = elements 16-31 (lanes tig 2,3)
     long long gs = 0;

@@ -36,7 +36,7 @@ class SepiaMoeLayer(C.Structure):
 
 
 class SepiaMoeWork(C.Structure):
-    _fields_ = [("logits", vp), ("topk_idx", vp), ("weights", vp), ("h", vp), ("slots", vp), ("counter", vp), ("router_part", vp)]
+    _fields_ = [("logits", vp), ("topk_idx", vp), ("weights", vp), ("h", vp), ("slots", vp), ("counter", vp), ("router_part", vp), ("sync", vp), ("htab", vp)]
 
 
 class SepiaGpuMoeDesc(C.Structure):
@@ -131,6 +131,8 @@ _PROTOS = {
     "sepia_cuda_moe_down": (C.c_int, [C.POINTER(SepiaMoeLayer), C.POINTER(SepiaMoeWork), vp, C.c_int, vp]),
     "sepia_cuda_moe_combine": (C.c_int, [C.POINTER(SepiaMoeLayer), C.POINTER(SepiaMoeWork), vp, vp]),
     "sepia_cuda_moe_layer": (C.c_int, [C.POINTER(SepiaMoeLayer), vp, C.POINTER(SepiaMoeWork), vp, vp]),
+    "sepia_cuda_moe_fused_eligible": (C.c_int, [C.POINTER(SepiaMoeLayer), C.POINTER(SepiaMoeWork)]),
+    "sepia_cuda_moe_layer_fused": (C.c_int, [C.POINTER(SepiaMoeLayer), vp, C.POINTER(SepiaMoeWork), vp, vp]),
     "sepia_cuda_topk_select": (C.c_int, [vp, i32, i32, vp, vp]),
     "sepia_cuda_rel_project": (C.c_int, [vp, vp, vp, i64, i64, i64, i64, vp]),
     "sepia_cuda_banded_attn_ws_bytes": (C.c_size_t, [i64, i64, i64, i64, i64]),

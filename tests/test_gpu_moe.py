@@ -208,3 +208,52 @@ def test_config2_full_layer_seeds_1_to_64(lib, oracle):
         assert err <= TOL, (seed, err)
     del D
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("name", ["baseline_types_small", "baseline_types_full_dims"])
+def test_fused_layer_matches_kernel_chain(layers, lib, name):
+    """The single-launch layer (router, top-k, gate/up, down and combine in
+    one persistent kernel) against the four-kernel chain on the same inputs:
+    identical expert ids and weights, outputs within 1e-6 (the two paths sum
+    the fp64 partials of a row in different groupings). Repeated calls and a
+    CUDA-graph replay check that every launch leaves its counters zeroed."""
+    import torch
+    from sepia_b200.lib import ok
+    H, D = layers[name]
+    Ls, ws = C.byref(D.struct), C.byref(D.ws)
+    assert lib.sepia_cuda_moe_fused_eligible(Ls, ws) == 1
+    st = torch.cuda.current_stream().cuda_stream
+    out_f = torch.empty(H.hidden, device="cuda")
+    out_c = torch.empty(H.hidden, device="cuda")
+    xin = torch.empty(H.hidden, device="cuda")
+    g = None
+    for rep, seed in enumerate((3, 9, 3, 40)):
+        x = torch.from_numpy(hidden_state(seed, H.hidden)).cuda()
+        ok(lib.sepia_cuda_moe_router(Ls, x.data_ptr(), ws, st))
+        ok(lib.sepia_cuda_moe_experts(Ls, x.data_ptr(), ws, out_c.data_ptr(), 0, st))
+        torch.cuda.synchronize()
+        idx_c, w_c = D.topk_idx.clone(), D.weights.clone()
+        if rep < 3:
+            ok(lib.sepia_cuda_moe_layer_fused(Ls, x.data_ptr(), ws, out_f.data_ptr(), st))
+        else:
+            xin.copy_(x)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                ok(lib.sepia_cuda_moe_layer_fused(Ls, xin.data_ptr(), ws, out_f.data_ptr(),
+                                                  torch.cuda.current_stream().cuda_stream))
+            for _ in range(3):
+                g.replay()
+        torch.cuda.synchronize()
+        assert lib.sepia_cuda_device_error(None) == 0
+        assert torch.equal(D.topk_idx, idx_c), (rep, seed)
+        assert torch.equal(D.weights, w_c), (rep, seed)
+        a, b = out_f.cpu().numpy().astype(np.float64), out_c.cpu().numpy().astype(np.float64)
+        den = np.maximum(np.abs(b), 1e-3 * np.abs(b).max())
+        assert float(np.max(np.abs(a - b) / den)) <= 1e-6, (rep, seed)
+
+
+def test_fused_not_taken_for_other_formats(layers, lib):
+    """Layers whose experts are not in the tensor-core formats are not eligible."""
+    H, D = layers["inkling_real_types"]
+    assert lib.sepia_cuda_moe_fused_eligible(C.byref(D.struct), C.byref(D.ws)) == 0
