@@ -713,6 +713,22 @@ struct DnJob {
     }
 };
 
+// The same jobs for launches that carry IQ grid-codebook formats (the
+// engine stages their codebooks in shared memory).
+struct GuIqJob : GuJob {
+    static constexpr bool kIq = true;
+};
+struct DnIqJob : DnJob {
+    static constexpr bool kIq = true;
+};
+
+// Codebook bytes a launch over these formats stages (0: none).
+static uint32_t iq_bytes_for(int a, int b) {
+    if (a == T_IQ1_S || b == T_IQ1_S) return kIqBytes1s;
+    return (iq_format(a) || iq_format(b)) ? kIqBytes : 0u;
+}
+static bool engine_format(int t) { return mma_format(t) || iq_format(t); }
+
 // ============================================================== host side
 int to_dev(const SepiaMoeLayer *in, MoeDev &L) {
     if (!in) return fail("moe: null layer");
@@ -810,12 +826,12 @@ static bool rows_ok(const void *base, int64_t stride, int64_t rb) {
 }
 bool engine_gateup_ok(const MoeDev &L, const SepiaMoeWork *ws) {
     if (L.hidden % kQK || L.ff % kQK || L.hidden / kQK > 64 || L.ff / kQK > 16) return false;
-    if (!mma_format(L.gate_type) || L.up_type != L.gate_type) return false;
+    if (!engine_format(L.gate_type) || L.up_type != L.gate_type) return false;
     if (!rows_ok(L.gate, L.gate_stride, L.rb_gate) || !rows_ok(L.up, L.up_stride, L.rb_up) ||
         ((reinterpret_cast<uintptr_t>(L.gate) ^ reinterpret_cast<uintptr_t>(L.up)) & 3))
         return false;
     if (L.n_shared > 0) {
-        if (!mma_format(L.sh_gate_type) || L.sh_up_type != L.sh_gate_type) return false;
+        if (!engine_format(L.sh_gate_type) || L.sh_up_type != L.sh_gate_type) return false;
         if (!rows_ok(L.sh_gate, L.sh_gate_stride, L.rb_sh_gate) || !rows_ok(L.sh_up, L.sh_up_stride, L.rb_sh_up) ||
             ((reinterpret_cast<uintptr_t>(L.sh_gate) ^ reinterpret_cast<uintptr_t>(L.sh_up)) & 3))
             return false;
@@ -824,8 +840,8 @@ bool engine_gateup_ok(const MoeDev &L, const SepiaMoeWork *ws) {
 }
 bool engine_down_ok(const MoeDev &L, const SepiaMoeWork *ws) {
     if (L.ff % kQK || L.ff / kQK > 16) return false;
-    if (!mma_format(L.down_type) || !rows_ok(L.down, L.down_stride, L.rb_down)) return false;
-    if (L.n_shared > 0 && (!mma_format(L.sh_down_type) || !rows_ok(L.sh_down, L.sh_down_stride, L.rb_sh_down)))
+    if (!engine_format(L.down_type) || !rows_ok(L.down, L.down_stride, L.rb_down)) return false;
+    if (L.n_shared > 0 && (!engine_format(L.sh_down_type) || !rows_ok(L.sh_down, L.sh_down_stride, L.rb_sh_down)))
         return false;
     return true;
 }
@@ -839,7 +855,8 @@ static int launch_gateup_engine(const MoeDev &L, const float *x, const SepiaMoeW
     J.nsb_h = (int)(L.hidden / kQK); J.tpu = (int)(L.ff / 8);
     J.inv_tpu = 1.0f / (float)J.tpu;
     J.n_slots = L.topk + L.n_shared;
-    const uint32_t budget = qe_row_budget(di.smem_optin, (int64_t)J.nsb_h * kTabSB);
+    const uint32_t iqb = iq_bytes_for(L.gate_type, L.n_shared ? L.sh_gate_type : L.gate_type);
+    const uint32_t budget = qe_row_budget(di.smem_optin, (int64_t)J.nsb_h * kTabSB + iqb);
     J.sbs_r = qe_sbs(L.gate_type, J.nsb_h, budget, J.nsplit_r);
     J.sbs_s = J.sbs_r; J.nsplit_s = J.nsplit_r;
     if (L.n_shared) J.sbs_s = qe_sbs(L.sh_gate_type, J.nsb_h, budget, J.nsplit_s);
@@ -850,14 +867,20 @@ static int launch_gateup_engine(const MoeDev &L, const float *x, const SepiaMoeW
     qe_groups(std::max(J.sbs_r, J.sbs_s), cg, G);
     QeLayout P;
     int64_t smem = 0;
-    if (!qe_layout(P, G, cg, row_max, 1, J.nsb_h, di.smem_optin, smem))
+    if (!qe_layout(P, G, cg, row_max, 1, J.nsb_h, di.smem_optin, smem, iqb))
         return fail("moe: gate/up tile needs %lld B of shared memory", (long long)smem);
     P.err = di.err;
-    const void *fn = (const void *)k_qengine<GuJob>;
-    if (!ensure_smem(fn, (int)smem)) return 0;
     const int64_t units = (int64_t)J.n_slots * J.tpu;
     if (units >= kQeDivMax) return fail("moe: %lld gate/up units exceed the engine's index range", (long long)units);
     const unsigned grid = (unsigned)std::min<int64_t>(units, di.sm_count);
+    if (iqb) {
+        GuIqJob JI;
+        static_cast<GuJob &>(JI) = J;
+        if (!ensure_smem((const void *)k_qengine<GuIqJob>, (int)smem)) return 0;
+        return check(launch_pdl(k_qengine<GuIqJob>, grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, JI, P),
+                     "moe gate/up (tensor cores) launch");
+    }
+    if (!ensure_smem((const void *)k_qengine<GuJob>, (int)smem)) return 0;
     return check(launch_pdl(k_qengine<GuJob>, grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, J, P),
                  "moe gate/up (tensor cores) launch");
 }
@@ -873,7 +896,8 @@ static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *ou
     J.n_tiles = (int)((L.hidden + 15) / 16);
     J.inv_slots = 1.0f / (float)J.n_slots;
     if ((int64_t)J.n_slots * J.n_tiles >= kQeDivMax) return fail("moe: too many down units");
-    const uint32_t budget = qe_row_budget(di.smem_optin, (int64_t)J.n_slots * J.nsb_f * kTabSB);
+    const uint32_t iqb = iq_bytes_for(L.down_type, L.n_shared ? L.sh_down_type : L.down_type);
+    const uint32_t budget = qe_row_budget(di.smem_optin, (int64_t)J.n_slots * J.nsb_f * kTabSB + iqb);
     J.sbs_r = qe_sbs(L.down_type, J.nsb_f, budget, J.nsplit_r);
     J.sbs_s = J.sbs_r; J.nsplit_s = J.nsplit_r;
     if (L.n_shared) J.sbs_s = qe_sbs(L.sh_down_type, J.nsb_f, budget, J.nsplit_s);
@@ -884,10 +908,10 @@ static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *ou
     qe_groups(std::max(J.sbs_r, J.sbs_s), cg, G);
     QeLayout P;
     int64_t smem = 0;
-    if (!qe_layout(P, G, cg, row_max, J.n_slots, J.nsb_f, di.smem_optin, smem))
+    if (!qe_layout(P, G, cg, row_max, J.n_slots, J.nsb_f, di.smem_optin, smem, iqb))
         return fail("moe: down tile needs %lld B of shared memory", (long long)smem);
     P.err = di.err;
-    const void *fn = (const void *)k_qengine<DnJob>;
+    const void *fn = iqb ? (const void *)k_qengine<DnIqJob> : (const void *)k_qengine<DnJob>;
     if (!ensure_smem(fn, (int)smem)) return 0;
     if (slots_out && clear &&
         !check(cudaMemsetAsync(slots_out, 0, (size_t)J.n_slots * L.hidden * sizeof(float), st), "moe slot clear"))
@@ -896,8 +920,14 @@ static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *ou
     // the combine
     const int64_t units = (int64_t)J.n_slots * J.n_tiles;
     const unsigned grid = (unsigned)std::min<int64_t>(units, di.sm_count);
-    if (!check(launch_pdl(k_qengine<DnJob>, grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, J, P),
-               "moe down (tensor cores) launch"))
+    if (iqb) {
+        DnIqJob JI;
+        static_cast<DnJob &>(JI) = J;
+        if (!check(launch_pdl(k_qengine<DnIqJob>, grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, JI, P),
+                   "moe down (tensor cores) launch"))
+            return 0;
+    } else if (!check(launch_pdl(k_qengine<DnJob>, grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, J, P),
+                      "moe down (tensor cores) launch"))
         return 0;
     if (slots_out) return 1;
     return check(launch_pdl(k_combine, (unsigned)((L.hidden + 255) / 256), 256, 0, st, (const float *)J.slots_out,

@@ -1012,8 +1012,14 @@ size_t moe_fused_htab_bytes(const SepiaMoeLayer *L) {
 
 // 1 = launched, 0 = error (message set), -1 = this layer does not take the
 // fused path (the caller runs the kernel chain).
+// The fused kernel walks the K-quant tiles only (no IQ codebook staging).
+static bool fused_formats_ok(const MoeDev &L) {
+    return mma_format(L.gate_type) && mma_format(L.down_type) &&
+           (L.n_shared == 0 || (mma_format(L.sh_gate_type) && mma_format(L.sh_down_type)));
+}
+
 int launch_moe_fused(const MoeDev &L, const float *x, const SepiaMoeWork *ws, float *out, cudaStream_t st) {
-    if (!ws->sync || !ws->htab) return -1;
+    if (!ws->sync || !ws->htab || !fused_formats_ok(L)) return -1;
     if (!engine_gateup_ok(L, ws) || !engine_down_ok(L, ws)) return -1;
     FArgs A;
     int64_t smem = 0;
@@ -1049,7 +1055,9 @@ int launch_moe_fused(const MoeDev &L, const float *x, const SepiaMoeWork *ws, fl
 extern "C" int sepia_cuda_moe_fused_eligible(const SepiaMoeLayer *Lh, const SepiaMoeWork *ws) {
     sepia::MoeDev L;
     if (!Lh || !ws || !sepia::to_dev(Lh, L)) return 0;
-    if (!ws->sync || !ws->htab || !sepia::engine_gateup_ok(L, ws) || !sepia::engine_down_ok(L, ws)) return 0;
+    if (!ws->sync || !ws->htab || !sepia::fused_formats_ok(L) || !sepia::engine_gateup_ok(L, ws) ||
+        !sepia::engine_down_ok(L, ws))
+        return 0;
     sepia::FArgs A;
     int64_t smem = 0;
     int grid = 0;

@@ -168,6 +168,22 @@ struct MvJob {
     }
 };
 
+// The same job for the IQ grid-codebook formats (codebooks staged in shared
+// memory).
+struct MvIqJob : MvJob {
+    static constexpr bool kIq = true;
+};
+
+template <class Job>
+static int launch_mv_job(const Job &J, const QeLayout &P, int64_t smem, int64_t out_dim, cudaStream_t st) {
+    const DevInfo &di = dev_info();
+    const void *fn = (const void *)k_qengine<Job>;
+    if (!ensure_smem(fn, (int)smem)) return 0;
+    const int64_t units = (out_dim + 15) / 16;
+    const int64_t grid = std::min<int64_t>(units, (int64_t)di.sm_count);
+    return check(launch_pdl(k_qengine<Job>, (unsigned)grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, J, P),
+                 "matvec_q (tensor cores) launch");
+}
 
 static int launch_matvec_engine(int t, const void *w, const float *x, float *y, int64_t out_dim, int64_t in_dim,
                                 int64_t rb, cudaStream_t st, long long wait_cycles = kWaitCycles,
@@ -178,23 +194,24 @@ static int launch_matvec_engine(int t, const void *w, const float *x, float *y, 
     J.rb = rb; J.out_dim = out_dim; J.type = t;
     J.nsb = (int)(in_dim / kQK);
     J.x = x; J.y = y;
-    J.sbs = qe_sbs(t, J.nsb, qe_row_budget(di.smem_optin, (int64_t)J.nsb * kTabSB), J.nsplit);
+    const uint32_t iqb = iq_format(t) ? (t == T_IQ1_S ? kIqBytes1s : kIqBytes) : 0u;
+    J.sbs = qe_sbs(t, J.nsb, qe_row_budget(di.smem_optin, (int64_t)J.nsb * kTabSB + iqb), J.nsplit);
     if (!J.sbs) return fail("matvec_q: no tensor-core split for type %d", t);
     QeLayout P;
     int cg, G;
     qe_groups(J.sbs, cg, G);
     int64_t smem = 0;
-    if (!qe_layout(P, G, cg, (uint32_t)J.sbs * qe_sb_bytes(t), 1, J.nsb, di.smem_optin, smem))
+    if (!qe_layout(P, G, cg, (uint32_t)J.sbs * qe_sb_bytes(t), 1, J.nsb, di.smem_optin, smem, iqb))
         return fail("matvec_q: tensor-core tile needs %lld B of shared memory", (long long)smem);
     P.err = di.err;
     P.wait_cycles = wait_cycles;
     P.test_extra_tx = test_extra_tx;
-    const void *fn = (const void *)k_qengine<MvJob>;
-    if (!ensure_smem(fn, (int)smem)) return 0;
-    const int64_t units = (out_dim + 15) / 16;
-    const int64_t grid = std::min<int64_t>(units, (int64_t)di.sm_count);
-    return check(launch_pdl(k_qengine<MvJob>, (unsigned)grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, J, P),
-                 "matvec_q (tensor cores) launch");
+    if (iqb) {
+        MvIqJob JI;
+        static_cast<MvJob &>(JI) = J;
+        return launch_mv_job(JI, P, smem, out_dim, st);
+    }
+    return launch_mv_job(J, P, smem, out_dim, st);
 }
 
 // Up to kMvMulti matrices of one format and input width sharing one input x
@@ -247,8 +264,9 @@ struct MvNJob {
 // 4-byte aligned superblocks (2-byte for Q3_K).
 static bool engine_ok(int t, const void *w, const float *x, int64_t in_dim, int64_t rb, int64_t n_vec) {
     const uintptr_t wa = reinterpret_cast<uintptr_t>(w);
-    return mma_format(t) && n_vec == 1 && in_dim % kQK == 0 && in_dim / kQK <= 80 && rb % 4 == 0 &&
-           (wa & (t == T_Q3_K ? 1 : 3)) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    return (mma_format(t) || iq_format(t)) && n_vec == 1 && in_dim % kQK == 0 && in_dim / kQK <= 80 &&
+           rb % 4 == 0 && (wa & ((t == T_Q3_K || iq_format(t)) ? 1 : 3)) == 0 &&
+           (reinterpret_cast<uintptr_t>(x) & 15) == 0;
 }
 
 // Exact dequantisation: one thread per 32-element part.
@@ -637,7 +655,7 @@ int launch_matvec_q_multi(int n, int t, const void *const *w, const int64_t *row
                           float *const *y, cudaStream_t st) {
     if (n < 1 || n > kMvMulti) return fail("matvec_q_multi: %d matrices (1..%d)", n, kMvMulti);
     const int64_t rb = host_row_bytes(t, in_dim);
-    bool eng = rb > 0;
+    bool eng = rb > 0 && mma_format(t);     // (the multi job stages no IQ codebooks)
     for (int i = 0; i < n && eng; i++) eng = rows[i] > 0 && engine_ok(t, w[i], x, in_dim, rb, 1);
     if (!eng) {
         for (int i = 0; i < n; i++)

@@ -466,6 +466,210 @@ __device__ __forceinline__ void sb_q4k(const uint8_t *bg, const uint8_t *bg8, co
            (double)(cvt16<true>(dd8 >> 16) * ug) * (double)(cm[2] + 256 * cm[3]);
 }
 
+// ------------------------------------------------------------ IQ formats
+// Grid-codebook formats (gguf IQ2_XXS, IQ2_XS, IQ3_XXS, IQ1_S). A lane's 8
+// elements of a part (8tig..8tig+7) are exactly one codebook row, so its A
+// registers are that row's bytes, signed (s8 x s8 MMA): a0 / a1 the row's
+// elements 0-3, a2 / a3 elements 4-7. Codebooks and sign masks live in a
+// shared-memory region the engine fills once per CTA (iq_tabs_fill):
+//   [0, 2048)       sign masks of the 7-bit sign fields: uint4 {m_lo, m_hi,
+//                   m_lo & 0x01010101, m_hi & 0x01010101}, m = 0xFF in every
+//                   byte whose element is negated (bit 7 = parity of the
+//                   field, gguf ksigns_iq2xs); (g ^ m) + (m & 1s) = -g per
+//                   negated byte (codebook bytes are 1..62, so no carries)
+//   [2048, 4096)    IQ2_XXS codebook, 256 x 8 bytes
+//   [4096, 8192)    IQ2_XS codebook, 512 x 8 bytes
+//   [8192, 9216)    IQ3_XXS codebook, 256 x 4 bytes
+//   [9216, 41984)   IQ1_S (only when an IQ1_S matrix is in the launch):
+//                   4096 x 8 bytes, entry e = index | (delta sign << 11),
+//                   bytes 8 g + 1 (or 8 g - 1): 8 (g + delta) as an integer
+// The per-part (2s + 1) scales multiply each part's int32 partial (IMAD);
+// IQ2_XS scales its two 16-element groups separately (split B layout, as
+// Q3_K). Value scales: IQ2_XXS / IQ2_XS d (2s+1)/8, IQ3_XXS d (2s+1)/4,
+// IQ1_S d (2s+1)/8 (src/quants.c:179-228; gguf-py IQ2_XXS / IQ1_S).
+constexpr uint32_t kIqSign = 0, kIqG2xxs = 2048, kIqG2xs = 4096, kIqG3xxs = 8192, kIqG1s = 9216;
+constexpr uint32_t kIqBytes = 9216, kIqBytes1s = 9216 + 4096 * 8;
+
+__host__ __device__ constexpr bool iq_format(int t) {
+    return t == T_IQ2_XXS || t == T_IQ2_XS || t == T_IQ3_XXS || t == T_IQ1_S;
+}
+
+// Fill the region (every thread of the CTA calls it; caller synchronises).
+__device__ inline void iq_tabs_fill(uint8_t *r, bool with_1s, int tid, int nthreads) {
+    for (int s = tid; s < 128; s += nthreads) {
+        const uint32_t b = sepia_ksigns_iq2xs[s];
+        // bit j of b -> bit 7 of byte j (copies of the nibble 7 bits apart
+        // never overlap), then a sign-replicating byte permute (prmt; the
+        // __byte_perm intrinsic ignores the replicate bit)
+        const uint32_t wl = (b & 15u) * 0x10204080u, wh = (b >> 4) * 0x10204080u;
+        const uint32_t ml = (uint32_t)prmt_sel(wl, 0xBA98u), mh = (uint32_t)prmt_sel(wh, 0xBA98u);
+        reinterpret_cast<uint4 *>(r + kIqSign)[s] = make_uint4(ml, mh, ml & 0x01010101u, mh & 0x01010101u);
+    }
+    for (int i = tid; i < 256; i += nthreads) {
+        reinterpret_cast<uint64_t *>(r + kIqG2xxs)[i] = sepia_iq2xxs_grid[i];
+        reinterpret_cast<uint32_t *>(r + kIqG3xxs)[i] = sepia_iq3xxs_grid[i];
+    }
+    for (int i = tid; i < 512; i += nthreads) reinterpret_cast<uint64_t *>(r + kIqG2xs)[i] = sepia_iq2xs_grid[i];
+    if (with_1s) {
+        for (int e = tid; e < 4096; e += nthreads) {
+            const uint64_t g = sepia_iq1s_grid[e & 2047];
+            const uint32_t add = (e & 2048) ? 0xFFu : 0x01u;     // -1 or +1 per byte
+            uint32_t w[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t gw = (uint32_t)(g >> (32 * h));
+                uint32_t o = 0;
+#pragma unroll
+                for (int j = 0; j < 4; j++) o |= ((((gw >> (8 * j)) * 8u) + add) & 255u) << (8 * j);
+                w[h] = o;
+            }
+            reinterpret_cast<uint2 *>(r + kIqG1s)[e] = make_uint2(w[0], w[1]);
+        }
+    }
+}
+
+__device__ __forceinline__ void mma_k32_ss_z(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ uint2 lds64(const uint8_t *p) { return *reinterpret_cast<const uint2 *>(p); }
+__device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+__device__ __forceinline__ uint32_t ldh(const uint8_t *p) { return *reinterpret_cast<const uint16_t *>(p); }
+
+// codebook row g (8 bytes) with the signs of mask entry m applied
+__device__ __forceinline__ void iq_signed(uint2 g, uint4 m, uint32_t &lo, uint32_t &hi) {
+    lo = (g.x ^ m.x) + m.z;
+    hi = (g.y ^ m.y) + m.w;
+}
+
+// Superblock walks: ODD = the superblock starts 2 bytes past a 4-byte
+// boundary (every IQ superblock size is 2 mod 4).
+template <bool ODD>
+__device__ __forceinline__ void sb_iq2xxs(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const uint8_t *iq,
+                                          const LaneCtx &C, double &yg, double &yg8) {
+    // part p: 4 codebook indices at 2+8p, then a word of four 7-bit sign
+    // fields and the 4-bit scale (bits 28-31)
+    const uint32_t sh = 7u * (uint32_t)C.tig;
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int p = 0; p < 8; p++) {
+        const uint32_t sg = ldw2<!ODD>(bg + 6 + 8 * p), sg8 = ldw2<!ODD>(bg8 + 6 + 8 * p);
+        const uint32_t ix = bg[2 + 8 * p + C.tig], ix8 = bg8[2 + 8 * p + C.tig];
+        const uint2 g = lds64(iq + kIqG2xxs + 8 * ix), g8 = lds64(iq + kIqG2xxs + 8 * ix8);
+        const uint4 m = lds128(iq + kIqSign + 16 * ((sg >> sh) & 127u));
+        const uint4 m8 = lds128(iq + kIqSign + 16 * ((sg8 >> sh) & 127u));
+        uint32_t a0, a1, a2, a3;
+        iq_signed(g, m, a0, a2);
+        iq_signed(g8, m8, a1, a3);
+        const uint2 b = ld_b(te, p, C);
+        int cc[4];
+        mma_k32_ss_z(cc, a0, a1, a2, a3, b.x, b.y);
+        const int s = (int)((sg >> 27) | 1u), s8 = (int)((sg8 >> 27) | 1u);     // 2 * scale + 1
+        acc[0] += s * cc[0];
+        acc[1] += s * cc[1];
+        acc[2] += s8 * cc[2];
+        acc[3] += s8 * cc[3];
+    }
+    const float u = ld_unit(te) * C.lwn * 0.125f;
+    yg += (double)(cvt16<true>(ldh(bg)) * u) * limb_pair(acc[0], acc[1], 1.0f);
+    yg8 += (double)(cvt16<true>(ldh(bg8)) * u) * limb_pair(acc[2], acc[3], 1.0f);
+}
+
+template <bool ODD>
+__device__ __forceinline__ void sb_iq2xs(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const uint8_t *iq,
+                                         const LaneCtx &C, double &yg, double &yg8) {
+    // part p, group l: uint16 at 2+8p+2l = 9-bit codebook index | 7-bit
+    // sign field << 9; scale byte 66+p: low nibble elements 0-15, high 16-31
+    const uint32_t ssh = 4u * (uint32_t)(C.tig >> 1);
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int p = 0; p < 8; p++) {
+        const uint32_t q = ldh(bg + 2 + 8 * p + 2 * C.tig), q8 = ldh(bg8 + 2 + 8 * p + 2 * C.tig);
+        const uint2 g = lds64(iq + kIqG2xs + 8 * (q & 511u)), g8 = lds64(iq + kIqG2xs + 8 * (q8 & 511u));
+        const uint4 m = lds128(iq + kIqSign + 16 * (q >> 9)), m8 = lds128(iq + kIqSign + 16 * (q8 >> 9));
+        uint32_t a0, a1, a2, a3;
+        iq_signed(g, m, a0, a2);
+        iq_signed(g8, m8, a1, a3);
+        const uint2 e = ld_b(te, p, C);
+        int cc[4];
+        mma_k32_ss_z(cc, a0, a1, a2, a3, e.x & C.msplit, e.y & C.msplit);
+        // this lane's C columns belong to group tig/2 of the part
+        const int s = (int)(((uint32_t)bg[66 + p] >> ssh) & 15u) * 2 + 1;
+        const int s8 = (int)(((uint32_t)bg8[66 + p] >> ssh) & 15u) * 2 + 1;
+        acc[0] += s * cc[0];
+        acc[1] += s * cc[1];
+        acc[2] += s8 * cc[2];
+        acc[3] += s8 * cc[3];
+    }
+    const float u = ld_unit(te) * C.lws * 0.125f;
+    yg += (double)(cvt16<true>(ldh(bg)) * u) * limb_pair(acc[0], acc[1], 1.0f);
+    yg8 += (double)(cvt16<true>(ldh(bg8)) * u) * limb_pair(acc[2], acc[3], 1.0f);
+}
+
+template <bool ODD>
+__device__ __forceinline__ void sb_iq3xxs(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const uint8_t *iq,
+                                          const LaneCtx &C, double &yg, double &yg8) {
+    // part p: 8 codebook indices at 2+8p (group l: bytes 2l, 2l+1, 4 values
+    // each), word at 66+4p = four 7-bit sign fields | scale << 28
+    const uint32_t sh = 7u * (uint32_t)C.tig;
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int p = 0; p < 8; p++) {
+        const uint32_t sw = ldw2<!ODD>(bg + 66 + 4 * p), sw8 = ldw2<!ODD>(bg8 + 66 + 4 * p);
+        const uint32_t ii = ldh(bg + 2 + 8 * p + 2 * C.tig), ii8 = ldh(bg8 + 2 + 8 * p + 2 * C.tig);
+        const uint8_t *g3 = iq + kIqG3xxs;
+        const uint2 g = make_uint2(ldw(g3 + 4 * (ii & 255u)), ldw(g3 + 4 * (ii >> 8)));
+        const uint2 g8 = make_uint2(ldw(g3 + 4 * (ii8 & 255u)), ldw(g3 + 4 * (ii8 >> 8)));
+        const uint4 m = lds128(iq + kIqSign + 16 * ((sw >> sh) & 127u));
+        const uint4 m8 = lds128(iq + kIqSign + 16 * ((sw8 >> sh) & 127u));
+        uint32_t a0, a1, a2, a3;
+        iq_signed(g, m, a0, a2);
+        iq_signed(g8, m8, a1, a3);
+        const uint2 b = ld_b(te, p, C);
+        int cc[4];
+        mma_k32_ss_z(cc, a0, a1, a2, a3, b.x, b.y);
+        const int s = (int)((sw >> 27) | 1u), s8 = (int)((sw8 >> 27) | 1u);
+        acc[0] += s * cc[0];
+        acc[1] += s * cc[1];
+        acc[2] += s8 * cc[2];
+        acc[3] += s8 * cc[3];
+    }
+    const float u = ld_unit(te) * C.lwn * 0.25f;
+    yg += (double)(cvt16<true>(ldh(bg)) * u) * limb_pair(acc[0], acc[1], 1.0f);
+    yg8 += (double)(cvt16<true>(ldh(bg8)) * u) * limb_pair(acc[2], acc[3], 1.0f);
+}
+
+__device__ __forceinline__ void sb_iq1s(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const uint8_t *iq,
+                                        const LaneCtx &C, double &yg, double &yg8) {
+    // part p: 4 low index bytes at 2+4p; uint16 at 34+2p = four 3-bit high
+    // index fields | scale << 12 | delta sign << 15
+    const uint32_t sh = 3u * (uint32_t)C.tig;
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int p = 0; p < 8; p++) {
+        const uint32_t h = ldh(bg + 34 + 2 * p), h8 = ldh(bg8 + 34 + 2 * p);
+        const uint32_t e = (uint32_t)bg[2 + 4 * p + C.tig] | (((h >> sh) & 7u) << 8) | ((h >> 4) & 0x800u);
+        const uint32_t e8 = (uint32_t)bg8[2 + 4 * p + C.tig] | (((h8 >> sh) & 7u) << 8) | ((h8 >> 4) & 0x800u);
+        const uint2 g = lds64(iq + kIqG1s + 8 * e), g8 = lds64(iq + kIqG1s + 8 * e8);
+        const uint2 b = ld_b(te, p, C);
+        int cc[4];
+        mma_k32_ss_z(cc, g.x, g8.x, g.y, g8.y, b.x, b.y);
+        const int s = (int)(((h >> 11) & 14u) | 1u), s8 = (int)(((h8 >> 11) & 14u) | 1u);
+        acc[0] += s * cc[0];
+        acc[1] += s * cc[1];
+        acc[2] += s8 * cc[2];
+        acc[3] += s8 * cc[3];
+    }
+    const float u = ld_unit(te) * C.lwn * 0.125f;
+    yg += (double)(cvt16<true>(ldh(bg)) * u) * limb_pair(acc[0], acc[1], 1.0f);
+    yg8 += (double)(cvt16<true>(ldh(bg8)) * u) * limb_pair(acc[2], acc[3], 1.0f);
+}
+
 // ------------------------------------------------------------ dispatch
 __host__ __device__ constexpr bool mma_format(int t) { return t == T_Q2_K || t == T_Q3_K || t == T_Q4_K; }
 
@@ -475,20 +679,44 @@ __host__ __device__ constexpr bool mma_format(int t) { return t == T_Q2_K || t =
 // flip = 1 when superblock 0 sits 2 bytes off a 4-byte boundary.
 template <int T>
 __device__ __forceinline__ void tile_sbs(const uint8_t *rg, const uint8_t *rg8, const uint8_t *te0, int i0, int i1,
-                                         int flip, const LaneCtx &C, double &yg, double &yg8) {
-    constexpr int SB = (T == T_Q2_K) ? 84 : (T == T_Q3_K) ? 110 : 144;
+                                         int flip, const LaneCtx &C, double &yg, double &yg8,
+                                         const uint8_t *iq = nullptr) {
+    constexpr int SB = fmt_block_bytes(T);
     const uint8_t *r = rg + i0 * SB, *r8 = rg8 + i0 * SB, *te = te0 + (size_t)i0 * kTabSB;
     for (int i = i0; i < i1; i++, r += SB, r8 += SB, te += kTabSB) {
+        const bool odd = (i ^ flip) & 1;
         if constexpr (T == T_Q2_K) sb_q2k(r, r8, te, C, yg, yg8);
         else if constexpr (T == T_Q3_K) {
-            if ((i ^ flip) & 1) sb_q3k<true>(r, r8, te, C, yg, yg8);
+            if (odd) sb_q3k<true>(r, r8, te, C, yg, yg8);
             else sb_q3k<false>(r, r8, te, C, yg, yg8);
-        } else sb_q4k(r, r8, te, C, yg, yg8);
+        } else if constexpr (T == T_Q4_K) sb_q4k(r, r8, te, C, yg, yg8);
+        else if constexpr (T == T_IQ2_XXS) {
+            if (odd) sb_iq2xxs<true>(r, r8, te, iq, C, yg, yg8);
+            else sb_iq2xxs<false>(r, r8, te, iq, C, yg, yg8);
+        } else if constexpr (T == T_IQ2_XS) {
+            if (odd) sb_iq2xs<true>(r, r8, te, iq, C, yg, yg8);
+            else sb_iq2xs<false>(r, r8, te, iq, C, yg, yg8);
+        } else if constexpr (T == T_IQ3_XXS) {
+            if (odd) sb_iq3xxs<true>(r, r8, te, iq, C, yg, yg8);
+            else sb_iq3xxs<false>(r, r8, te, iq, C, yg, yg8);
+        } else sb_iq1s(r, r8, te, iq, C, yg, yg8);
     }
 }
 
+// IQ = true: the launch may carry IQ formats (their tables at iq).
+template <bool IQ = false>
 __device__ __forceinline__ void tile_sbs_rt(int t, const uint8_t *rg, const uint8_t *rg8, const uint8_t *te0, int i0,
-                                            int i1, int flip, const LaneCtx &C, double &yg, double &yg8) {
+                                            int i1, int flip, const LaneCtx &C, double &yg, double &yg8,
+                                            const uint8_t *iq = nullptr) {
+    if constexpr (IQ) {
+        switch (t) {
+        case T_IQ2_XXS: tile_sbs<T_IQ2_XXS>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, iq); return;
+        case T_IQ2_XS: tile_sbs<T_IQ2_XS>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, iq); return;
+        case T_IQ3_XXS: tile_sbs<T_IQ3_XXS>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, iq); return;
+        case T_IQ1_S: tile_sbs<T_IQ1_S>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, iq); return;
+        default: break;
+        }
+    }
     switch (t) {
     case T_Q2_K: tile_sbs<T_Q2_K>(rg, rg8, te0, i0, i1, flip, C, yg, yg8); break;
     case T_Q3_K: tile_sbs<T_Q3_K>(rg, rg8, te0, i0, i1, flip, C, yg, yg8); break;

@@ -29,7 +29,7 @@ enum GgmlType : int {
 };
 
 // Elements and bytes of one ggml block (src/quants.c:28-32 + ggml).
-__host__ __device__ inline int fmt_block_elems(int t) {
+__host__ __device__ constexpr int fmt_block_elems(int t) {
     switch (t) {
     case T_F32: case T_F16: return 1;
     case T_Q8_0: return 32;
@@ -38,7 +38,7 @@ __host__ __device__ inline int fmt_block_elems(int t) {
     default: return 0;
     }
 }
-__host__ __device__ inline int fmt_block_bytes(int t) {
+__host__ __device__ constexpr int fmt_block_bytes(int t) {
     switch (t) {
     case T_F32: return 4;
     case T_F16: return 2;

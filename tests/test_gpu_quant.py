@@ -102,9 +102,10 @@ def test_matvec_unaligned_base(torch_cuda, oracle, t, off):
 @pytest.mark.parametrize("n_vec", [2, 4, 5, 16])
 def test_matvec_batched(torch_cuda, oracle, t, n_vec):
     """BASELINE configuration 3 batches (smaller, ragged row count; n_vec 5
-    leaves a partial vector group). Every vector's row values also equal
-    the batch-1 call's bit for bit: the batched path keeps the per-part
-    accumulation order."""
+    leaves a partial vector group). Batch 1 of these formats runs on the
+    tensor-core engine (exact integer dots), the batches on the CUDA-core
+    kernel (fp32 part sums): both stay within the tolerance of the oracle
+    and of each other."""
     from sepia_b200 import ops
     torch = torch_cuda
     rng = np.random.default_rng(n_vec + t)
@@ -118,7 +119,7 @@ def test_matvec_batched(torch_cuda, oracle, t, n_vec):
         assert oracle.rel_err(got[v], want) <= TOL
         if t != Q.Q2_K:
             one = ops.matvec_q(t, wd, _dev(torch, np.ascontiguousarray(X[v])), out_dim, in_dim).cpu().numpy()
-            assert np.array_equal(one, got[v])
+            assert oracle.rel_err(one, got[v]) <= TOL
 
 
 @pytest.mark.parametrize("rows", [2048, 7168, 16384])
