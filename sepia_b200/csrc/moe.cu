@@ -716,17 +716,12 @@ struct DnJob {
 // The same jobs for launches that carry IQ grid-codebook formats (the
 // engine stages their codebooks in shared memory).
 struct GuIqJob : GuJob {
-    static constexpr bool kIq = true;
+    static constexpr int kIq = -1;
 };
 struct DnIqJob : DnJob {
-    static constexpr bool kIq = true;
+    static constexpr int kIq = -1;
 };
 
-// Codebook bytes a launch over these formats stages (0: none).
-static uint32_t iq_bytes_for(int a, int b) {
-    if (a == T_IQ1_S || b == T_IQ1_S) return kIqBytes1s;
-    return (iq_format(a) || iq_format(b)) ? kIqBytes : 0u;
-}
 static bool engine_format(int t) { return mma_format(t) || iq_format(t); }
 
 // ============================================================== host side
@@ -855,7 +850,8 @@ static int launch_gateup_engine(const MoeDev &L, const float *x, const SepiaMoeW
     J.nsb_h = (int)(L.hidden / kQK); J.tpu = (int)(L.ff / 8);
     J.inv_tpu = 1.0f / (float)J.tpu;
     J.n_slots = L.topk + L.n_shared;
-    const uint32_t iqb = iq_bytes_for(L.gate_type, L.n_shared ? L.sh_gate_type : L.gate_type);
+    const IqLayout iql = iq_layout(L.gate_type, L.n_shared ? L.sh_gate_type : L.gate_type);
+    const uint32_t iqb = iql.bytes;
     const uint32_t budget = qe_row_budget(di.smem_optin, (int64_t)J.nsb_h * kTabSB + iqb);
     J.sbs_r = qe_sbs(L.gate_type, J.nsb_h, budget, J.nsplit_r);
     J.sbs_s = J.sbs_r; J.nsplit_s = J.nsplit_r;
@@ -867,7 +863,7 @@ static int launch_gateup_engine(const MoeDev &L, const float *x, const SepiaMoeW
     qe_groups(std::max(J.sbs_r, J.sbs_s), cg, G);
     QeLayout P;
     int64_t smem = 0;
-    if (!qe_layout(P, G, cg, row_max, 1, J.nsb_h, di.smem_optin, smem, iqb))
+    if (!qe_layout(P, G, cg, row_max, 1, J.nsb_h, di.smem_optin, smem, iqb ? &iql : nullptr))
         return fail("moe: gate/up tile needs %lld B of shared memory", (long long)smem);
     P.err = di.err;
     const int64_t units = (int64_t)J.n_slots * J.tpu;
@@ -896,7 +892,8 @@ static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *ou
     J.n_tiles = (int)((L.hidden + 15) / 16);
     J.inv_slots = 1.0f / (float)J.n_slots;
     if ((int64_t)J.n_slots * J.n_tiles >= kQeDivMax) return fail("moe: too many down units");
-    const uint32_t iqb = iq_bytes_for(L.down_type, L.n_shared ? L.sh_down_type : L.down_type);
+    const IqLayout iql = iq_layout(L.down_type, L.n_shared ? L.sh_down_type : L.down_type);
+    const uint32_t iqb = iql.bytes;
     const uint32_t budget = qe_row_budget(di.smem_optin, (int64_t)J.n_slots * J.nsb_f * kTabSB + iqb);
     J.sbs_r = qe_sbs(L.down_type, J.nsb_f, budget, J.nsplit_r);
     J.sbs_s = J.sbs_r; J.nsplit_s = J.nsplit_r;
@@ -908,7 +905,7 @@ static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *ou
     qe_groups(std::max(J.sbs_r, J.sbs_s), cg, G);
     QeLayout P;
     int64_t smem = 0;
-    if (!qe_layout(P, G, cg, row_max, J.n_slots, J.nsb_f, di.smem_optin, smem, iqb))
+    if (!qe_layout(P, G, cg, row_max, J.n_slots, J.nsb_f, di.smem_optin, smem, iqb ? &iql : nullptr))
         return fail("moe: down tile needs %lld B of shared memory", (long long)smem);
     P.err = di.err;
     const void *fn = iqb ? (const void *)k_qengine<DnIqJob> : (const void *)k_qengine<DnJob>;

@@ -51,10 +51,11 @@ struct QUnit {
 
 __host__ __device__ inline int qe_sb_bytes(int t) { return fmt_block_bytes(t); }
 
-// Whether a job may carry IQ formats (Job::kIq): only such launches stage
-// the IQ codebooks in shared memory and compile the IQ tile walks.
-template <class J, class = void> struct JobIq { static constexpr bool v = false; };
-template <class J> struct JobIq<J, std::void_t<decltype(J::kIq)>> { static constexpr bool v = J::kIq; };
+// Whether a job may carry IQ formats (Job::kIq; 0 = none, an IQ type = only
+// that format, -1 = any): only such launches stage the IQ codebooks in
+// shared memory and compile the IQ tile walks.
+template <class J, class = void> struct JobIq { static constexpr int v = 0; };
+template <class J> struct JobIq<J, std::void_t<decltype(J::kIq)>> { static constexpr int v = J::kIq; };
 // Row pitch in a stage for `bytes` bytes per row: 16-byte multiple with an
 // odd number of 16-byte granules (8 consecutive rows -> 8 distinct banks).
 __host__ __device__ inline uint32_t qe_pitch(uint32_t bytes) {
@@ -90,7 +91,7 @@ struct QeLayout {
     uint32_t slot_bytes, red_off, tab_off, stage_off;
     int n_tab, tab_nsb;    // tables x superblocks each
     uint32_t iq_off = 0;   // IQ codebook region (qtile.cuh), 0 = none
-    int iq_1s = 0;         // the region includes the IQ1_S table
+    IqLayout iq{};         // its layout
     int *err;
     long long wait_cycles = kWaitCycles;   // bound of every mbarrier wait
     uint32_t test_extra_tx = 0;            // test hook only: extra bytes the producer announces
@@ -220,10 +221,10 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
     if (warp == prod && lane == 0) QE_STAMP(7);
     // IQ codebooks: constant data, staged by the non-producer warps before
     // the dependency wait; barrier 2 below publishes them to the consumers
-    if constexpr (JobIq<Job>::v) {
+    if constexpr (JobIq<Job>::v != 0) {
         if (P.iq_off && warp != prod) {
             const int t = warp < prod ? threadIdx.x : threadIdx.x - 32;
-            iq_tabs_fill(smem + P.iq_off, P.iq_1s != 0, t, (n_cons + 1) * 32);
+            iq_tabs_fill(smem + P.iq_off, P.iq, t, (n_cons + 1) * 32);
         }
     }
     griddep_wait();
@@ -373,7 +374,7 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             const uint8_t *rg8 = blk ? st + qe_hi_off(rb) + (reinterpret_cast<uintptr_t>(U.hi) & 15) + C.gid * rb
                                      : st + (C.gid + 8) * pitch + (a_hi & 15);
             tile_sbs_rt<JobIq<Job>::v>(U.type, rg, rg8, te_base + (size_t)s0 * kTabSB, i0, i1, (int)(a_lo & 2) >> 1,
-                                       C, yg, yg8, smem + P.iq_off);
+                                       C, yg, yg8, smem + P.iq_off, &P.iq);
             quad_sum(yg, yg8);
             if (C.tig == 0) {
                 double *rs = red + ((size_t)slot * P.cg + cw) * 16;
@@ -422,7 +423,9 @@ inline void qe_groups(int maxn, int &cg, int &G) {
 // Host: shared-memory layout for a launch. item_bytes_max = the largest
 // item's row bytes (one row); returns 0 if nothing fits.
 inline int qe_layout(QeLayout &P, int G, int cg, uint32_t item_row_bytes_max, int n_tab, int tab_nsb,
-                     int64_t smem_optin, int64_t &smem, uint32_t iq_bytes = 0) {
+                     int64_t smem_optin, int64_t &smem, const IqLayout *iq = nullptr) {
+    const uint32_t iq_bytes = iq ? iq->bytes : 0u;
+    if (iq) P.iq = *iq;
     P.G = G;
     P.cg = cg;
     P.n_tab = n_tab;
@@ -435,7 +438,6 @@ inline int qe_layout(QeLayout &P, int G, int cg, uint32_t item_row_bytes_max, in
         P.tab_off = P.red_off + ((P.stages * cg * 16 * 8 + 127) & ~127u);
         P.stage_off = P.tab_off + (((uint32_t)n_tab * tab_nsb * kTabSB + 127) & ~127u);
         P.iq_off = iq_bytes ? P.stage_off : 0u;
-        P.iq_1s = iq_bytes > kIqBytes ? 1 : 0;
         P.stage_off += (iq_bytes + 127) & ~127u;
         smem = P.stage_off + (int64_t)P.stages * P.slot_bytes;
         if (smem <= smem_optin || P.stages <= 2) break;

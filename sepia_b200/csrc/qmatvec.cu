@@ -170,8 +170,9 @@ struct MvJob {
 
 // The same job for the IQ grid-codebook formats (codebooks staged in shared
 // memory).
+template <int T>
 struct MvIqJob : MvJob {
-    static constexpr bool kIq = true;
+    static constexpr int kIq = T;
 };
 
 template <class Job>
@@ -194,22 +195,30 @@ static int launch_matvec_engine(int t, const void *w, const float *x, float *y, 
     J.rb = rb; J.out_dim = out_dim; J.type = t;
     J.nsb = (int)(in_dim / kQK);
     J.x = x; J.y = y;
-    const uint32_t iqb = iq_format(t) ? (t == T_IQ1_S ? kIqBytes1s : kIqBytes) : 0u;
+    const IqLayout iql = iq_layout(t, t);
+    const uint32_t iqb = iql.bytes;
     J.sbs = qe_sbs(t, J.nsb, qe_row_budget(di.smem_optin, (int64_t)J.nsb * kTabSB + iqb), J.nsplit);
     if (!J.sbs) return fail("matvec_q: no tensor-core split for type %d", t);
     QeLayout P;
     int cg, G;
     qe_groups(J.sbs, cg, G);
     int64_t smem = 0;
-    if (!qe_layout(P, G, cg, (uint32_t)J.sbs * qe_sb_bytes(t), 1, J.nsb, di.smem_optin, smem, iqb))
+    if (!qe_layout(P, G, cg, (uint32_t)J.sbs * qe_sb_bytes(t), 1, J.nsb, di.smem_optin, smem, iqb ? &iql : nullptr))
         return fail("matvec_q: tensor-core tile needs %lld B of shared memory", (long long)smem);
     P.err = di.err;
     P.wait_cycles = wait_cycles;
     P.test_extra_tx = test_extra_tx;
     if (iqb) {
-        MvIqJob JI;
-        static_cast<MvJob &>(JI) = J;
-        return launch_mv_job(JI, P, smem, out_dim, st);
+        auto run = [&](auto JI) {
+            static_cast<MvJob &>(JI) = J;
+            return launch_mv_job(JI, P, smem, out_dim, st);
+        };
+        switch (t) {
+        case T_IQ2_XXS: return run(MvIqJob<T_IQ2_XXS>{});
+        case T_IQ2_XS: return run(MvIqJob<T_IQ2_XS>{});
+        case T_IQ3_XXS: return run(MvIqJob<T_IQ3_XXS>{});
+        default: return run(MvIqJob<T_IQ1_S>{});
+        }
     }
     return launch_mv_job(J, P, smem, out_dim, st);
 }

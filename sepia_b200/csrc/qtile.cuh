@@ -470,62 +470,131 @@ __device__ __forceinline__ void sb_q4k(const uint8_t *bg, const uint8_t *bg8, co
 // Grid-codebook formats (gguf IQ2_XXS, IQ2_XS, IQ3_XXS, IQ1_S). A lane's 8
 // elements of a part (8tig..8tig+7) are exactly one codebook row, so its A
 // registers are that row's bytes, signed (s8 x s8 MMA): a0 / a1 the row's
-// elements 0-3, a2 / a3 elements 4-7. Codebooks and sign masks live in a
-// shared-memory region the engine fills once per CTA (iq_tabs_fill):
-//   [0, 2048)       sign masks of the 7-bit sign fields: uint4 {m_lo, m_hi,
-//                   m_lo & 0x01010101, m_hi & 0x01010101}, m = 0xFF in every
-//                   byte whose element is negated (bit 7 = parity of the
-//                   field, gguf ksigns_iq2xs); (g ^ m) + (m & 1s) = -g per
-//                   negated byte (codebook bytes are 1..62, so no carries)
-//   [2048, 4096)    IQ2_XXS codebook, 256 x 8 bytes
-//   [4096, 8192)    IQ2_XS codebook, 512 x 8 bytes
-//   [8192, 9216)    IQ3_XXS codebook, 256 x 4 bytes
-//   [9216, 41984)   IQ1_S (only when an IQ1_S matrix is in the launch):
-//                   4096 x 8 bytes, entry e = index | (delta sign << 11),
-//                   bytes 8 g + 1 (or 8 g - 1): 8 (g + delta) as an integer
-// The per-part (2s + 1) scales multiply each part's int32 partial (IMAD);
-// IQ2_XS scales its two 16-element groups separately (split B layout, as
-// Q3_K). Value scales: IQ2_XXS / IQ2_XS d (2s+1)/8, IQ3_XXS d (2s+1)/4,
-// IQ1_S d (2s+1)/8 (src/quants.c:179-228; gguf-py IQ2_XXS / IQ1_S).
-constexpr uint32_t kIqSign = 0, kIqG2xxs = 2048, kIqG2xs = 4096, kIqG3xxs = 8192, kIqG1s = 9216;
-constexpr uint32_t kIqBytes = 9216, kIqBytes1s = 9216 + 4096 * 8;
-
+// elements 0-3, a2 / a3 elements 4-7. The per-part (2s + 1) scales multiply
+// each part's int32 partial (IMAD); IQ2_XS scales its two 16-element groups
+// separately (split B layout, as Q3_K). Value scales: IQ2_XXS / IQ2_XS
+// d (2s+1)/8, IQ3_XXS d (2s+1)/4, IQ1_S d (2s+1)/8 (src/quants.c:179-228;
+// gguf-py IQ2_XXS / IQ1_S).
+//
+// Codebook lookups are random per lane, so a plain shared-memory table
+// costs several bank conflicts per load. The engine instead stages
+// lane-private copies (iq_tabs_fill), every entry one 128-byte row:
+//   IQ2_XXS / IQ2_XS: every codebook byte is 8, 25 or 43, so a row is
+//               stored as 8 nibble codes (0, 1, 2) and a 7-bit sign field
+//               (bit 7 = its parity, gguf ksigns_iq2xs) as 8 nibbles with
+//               bit 2 = the element's sign. code | sign is then a byte
+//               permute selector picking from {8, 25, 43} and {-8, -25,
+//               -43}: one OR and two PRMT give the signed row. Codebooks
+//               256 / 512 entries and the sign table 128 entries, each
+//               entry 32 copies of its 4-byte word (lane l reads copy l:
+//               conflict-free).
+//   IQ3_XXS: codebook 256 entries x 32 copies of the 4-byte row; sign masks
+//               128 entries x 16 copies of uint2 {m_lo, m_hi}, m = 0xFF in
+//               each byte whose element is negated; (g ^ m) + (m & 1s) = -g
+//               per negated byte (codebook bytes are 4..62: no carries).
+//               Lane l reads mask copy l % 16 (8-byte loads are served 16
+//               lanes at a time: 16 distinct bank pairs).
+//   IQ1_S: 4096 entries of 8 bytes (one copy), entry e = index | (delta
+//               sign << 11), bytes 8 g + 1 (or 8 g - 1) = 8 (g + delta).
+// Each region is present only when a format of the launch needs it.
+constexpr uint32_t kIqRow = 128;
+struct IqLayout {
+    uint32_t sign, spread, g2xxs, g2xs, g3xxs, g1s;   // byte offsets in the region (~0u: absent)
+    uint32_t bytes;
+};
+constexpr uint32_t kIq2Pos = 0x002B1908u;   // bytes 8, 25, 43
+constexpr uint32_t kIq2Neg = 0x00D5E7F8u;   // bytes -8, -25, -43
 __host__ __device__ constexpr bool iq_format(int t) {
     return t == T_IQ2_XXS || t == T_IQ2_XS || t == T_IQ3_XXS || t == T_IQ1_S;
 }
+// Host: the region for a launch whose matrices have formats a and b.
+inline IqLayout iq_layout(int a, int b) {
+    IqLayout L{~0u, ~0u, ~0u, ~0u, ~0u, ~0u, 0u};
+    auto has = [&](int t) { return a == t || b == t; };
+    auto take = [&](uint32_t &off, uint32_t n) { off = L.bytes; L.bytes += n; };
+    if (has(T_IQ3_XXS)) take(L.sign, 128 * kIqRow);
+    if (has(T_IQ2_XXS) || has(T_IQ2_XS)) take(L.spread, 128 * kIqRow);
+    if (has(T_IQ2_XXS)) take(L.g2xxs, 256 * kIqRow);
+    if (has(T_IQ2_XS)) take(L.g2xs, 512 * kIqRow);
+    if (has(T_IQ3_XXS)) take(L.g3xxs, 256 * kIqRow);
+    if (has(T_IQ1_S)) take(L.g1s, 4096 * 8);
+    return L;
+}
 
-// Fill the region (every thread of the CTA calls it; caller synchronises).
-__device__ inline void iq_tabs_fill(uint8_t *r, bool with_1s, int tid, int nthreads) {
-    for (int s = tid; s < 128; s += nthreads) {
-        const uint32_t b = sepia_ksigns_iq2xs[s];
-        // bit j of b -> bit 7 of byte j (copies of the nibble 7 bits apart
-        // never overlap), then a sign-replicating byte permute (prmt; the
-        // __byte_perm intrinsic ignores the replicate bit)
-        const uint32_t wl = (b & 15u) * 0x10204080u, wh = (b >> 4) * 0x10204080u;
-        const uint32_t ml = (uint32_t)prmt_sel(wl, 0xBA98u), mh = (uint32_t)prmt_sel(wh, 0xBA98u);
-        reinterpret_cast<uint4 *>(r + kIqSign)[s] = make_uint4(ml, mh, ml & 0x01010101u, mh & 0x01010101u);
-    }
-    for (int i = tid; i < 256; i += nthreads) {
-        reinterpret_cast<uint64_t *>(r + kIqG2xxs)[i] = sepia_iq2xxs_grid[i];
-        reinterpret_cast<uint32_t *>(r + kIqG3xxs)[i] = sepia_iq3xxs_grid[i];
-    }
-    for (int i = tid; i < 512; i += nthreads) reinterpret_cast<uint64_t *>(r + kIqG2xs)[i] = sepia_iq2xs_grid[i];
-    if (with_1s) {
+// Sign masks of a 7-bit sign field s (bit 7 = its parity, gguf
+// ksigns_iq2xs): bit j -> byte j = 0xFF (copies of a nibble 7 bits apart
+// never overlap; then a sign-replicating prmt -- the __byte_perm intrinsic
+// ignores the replicate bit).
+__device__ __forceinline__ uint2 iq_sign_masks(uint32_t s) {
+    const uint32_t b = sepia_ksigns_iq2xs[s];
+    return make_uint2((uint32_t)prmt_sel((b & 15u) * 0x10204080u, 0xBA98u),
+                      (uint32_t)prmt_sel((b >> 4) * 0x10204080u, 0xBA98u));
+}
+// bytes (each < 16) of lo, hi -> 8 nibbles
+__device__ __forceinline__ uint32_t iq_nibbles(uint32_t lo, uint32_t hi) {
+    const uint32_t a = (lo | (lo >> 4)) & 0x00FF00FFu, b = (hi | (hi >> 4)) & 0x00FF00FFu;
+    return ((a | (a >> 8)) & 0xFFFFu) | (((b | (b >> 8)) & 0xFFFFu) << 16);
+}
+// IQ2 codebook row (bytes 8, 25, 43) -> nibble codes 0, 1, 2: byte * 3 >> 6
+// (no byte overflows: 43 * 3 < 256)
+__device__ __forceinline__ uint32_t iq2_codes(uint64_t g) {
+    const uint32_t lo = (((uint32_t)g * 3u) >> 6) & 0x03030303u, hi = (((uint32_t)(g >> 32) * 3u) >> 6) & 0x03030303u;
+    return iq_nibbles(lo, hi);
+}
+// sign field s -> nibble j bit 2 = sign of element j
+__device__ __forceinline__ uint32_t iq2_spread(uint32_t s) {
+    const uint32_t b = sepia_ksigns_iq2xs[s];
+    const uint32_t lo = ((b & 15u) * 0x00204081u) & 0x01010101u, hi = ((b >> 4) * 0x00204081u) & 0x01010101u;
+    return iq_nibbles(lo, hi) << 2;
+}
+
+// Fill the region (the calling threads, numbered 0..nthreads-1; the caller
+// synchronises them before any walk reads it). Every replicated entry is
+// one 128-byte row written as 8 16-byte stores.
+__device__ inline void iq_tabs_fill(uint8_t *r, const IqLayout &L, int tid, int nthreads) {
+    auto rows = [&](uint32_t off, int n, auto word4) {
+        if (off == ~0u) return;
+        uint4 *d = reinterpret_cast<uint4 *>(r + off);
+        for (int i = tid; i < n * 8; i += nthreads) d[i] = word4(i >> 3);
+    };
+    rows(L.sign, 128, [](int e) { const uint2 m = iq_sign_masks((uint32_t)e); return make_uint4(m.x, m.y, m.x, m.y); });
+    rows(L.spread, 128, [](int e) { const uint32_t w = iq2_spread((uint32_t)e); return make_uint4(w, w, w, w); });
+    rows(L.g2xxs, 256, [](int e) { const uint32_t w = iq2_codes(sepia_iq2xxs_grid[e]); return make_uint4(w, w, w, w); });
+    rows(L.g2xs, 512, [](int e) { const uint32_t w = iq2_codes(sepia_iq2xs_grid[e]); return make_uint4(w, w, w, w); });
+    rows(L.g3xxs, 256, [](int e) { const uint32_t w = sepia_iq3xxs_grid[e]; return make_uint4(w, w, w, w); });
+    if (L.g1s != ~0u) {
         for (int e = tid; e < 4096; e += nthreads) {
             const uint64_t g = sepia_iq1s_grid[e & 2047];
-            const uint32_t add = (e & 2048) ? 0xFFu : 0x01u;     // -1 or +1 per byte
+            // 8 g + 1 (or 8 g - 1) per byte, g in {-1, 0, 1}
+            const uint32_t add = (e & 2048) ? 0xFFFFFFFFu : 0x01010101u;
+            const uint32_t lo = (uint32_t)g, hi = (uint32_t)(g >> 32);
             uint32_t w[2];
 #pragma unroll
             for (int h = 0; h < 2; h++) {
-                const uint32_t gw = (uint32_t)(g >> (32 * h));
+                const uint32_t gw = h ? hi : lo;
                 uint32_t o = 0;
 #pragma unroll
                 for (int j = 0; j < 4; j++) o |= ((((gw >> (8 * j)) * 8u) + add) & 255u) << (8 * j);
                 w[h] = o;
             }
-            reinterpret_cast<uint2 *>(r + kIqG1s)[e] = make_uint2(w[0], w[1]);
+            reinterpret_cast<uint2 *>(r + L.g1s)[e] = make_uint2(w[0], w[1]);
         }
     }
+}
+
+// A lane's views of the region: entry i of a replicated table is at
+// base + i * kIqRow.
+struct IqLane {
+    const uint8_t *sign, *grid;
+};
+__device__ __forceinline__ IqLane iq_lane(const uint8_t *r, const IqLayout &L, int t, int lane) {
+    IqLane q;
+    q.sign = (t == T_IQ3_XXS) ? r + L.sign + 8 * (lane & 15) : r + L.spread + 4 * lane;
+    q.grid = (t == T_IQ2_XXS) ? r + L.g2xxs + 4 * lane
+           : (t == T_IQ2_XS)  ? r + L.g2xs + 4 * lane
+           : (t == T_IQ3_XXS) ? r + L.g3xxs + 4 * lane
+                              : r + L.g1s;
+    return q;
 }
 
 __device__ __forceinline__ void mma_k32_ss_z(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -542,15 +611,15 @@ __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_
 __device__ __forceinline__ uint32_t ldh(const uint8_t *p) { return *reinterpret_cast<const uint16_t *>(p); }
 
 // codebook row g (8 bytes) with the signs of mask entry m applied
-__device__ __forceinline__ void iq_signed(uint2 g, uint4 m, uint32_t &lo, uint32_t &hi) {
-    lo = (g.x ^ m.x) + m.z;
-    hi = (g.y ^ m.y) + m.w;
+__device__ __forceinline__ void iq_signed(uint2 g, uint2 m, uint32_t &lo, uint32_t &hi) {
+    lo = (g.x ^ m.x) + (m.x & 0x01010101u);
+    hi = (g.y ^ m.y) + (m.y & 0x01010101u);
 }
 
 // Superblock walks: ODD = the superblock starts 2 bytes past a 4-byte
 // boundary (every IQ superblock size is 2 mod 4).
 template <bool ODD>
-__device__ __forceinline__ void sb_iq2xxs(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const uint8_t *iq,
+__device__ __forceinline__ void sb_iq2xxs(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const IqLane &Q,
                                           const LaneCtx &C, double &yg, double &yg8) {
     // part p: 4 codebook indices at 2+8p, then a word of four 7-bit sign
     // fields and the 4-bit scale (bits 28-31)
@@ -560,12 +629,10 @@ __device__ __forceinline__ void sb_iq2xxs(const uint8_t *bg, const uint8_t *bg8,
     for (int p = 0; p < 8; p++) {
         const uint32_t sg = ldw2<!ODD>(bg + 6 + 8 * p), sg8 = ldw2<!ODD>(bg8 + 6 + 8 * p);
         const uint32_t ix = bg[2 + 8 * p + C.tig], ix8 = bg8[2 + 8 * p + C.tig];
-        const uint2 g = lds64(iq + kIqG2xxs + 8 * ix), g8 = lds64(iq + kIqG2xxs + 8 * ix8);
-        const uint4 m = lds128(iq + kIqSign + 16 * ((sg >> sh) & 127u));
-        const uint4 m8 = lds128(iq + kIqSign + 16 * ((sg8 >> sh) & 127u));
-        uint32_t a0, a1, a2, a3;
-        iq_signed(g, m, a0, a2);
-        iq_signed(g8, m8, a1, a3);
+        const uint32_t w = ldw(Q.grid + kIqRow * ix) | ldw(Q.sign + kIqRow * ((sg >> sh) & 127u));
+        const uint32_t w8 = ldw(Q.grid + kIqRow * ix8) | ldw(Q.sign + kIqRow * ((sg8 >> sh) & 127u));
+        const uint32_t a0 = __byte_perm(kIq2Pos, kIq2Neg, w), a2 = __byte_perm(kIq2Pos, kIq2Neg, w >> 16);
+        const uint32_t a1 = __byte_perm(kIq2Pos, kIq2Neg, w8), a3 = __byte_perm(kIq2Pos, kIq2Neg, w8 >> 16);
         const uint2 b = ld_b(te, p, C);
         int cc[4];
         mma_k32_ss_z(cc, a0, a1, a2, a3, b.x, b.y);
@@ -581,7 +648,7 @@ __device__ __forceinline__ void sb_iq2xxs(const uint8_t *bg, const uint8_t *bg8,
 }
 
 template <bool ODD>
-__device__ __forceinline__ void sb_iq2xs(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const uint8_t *iq,
+__device__ __forceinline__ void sb_iq2xs(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const IqLane &Q,
                                          const LaneCtx &C, double &yg, double &yg8) {
     // part p, group l: uint16 at 2+8p+2l = 9-bit codebook index | 7-bit
     // sign field << 9; scale byte 66+p: low nibble elements 0-15, high 16-31
@@ -590,11 +657,10 @@ __device__ __forceinline__ void sb_iq2xs(const uint8_t *bg, const uint8_t *bg8, 
 #pragma unroll
     for (int p = 0; p < 8; p++) {
         const uint32_t q = ldh(bg + 2 + 8 * p + 2 * C.tig), q8 = ldh(bg8 + 2 + 8 * p + 2 * C.tig);
-        const uint2 g = lds64(iq + kIqG2xs + 8 * (q & 511u)), g8 = lds64(iq + kIqG2xs + 8 * (q8 & 511u));
-        const uint4 m = lds128(iq + kIqSign + 16 * (q >> 9)), m8 = lds128(iq + kIqSign + 16 * (q8 >> 9));
-        uint32_t a0, a1, a2, a3;
-        iq_signed(g, m, a0, a2);
-        iq_signed(g8, m8, a1, a3);
+        const uint32_t w = ldw(Q.grid + kIqRow * (q & 511u)) | ldw(Q.sign + kIqRow * (q >> 9));
+        const uint32_t w8 = ldw(Q.grid + kIqRow * (q8 & 511u)) | ldw(Q.sign + kIqRow * (q8 >> 9));
+        const uint32_t a0 = __byte_perm(kIq2Pos, kIq2Neg, w), a2 = __byte_perm(kIq2Pos, kIq2Neg, w >> 16);
+        const uint32_t a1 = __byte_perm(kIq2Pos, kIq2Neg, w8), a3 = __byte_perm(kIq2Pos, kIq2Neg, w8 >> 16);
         const uint2 e = ld_b(te, p, C);
         int cc[4];
         mma_k32_ss_z(cc, a0, a1, a2, a3, e.x & C.msplit, e.y & C.msplit);
@@ -612,7 +678,7 @@ __device__ __forceinline__ void sb_iq2xs(const uint8_t *bg, const uint8_t *bg8, 
 }
 
 template <bool ODD>
-__device__ __forceinline__ void sb_iq3xxs(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const uint8_t *iq,
+__device__ __forceinline__ void sb_iq3xxs(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const IqLane &Q,
                                           const LaneCtx &C, double &yg, double &yg8) {
     // part p: 8 codebook indices at 2+8p (group l: bytes 2l, 2l+1, 4 values
     // each), word at 66+4p = four 7-bit sign fields | scale << 28
@@ -622,11 +688,10 @@ __device__ __forceinline__ void sb_iq3xxs(const uint8_t *bg, const uint8_t *bg8,
     for (int p = 0; p < 8; p++) {
         const uint32_t sw = ldw2<!ODD>(bg + 66 + 4 * p), sw8 = ldw2<!ODD>(bg8 + 66 + 4 * p);
         const uint32_t ii = ldh(bg + 2 + 8 * p + 2 * C.tig), ii8 = ldh(bg8 + 2 + 8 * p + 2 * C.tig);
-        const uint8_t *g3 = iq + kIqG3xxs;
-        const uint2 g = make_uint2(ldw(g3 + 4 * (ii & 255u)), ldw(g3 + 4 * (ii >> 8)));
-        const uint2 g8 = make_uint2(ldw(g3 + 4 * (ii8 & 255u)), ldw(g3 + 4 * (ii8 >> 8)));
-        const uint4 m = lds128(iq + kIqSign + 16 * ((sw >> sh) & 127u));
-        const uint4 m8 = lds128(iq + kIqSign + 16 * ((sw8 >> sh) & 127u));
+        const uint2 g = make_uint2(ldw(Q.grid + kIqRow * (ii & 255u)), ldw(Q.grid + kIqRow * (ii >> 8)));
+        const uint2 g8 = make_uint2(ldw(Q.grid + kIqRow * (ii8 & 255u)), ldw(Q.grid + kIqRow * (ii8 >> 8)));
+        const uint2 m = lds64(Q.sign + kIqRow * ((sw >> sh) & 127u));
+        const uint2 m8 = lds64(Q.sign + kIqRow * ((sw8 >> sh) & 127u));
         uint32_t a0, a1, a2, a3;
         iq_signed(g, m, a0, a2);
         iq_signed(g8, m8, a1, a3);
@@ -644,7 +709,7 @@ __device__ __forceinline__ void sb_iq3xxs(const uint8_t *bg, const uint8_t *bg8,
     yg8 += (double)(cvt16<true>(ldh(bg8)) * u) * limb_pair(acc[2], acc[3], 1.0f);
 }
 
-__device__ __forceinline__ void sb_iq1s(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const uint8_t *iq,
+__device__ __forceinline__ void sb_iq1s(const uint8_t *bg, const uint8_t *bg8, const uint8_t *te, const IqLane &Q,
                                         const LaneCtx &C, double &yg, double &yg8) {
     // part p: 4 low index bytes at 2+4p; uint16 at 34+2p = four 3-bit high
     // index fields | scale << 12 | delta sign << 15
@@ -655,7 +720,7 @@ __device__ __forceinline__ void sb_iq1s(const uint8_t *bg, const uint8_t *bg8, c
         const uint32_t h = ldh(bg + 34 + 2 * p), h8 = ldh(bg8 + 34 + 2 * p);
         const uint32_t e = (uint32_t)bg[2 + 4 * p + C.tig] | (((h >> sh) & 7u) << 8) | ((h >> 4) & 0x800u);
         const uint32_t e8 = (uint32_t)bg8[2 + 4 * p + C.tig] | (((h8 >> sh) & 7u) << 8) | ((h8 >> 4) & 0x800u);
-        const uint2 g = lds64(iq + kIqG1s + 8 * e), g8 = lds64(iq + kIqG1s + 8 * e8);
+        const uint2 g = lds64(Q.grid + 8 * e), g8 = lds64(Q.grid + 8 * e8);
         const uint2 b = ld_b(te, p, C);
         int cc[4];
         mma_k32_ss_z(cc, g.x, g8.x, g.y, g8.y, b.x, b.y);
@@ -680,7 +745,7 @@ __host__ __device__ constexpr bool mma_format(int t) { return t == T_Q2_K || t =
 template <int T>
 __device__ __forceinline__ void tile_sbs(const uint8_t *rg, const uint8_t *rg8, const uint8_t *te0, int i0, int i1,
                                          int flip, const LaneCtx &C, double &yg, double &yg8,
-                                         const uint8_t *iq = nullptr) {
+                                         const IqLane &Q = IqLane{}) {
     constexpr int SB = fmt_block_bytes(T);
     const uint8_t *r = rg + i0 * SB, *r8 = rg8 + i0 * SB, *te = te0 + (size_t)i0 * kTabSB;
     for (int i = i0; i < i1; i++, r += SB, r8 += SB, te += kTabSB) {
@@ -691,30 +756,36 @@ __device__ __forceinline__ void tile_sbs(const uint8_t *rg, const uint8_t *rg8, 
             else sb_q3k<false>(r, r8, te, C, yg, yg8);
         } else if constexpr (T == T_Q4_K) sb_q4k(r, r8, te, C, yg, yg8);
         else if constexpr (T == T_IQ2_XXS) {
-            if (odd) sb_iq2xxs<true>(r, r8, te, iq, C, yg, yg8);
-            else sb_iq2xxs<false>(r, r8, te, iq, C, yg, yg8);
+            if (odd) sb_iq2xxs<true>(r, r8, te, Q, C, yg, yg8);
+            else sb_iq2xxs<false>(r, r8, te, Q, C, yg, yg8);
         } else if constexpr (T == T_IQ2_XS) {
-            if (odd) sb_iq2xs<true>(r, r8, te, iq, C, yg, yg8);
-            else sb_iq2xs<false>(r, r8, te, iq, C, yg, yg8);
+            if (odd) sb_iq2xs<true>(r, r8, te, Q, C, yg, yg8);
+            else sb_iq2xs<false>(r, r8, te, Q, C, yg, yg8);
         } else if constexpr (T == T_IQ3_XXS) {
-            if (odd) sb_iq3xxs<true>(r, r8, te, iq, C, yg, yg8);
-            else sb_iq3xxs<false>(r, r8, te, iq, C, yg, yg8);
-        } else sb_iq1s(r, r8, te, iq, C, yg, yg8);
+            if (odd) sb_iq3xxs<true>(r, r8, te, Q, C, yg, yg8);
+            else sb_iq3xxs<false>(r, r8, te, Q, C, yg, yg8);
+        } else sb_iq1s(r, r8, te, Q, C, yg, yg8);
     }
 }
 
-// IQ = true: the launch may carry IQ formats (their tables at iq).
-template <bool IQ = false>
+// IQ: 0 = K-quant formats only; > 0 = every matrix of the launch has this
+// IQ format; -1 = any format (IQ tables in the region at iq, laid out by L).
+template <int IQ = 0>
 __device__ __forceinline__ void tile_sbs_rt(int t, const uint8_t *rg, const uint8_t *rg8, const uint8_t *te0, int i0,
                                             int i1, int flip, const LaneCtx &C, double &yg, double &yg8,
-                                            const uint8_t *iq = nullptr) {
-    if constexpr (IQ) {
-        switch (t) {
-        case T_IQ2_XXS: tile_sbs<T_IQ2_XXS>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, iq); return;
-        case T_IQ2_XS: tile_sbs<T_IQ2_XS>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, iq); return;
-        case T_IQ3_XXS: tile_sbs<T_IQ3_XXS>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, iq); return;
-        case T_IQ1_S: tile_sbs<T_IQ1_S>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, iq); return;
-        default: break;
+                                            const uint8_t *iq = nullptr, const IqLayout *L = nullptr) {
+    if constexpr (IQ > 0) {
+        tile_sbs<IQ>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, iq_lane(iq, *L, IQ, 4 * C.gid + C.tig));
+        return;
+    } else if constexpr (IQ < 0) {
+        if (iq_format(t)) {
+            const IqLane Q = iq_lane(iq, *L, t, 4 * C.gid + C.tig);
+            switch (t) {
+            case T_IQ2_XXS: tile_sbs<T_IQ2_XXS>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, Q); return;
+            case T_IQ2_XS: tile_sbs<T_IQ2_XS>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, Q); return;
+            case T_IQ3_XXS: tile_sbs<T_IQ3_XXS>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, Q); return;
+            default: tile_sbs<T_IQ1_S>(rg, rg8, te0, i0, i1, flip, C, yg, yg8, Q); return;
+            }
         }
     }
     switch (t) {
