@@ -51,6 +51,7 @@ def parse():
     ap.add_argument("--parity", action="store_true", help="check one step against the CPU oracle")
     ap.add_argument("--only", default="", help="kernels workload: run only the lines whose name contains this")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-5 decode measurement")
+    ap.add_argument("--no-kernels", action="store_true", help="skip the config-1/3/4 kernel lines in the default run")
     ap.add_argument("--decode-layers", type=int, default=0, help="config-5 depth (default 24 at N=1, 66 at N>1)")
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--gen", type=int, default=256)
@@ -330,11 +331,16 @@ def kernel_lines(args):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / n * 1e-3
 
+    recs = []
+
     def emit(name, nbytes, sec, extra):
         gbs = nbytes / sec / 1e9
-        print(json.dumps({"metric": "kernel HBM GB/s", "kernel": name, "value": round(gbs, 1), "unit": "GB/s",
-                          "us": round(sec * 1e6, 2), "bytes": nbytes, "frac_of_measured_peak": round(gbs / peak, 4),
-                          "peak_kind": kind, "data": "synthetic", **extra}), flush=True)
+        rec = {"metric": "kernel HBM GB/s", "kernel": name, "value": round(gbs, 1), "unit": "GB/s",
+               "us": round(sec * 1e6, 2), "bytes": nbytes, "frac_of_measured_peak": round(gbs / peak, 4),
+               "peak_kind": kind, "data": "synthetic", **extra}
+        recs.append(rec)
+        if args.workload == "kernels":
+            print(json.dumps(rec), flush=True)
 
     def mats(t, rows, cols):
         nb = Q.row_bytes(t, cols) * rows
@@ -377,8 +383,10 @@ def kernel_lines(args):
             continue
         H, Hkv, Dh, E = 64, 8, 128, 256
         kvd = Hkv * Dh
-        k = torch.randn(ctx, kvd, device="cuda").half()
-        v = torch.randn(ctx, kvd, device="cuda").half()
+        # K/V sets rotated per call: more than L2 (126 MB) in all
+        nset = max(2, -(-300_000_000 // (ctx * kvd * 2 * 2)))
+        ks = [torch.randn(ctx, kvd, device="cuda").half() for _ in range(nset)]
+        vs = [torch.randn(ctx, kvd, device="cuda").half() for _ in range(nset)]
         q = torch.randn(H * Dh, device="cuda")
         rl = torch.randn(H * E, device="cuda") * 0.02
         hi = torch.tensor([ctx - 1], dtype=torch.int64, device="cuda")
@@ -388,13 +396,33 @@ def kernel_lines(args):
         max_kv = ctx - int(lo.item())
         wsb = L.sepia_cuda_banded_attn_ws_bytes(1, H, Hkv, Dh, max_kv)
         ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda")
-        fn = lambda i: ok(L.sepia_cuda_banded_attn(1, q.data_ptr(), k.data_ptr(), v.data_ptr(), rl.data_ptr(),
+        fn = lambda i: ok(L.sepia_cuda_banded_attn(1, q.data_ptr(), ks[i % nset].data_ptr(), vs[i % nset].data_ptr(),
+                                                   rl.data_ptr(),
                                                    out.data_ptr(), lo.data_ptr(), hi.data_ptr(), tau.data_ptr(), 1, H,
                                                    Hkv, Dh, E, ctx - 1, kvd, 1.0 / Dh, max_kv, ws.data_ptr(), wsb,
                                                    None))
         nbytes = ctx * kvd * 2 * 2 + 4 * (H * Dh * 2 + H * E)
         emit(f"config4_attn_ctx{ctx}_{'global' if not window else 'window'}", nbytes, timeit(fn, 50),
-             {"ctx": ctx, "note": "K/V stay L2-resident between calls at ctx 4096"})
+             {"ctx": ctx, "kv_sets": nset, "l2": "K/V sets rotated per call, more than L2 in all"})
+        del ks, vs, ws
+    if want("moe_layer_real_types"):
+        # the real Inkling expert formats: IQ2_XS gate/up, IQ3_XXS down
+        # (routed), Q4_K shared experts; BASELINE config-2 geometry
+        from sepia_b200.moe import MoeLayerDevice
+        from sepia_b200.synth import MoeShape, hidden_state
+        shape = MoeShape(gate_type=Q.IQ2_XS, up_type=Q.IQ2_XS, down_type=Q.IQ3_XXS)
+        lays = [MoeLayerDevice.random(shape, seed=300 + i) for i in range(4)]
+        X = torch.stack([torch.from_numpy(hidden_state(s, shape.hidden)) for s in range(1, 65)]).cuda()
+        y = torch.empty(shape.hidden, device="cuda")
+        st = torch.cuda.current_stream().cuda_stream
+
+        def layer(i):
+            D = lays[i % len(lays)]
+            ok(L.sepia_cuda_moe_layer(C.byref(D.struct), X[i % 64].data_ptr(), C.byref(D.ws), y.data_ptr(), st))
+        emit("moe_layer_real_types", shape.token_bytes(), timeit(layer, 100),
+             {"types": "IQ2_XS gate/up, IQ3_XXS down, Q4_K shared, f32 router", "layer_instances": len(lays)})
+        del lays
+    return recs
 
 
 def main():
@@ -527,6 +555,14 @@ def main():
         torch.cuda.empty_cache()
         decode = decode_measure(args, world, rank, group)
 
+    # ---- the other BASELINE kernels (configs 1, 3, 4) and the real-format layer ----
+    kernels = None
+    if world == 1 and not args.no_kernels:
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        kernels = {r["kernel"]: {k: r[k] for k in ("value", "us", "frac_of_measured_peak") if k in r}
+                   for r in kernel_lines(args)}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         sec, n, sample, sec1 = cpu_token_seconds(shape)
@@ -548,7 +584,7 @@ def main():
                 "pct_of_8tbs": round(100 * gbs / 8000, 2), "pct_of_measured_peak": round(100 * gbs / peak, 2),
                 "layer_steps_per_s": round(args.steps / (ms / 1e3), 1),
                 "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": launches_per_step * args.steps,
-                "clocks": clocks, "decode": decode}
+                "clocks": clocks, "decode": decode, "kernels": kernels}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
