@@ -11,10 +11,6 @@
 #include "../../include/sepia_gpu.h"
 #include "runtime.h"
 
-namespace sepia {
-size_t moe_fused_sync_bytes(const SepiaMoeLayer *L);   // moe_fused.cu
-}
-
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -592,9 +588,9 @@ extern "C" int sepia_gpu_moe_layer(const SepiaGpuMoeDesc *d, SepiaGpuBuf *x, Sep
     if (!wsmem) return fail("moe_layer: out of scratch memory");
     SepiaMoeWork ws;
     if (!sepia_cuda_moe_work_carve(&L, wsmem, wb, &ws)) return 0;
-    if (!check(cudaMemsetAsync(ws.counter, 0, sizeof(unsigned int), g.stream), "moe_layer: counter reset") ||
-        !check(cudaMemsetAsync(ws.sync, 0, moe_fused_sync_bytes(&L), g.stream), "moe_layer: counter reset"))
-        return 0;
+    // the kernel chain below uses only the router's CTA counter (the fused
+    // kernel's counters are not touched on this path)
+    if (!check(cudaMemsetAsync(ws.counter, 0, sizeof(unsigned int), g.stream), "moe_layer: counter reset")) return 0;
     if (!sepia_cuda_moe_layer(&L, dptr(x), &ws, dptr(out), g.stream)) return 0;
     mark(out);
     if (topk_idx) {
