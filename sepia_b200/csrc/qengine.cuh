@@ -389,10 +389,22 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
 }
 
 // Host: the largest row an item may carry whole, given the activation-table
-// bytes the CTA keeps in shared memory: three stages of 16 rows must fit.
-inline uint32_t qe_row_budget(int64_t smem_optin, int64_t tab_bytes) {
-    const int64_t b = (smem_optin - kQeJobSmem - tab_bytes - 8192) / (3 * 16) - 48;
-    return (uint32_t)std::max<int64_t>(512, std::min<int64_t>(4000, b));
+// bytes the CTA keeps in shared memory: `stages` stages of 16 rows must fit.
+inline uint32_t qe_row_budget(int64_t smem_optin, int64_t tab_bytes, int stages = 3) {
+    const int64_t b = (smem_optin - kQeJobSmem - tab_bytes - 8192) / (stages * 16) - 48;
+    return (uint32_t)std::max<int64_t>(512, std::min<int64_t>(stages >= 3 ? 4000 : 6000, b));
+}
+// Host: the row budget for rows of rb bytes: three stages, or two when that
+// keeps rows of up to 4 KB whole (whole rows move as two bulk copies per
+// item; split rows need one copy per row and slice, and the copy engine's
+// per-request cost then dominates). Measured on Q4_K rows of 7168 columns
+// (4032 B): 2495 -> 3717 GB/s at 65536 rows; rows of 4608 B measured
+// slower with two stages.
+inline uint32_t qe_row_budget_for(int64_t smem_optin, int64_t tab_bytes, int64_t rb) {
+    const uint32_t b3 = qe_row_budget(smem_optin, tab_bytes, 3);
+    if (rb <= (int64_t)b3 || rb > 4096) return b3;
+    const uint32_t b2 = qe_row_budget(smem_optin, tab_bytes, 2);
+    return rb <= (int64_t)b2 ? b2 : b3;
 }
 
 // Host: superblocks per split for a row of `nsb` superblocks of format t so

@@ -175,6 +175,19 @@ struct MvIqJob : MvJob {
     static constexpr int kIq = T;
 };
 
+// Consumer split of an item: whole rows that fit only two stages get one
+// group of up to 16 warps (one item in the consumers, one in flight), each
+// warp taking two superblocks; otherwise qe_groups' choice.
+static void mv_groups(int sbs, int64_t rb, int64_t tab_bytes, int &cg, int &G) {
+    const int64_t optin = dev_info().smem_optin;
+    if (qe_row_budget_for(optin, tab_bytes, rb) > qe_row_budget(optin, tab_bytes, 3)) {
+        cg = std::min(kQeMaxCons, (sbs + 1) / 2);
+        G = 1;
+        return;
+    }
+    qe_groups(sbs, cg, G);
+}
+
 template <class Job>
 static int launch_mv_job(const Job &J, const QeLayout &P, int64_t smem, int64_t out_dim, cudaStream_t st) {
     const DevInfo &di = dev_info();
@@ -197,11 +210,11 @@ static int launch_matvec_engine(int t, const void *w, const float *x, float *y, 
     J.x = x; J.y = y;
     const IqLayout iql = iq_layout(t, t);
     const uint32_t iqb = iql.bytes;
-    J.sbs = qe_sbs(t, J.nsb, qe_row_budget(di.smem_optin, (int64_t)J.nsb * kTabSB + iqb), J.nsplit);
+    J.sbs = qe_sbs(t, J.nsb, qe_row_budget_for(di.smem_optin, (int64_t)J.nsb * kTabSB + iqb, rb), J.nsplit);
     if (!J.sbs) return fail("matvec_q: no tensor-core split for type %d", t);
     QeLayout P;
     int cg, G;
-    qe_groups(J.sbs, cg, G);
+    mv_groups(J.sbs, rb, (int64_t)J.nsb * kTabSB + iqb, cg, G);
     int64_t smem = 0;
     if (!qe_layout(P, G, cg, (uint32_t)J.sbs * qe_sb_bytes(t), 1, J.nsb, di.smem_optin, smem, iqb ? &iql : nullptr))
         return fail("matvec_q: tensor-core tile needs %lld B of shared memory", (long long)smem);
@@ -681,11 +694,11 @@ int launch_matvec_q_multi(int n, int t, const void *const *w, const int64_t *row
         J.rows[i] = i < n ? rows[i] : 0;
         J.u0[i + 1] = J.u0[i] + (i < n ? (rows[i] + 15) / 16 : 0);
     }
-    J.sbs = qe_sbs(t, J.nsb, qe_row_budget(di.smem_optin, (int64_t)J.nsb * kTabSB), J.nsplit);
+    J.sbs = qe_sbs(t, J.nsb, qe_row_budget_for(di.smem_optin, (int64_t)J.nsb * kTabSB, rb), J.nsplit);
     if (!J.sbs) return fail("matvec_q_multi: no tensor-core split for type %d", t);
     QeLayout P;
     int cg, G;
-    qe_groups(J.sbs, cg, G);
+    mv_groups(J.sbs, rb, (int64_t)J.nsb * kTabSB, cg, G);
     int64_t smem = 0;
     if (!qe_layout(P, G, cg, (uint32_t)J.sbs * qe_sb_bytes(t), 1, J.nsb, di.smem_optin, smem))
         return fail("matvec_q_multi: tensor-core tile needs %lld B of shared memory", (long long)smem);
