@@ -860,7 +860,7 @@ static int launch_gateup_engine(const MoeDev &L, const float *x, const SepiaMoeW
     const uint32_t row_max = std::max((uint32_t)J.sbs_r * qe_sb_bytes(L.gate_type),
                                       L.n_shared ? (uint32_t)J.sbs_s * qe_sb_bytes(L.sh_gate_type) : 0u);
     int cg, G;
-    qe_groups(std::max(J.sbs_r, J.sbs_s), cg, G);
+    qe_groups_fmt(std::max(J.sbs_r, J.sbs_s), L.gate_type, L.n_shared ? L.sh_gate_type : L.gate_type, cg, G);
     QeLayout P;
     int64_t smem = 0;
     if (!qe_layout(P, G, cg, row_max, 1, J.nsb_h, di.smem_optin, smem, iqb ? &iql : nullptr))
@@ -902,7 +902,7 @@ static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *ou
     const uint32_t row_max = std::max((uint32_t)J.sbs_r * qe_sb_bytes(L.down_type),
                                       L.n_shared ? (uint32_t)J.sbs_s * qe_sb_bytes(L.sh_down_type) : 0u);
     int cg, G;
-    qe_groups(std::max(J.sbs_r, J.sbs_s), cg, G);
+    qe_groups_fmt(std::max(J.sbs_r, J.sbs_s), L.down_type, L.n_shared ? L.sh_down_type : L.down_type, cg, G);
     QeLayout P;
     int64_t smem = 0;
     if (!qe_layout(P, G, cg, row_max, J.n_slots, J.nsb_f, di.smem_optin, smem, iqb ? &iql : nullptr))

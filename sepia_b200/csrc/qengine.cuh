@@ -432,6 +432,29 @@ inline void qe_groups(int maxn, int &cg, int &G) {
     }
 }
 
+// Host: the same for items whose rows have formats a and b. Long rows
+// (>= 16 superblocks) get a format-tuned share per warp, measured on 65536 x
+// 7168 matrices and the config-2 gate/up: the cheap Q2_K walk does best with
+// 6 superblocks per warp and 3 groups (3430 -> 3721 GB/s; gate/up 28.7 ->
+// 26.9 us), the costly Q3_K and IQ2_XS / IQ3_XXS walks with 2 superblocks
+// per warp in one group of 14 (Q3_K 2586 -> 2807, IQ2_XS 1386 -> 1597
+// GB/s). IQ2_XXS and IQ1_S measured 3-4 % slower that way and keep
+// qe_groups' choice, as do short rows (the 8-superblock down projections).
+inline void qe_groups_fmt(int maxn, int a, int b, int &cg, int &G) {
+    auto heavy = [](int t) { return t == T_Q3_K || t == T_IQ2_XS || t == T_IQ3_XXS; };
+    int per = 0;
+    if (maxn >= 16) {
+        if (heavy(a) || heavy(b)) per = 2;
+        else if (a == T_Q2_K || b == T_Q2_K) per = 6;
+    }
+    if (!per) {
+        qe_groups(maxn, cg, G);
+        return;
+    }
+    cg = std::min(kQeMaxCons, (maxn + per - 1) / per);
+    G = std::max(1, std::min(4, kQeMaxCons / cg));
+}
+
 // Host: shared-memory layout for a launch. item_bytes_max = the largest
 // item's row bytes (one row); returns 0 if nothing fits.
 inline int qe_layout(QeLayout &P, int G, int cg, uint32_t item_row_bytes_max, int n_tab, int tab_nsb,
