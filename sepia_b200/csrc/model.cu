@@ -5,7 +5,8 @@
 //   xn -> q,k,v,r projections (matvec_q, four launches)
 //      -> k_attn_prep: K/V short convolutions with history roll, per-head
 //         RMSNorm of q and k, cache write, q scaled by tau, the kv range
-//      -> rel_project -> split-KV banded attention -> wo projection
+//         and the relative-position band (rel_project)
+//      -> split-KV banded attention -> wo projection
 //      -> k_residual: attention-output short convolution + residual, then
 //         the MLP norm of the new residual stream (one CTA)
 //      -> MoE layer (router, top-k, experts; moe.cu) or dense SwiGLU
@@ -33,8 +34,6 @@ int launch_matvec_q(int t, const void *w, const float *x, float *y, int64_t out_
                     cudaStream_t st);
 int launch_matvec_q_multi(int n, int t, const void *const *w, const int64_t *rows, int64_t in_dim, const float *x,
                           float *const *y, cudaStream_t st);
-int launch_rel_project(const float *r_vec, const float *rel_proj, float *rel_logits, int64_t T, int64_t H,
-                       int64_t d_rel, int64_t E, cudaStream_t st);
 int launch_banded_attn_ex(int kv_f16, const float *q, const void *k, const void *v, const float *rel_logits,
                           float *out, const int64_t *kv_lo_d, const int64_t *kv_hi_d, const float *tau_d,
                           const double *tau64_d, const int32_t *qpos_d, int64_t T, int64_t H, int64_t Hkv,
@@ -197,6 +196,10 @@ struct PrepArgs {
     int is_sliding, window;
     const double *tau_table;    // per position (global layers)
     ModelState *st;
+    // relative-position band: rel_logits[h, r] = sum_d r_vec[h, d] rel_proj[d, r]
+    const float *r_vec, *rel_proj;
+    float *rel_logits;
+    int d_rel, E;
 };
 
 // Depthwise causal convolution of one channel at T = 1 with its history,
@@ -225,6 +228,18 @@ __global__ void __launch_bounds__(128) k_attn_prep(const PrepArgs A) {
     const int d = threadIdx.x;
     griddep_wait();
     griddep_launch();
+    if ((int)blockIdx.x >= A.H + A.Hkv) {
+        // the band projection (rel_project, src/sepia.c:1188-1194; the
+        // same double accumulation as k_rel_project), one entry per thread
+        const int64_t i = (int64_t)(blockIdx.x - A.H - A.Hkv) * blockDim.x + threadIdx.x;
+        if (i >= (int64_t)A.H * A.E) return;
+        const int64_t h = i / A.E, r = i - h * A.E;
+        const float *rv = A.r_vec + h * A.d_rel;
+        double acc = 0.0;
+        for (int d = 0; d < A.d_rel; d++) acc = fma((double)rv[d], (double)A.rel_proj[(int64_t)d * A.E + r], acc);
+        A.rel_logits[i] = (float)acc;
+        return;
+    }
     const int64_t pos = A.st->pos;
     const double tau = (A.is_sliding || !A.tau_table) ? 1.0 : A.tau_table[pos];
     if ((int)blockIdx.x < A.H) {
@@ -461,9 +476,12 @@ int run_layers(SepiaModel *m, bool want_logits, cudaStream_t st) {
         P.H = H; P.Hkv = Hkv; P.Dh = Dh; P.K = K; P.kv_dim = kv_dim; P.eps = d.eps;
         P.is_sliding = L.is_sliding; P.window = d.window; P.tau_table = d.has_log_scaling ? m->tau : nullptr;
         P.st = m->st;
-        launch_pdl(k_attn_prep, (unsigned)(H + Hkv), 128, 0, st, P);
+        P.r_vec = m->r; P.rel_proj = L.rel_proj; P.rel_logits = m->rl; P.d_rel = (int)d.d_rel;
+        P.E = L.rel_extent;
+        if (L.rel_extent <= 0 || d.d_rel <= 0 || !L.rel_proj) return fail("model: layer %d has no relative band", l);
+        const unsigned rel_blocks = (unsigned)(((int64_t)H * L.rel_extent + 127) / 128);
+        launch_pdl(k_attn_prep, (unsigned)(H + Hkv) + rel_blocks, 128, 0, st, P);
         if (!check(cudaGetLastError(), "model: attn_prep launch")) return 0;
-        if (!launch_rel_project(m->r, L.rel_proj, m->rl, 1, H, d.d_rel, L.rel_extent, st)) return 0;
         if (!launch_banded_attn_ex(0, m->qs, m->kc[l], m->vc[l], m->rl, m->att, &m->st->kv_lo, &m->st->kv_hi,
                                    nullptr, &m->st->tau, &m->st->pos, 1, H, Hkv, Dh, L.rel_extent, 0, kv_dim,
                                    (float)(1.0 / Dh), m->splits[l], m->part, st))

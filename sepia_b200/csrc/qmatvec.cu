@@ -177,15 +177,19 @@ struct MvIqJob : MvJob {
 
 // Consumer split of an item: whole rows that fit only two stages get one
 // group of up to 16 warps (one item in the consumers, one in flight), each
-// warp taking two superblocks; otherwise qe_groups' choice.
-static void mv_groups(int t, int sbs, int64_t rb, int64_t tab_bytes, int &cg, int &G) {
+// warp taking two superblocks; otherwise the format-tuned choice when every
+// CTA gets several units, qe_groups' (more warps per item) when it gets
+// about one (the config-1 2048-row matrices measured slower with 6
+// superblocks per warp).
+static void mv_groups(int t, int sbs, int64_t rb, int64_t tab_bytes, int64_t units, int &cg, int &G) {
     const int64_t optin = dev_info().smem_optin;
     if (qe_row_budget_for(optin, tab_bytes, rb) > qe_row_budget(optin, tab_bytes, 3)) {
         cg = std::min(kQeMaxCons, (sbs + 1) / 2);
         G = 1;
         return;
     }
-    qe_groups_fmt(sbs, t, t, cg, G);
+    if (units >= 4 * (int64_t)dev_info().sm_count) qe_groups_fmt(sbs, t, t, cg, G);
+    else qe_groups(sbs, cg, G);
 }
 
 template <class Job>
@@ -214,7 +218,7 @@ static int launch_matvec_engine(int t, const void *w, const float *x, float *y, 
     if (!J.sbs) return fail("matvec_q: no tensor-core split for type %d", t);
     QeLayout P;
     int cg, G;
-    mv_groups(t, J.sbs, rb, (int64_t)J.nsb * kTabSB + iqb, cg, G);
+    mv_groups(t, J.sbs, rb, (int64_t)J.nsb * kTabSB + iqb, (out_dim + 15) / 16, cg, G);
     int64_t smem = 0;
     if (!qe_layout(P, G, cg, (uint32_t)J.sbs * qe_sb_bytes(t), 1, J.nsb, di.smem_optin, smem, iqb ? &iql : nullptr))
         return fail("matvec_q: tensor-core tile needs %lld B of shared memory", (long long)smem);
@@ -698,7 +702,7 @@ int launch_matvec_q_multi(int n, int t, const void *const *w, const int64_t *row
     if (!J.sbs) return fail("matvec_q_multi: no tensor-core split for type %d", t);
     QeLayout P;
     int cg, G;
-    mv_groups(t, J.sbs, rb, (int64_t)J.nsb * kTabSB, cg, G);
+    mv_groups(t, J.sbs, rb, (int64_t)J.nsb * kTabSB, J.u0[n], cg, G);
     int64_t smem = 0;
     if (!qe_layout(P, G, cg, (uint32_t)J.sbs * qe_sb_bytes(t), 1, J.nsb, di.smem_optin, smem))
         return fail("matvec_q_multi: tensor-core tile needs %lld B of shared memory", (long long)smem);
