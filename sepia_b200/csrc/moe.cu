@@ -42,7 +42,6 @@ __global__ void __launch_bounds__(kRouterMaxChunks * 32) k_router(const MoeDev L
     const int cpr = router_chunks(L.hidden);
     const int row = blockIdx.x;
     __shared__ double s_part[kRouterMaxChunks];
-    griddep_launch();
     if (warp < cpr) {
         const int64_t c0 = (int64_t)warp * kRouterChunk;
         const int64_t n = imin64(kRouterChunk, L.hidden - c0);
@@ -79,6 +78,9 @@ __global__ void __launch_bounds__(kRouterMaxChunks * 32) k_router(const MoeDev L
     // serial tail below only selects and normalises
     const float bias = (row < L.n_routed && threadIdx.x == 0) ? L.router_bias[row] : 0.0f;
     __syncthreads();
+    // every warp is past its dependency wait: the successor may launch (it
+    // reads x, final since this kernel's predecessor completed)
+    griddep_launch();
     if (warp != 0) return;
     unsigned int last = 0;
     if (lane == 0) {
@@ -110,16 +112,33 @@ __global__ void __launch_bounds__(kRouterMaxChunks * 32) k_router(const MoeDev L
 // dependency wait -- the weights do not depend on the previous kernel. A
 // single request per CTA keeps the whole matrix in flight without the
 // per-load queueing of thousands of 16-byte loads. Thread t then dots
-// elements t, t + T, ... of each row with x (held in registers) in fp64,
-// the warps' partials are summed in warp order, and the last CTA selects.
+// float4 t, t + T, ... of each row with x (held in registers) in four fp64
+// chains, the warps' partials are summed in warp order, and the last CTA
+// selects.
 constexpr int kRouter2Threads = 256;
 constexpr int kRouter2MaxPerThread = 64;       // hidden <= 64 * 256
+// Optional phase timestamps for profiling builds (-DSEPIA_ROUTER_STAMPS):
+// [CTA][phase] of the last router2 launch, in globaltimer nanoseconds.
+#ifdef SEPIA_ROUTER_STAMPS
+__device__ unsigned long long g_rstamps[256][8];
+#define RS(i)                                                                        \
+    do {                                                                             \
+        if (threadIdx.x == 0 && blockIdx.x < 256) {                                  \
+            unsigned long long t_;                                                   \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                   \
+            g_rstamps[blockIdx.x][i] = t_;                                           \
+        }                                                                            \
+    } while (0)
+#else
+#define RS(i) do { } while (0)
+#endif
 __global__ void __launch_bounds__(kRouter2Threads) k_router2(const MoeDev L, const float *x, float *logits,
                                                               int32_t *topk_idx, float *weights,
                                                               unsigned int *counter, float2 *row_out, int rpc) {
     extern __shared__ __align__(128) float w_sm[];
+    RS(0);
     __shared__ __align__(8) uint64_t bar;
-    __shared__ double s_w[kRouter2Threads / 32];
+    __shared__ double s_w[kRouter2Threads / 32], s_w2[kRouter2Threads / 32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_total = L.n_routed + L.n_shared;
     const int r0 = blockIdx.x * rpc;
@@ -132,36 +151,64 @@ __global__ void __launch_bounds__(kRouter2Threads) k_router2(const MoeDev L, con
         mbar_arrive_expect_tx(&bar, bytes);
         bulk_g2s(w_sm, L.router_w + (int64_t)r0 * H, bytes, &bar);
     }
-    griddep_launch();
+    // the successor (gate/up) may launch once this kernel's own predecessor,
+    // which wrote x, has completed: it reads x before its dependency wait
     griddep_wait();
-    float xv[kRouter2MaxPerThread];
-    const int per = (int)((H + kRouter2Threads - 1) / kRouter2Threads);
+    griddep_launch();
+    RS(1);
+    // x as float4 (H % 4 == 0): thread t holds float4 t, t + T, ...
+    constexpr int kV = kRouter2MaxPerThread / 4;
+    const int64_t H4 = H / 4;
+    float4 xv[kV];
 #pragma unroll
-    for (int j = 0; j < kRouter2MaxPerThread; j++) {
-        const int64_t i = threadIdx.x + (int64_t)j * kRouter2Threads;
-        xv[j] = (j < per && i < H) ? __ldg(x + i) : 0.0f;
+    for (int j = 0; j < kV; j++) {
+        const int64_t f = threadIdx.x + (int64_t)j * kRouter2Threads;
+        xv[j] = f < H4 ? __ldg(reinterpret_cast<const float4 *>(x) + f) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    const int rl = lane;     // warp 0, lane q finalises row q of each pair
     __syncthreads();                       // the barrier's init is visible
+    RS(2);
     const bool ok = mbar_wait(&bar, 0, L.err);
-    const float bias0 = 0.0f;
-    (void)bias0;
-    for (int r = 0; r < nr; r++) {
-        double acc = 0.0;
+    RS(3);
+    // rows two at a time: four fp64 chains per row and thread, one block
+    // reduction per pair, the pair's rows finalised by two lanes at once
+    for (int r = 0; r < nr; r += 2) {
+        const int nrr = min(2, nr - r);
+        double acc[2] = {0.0, 0.0};
         if (ok) {
-            const float *wr = w_sm + (int64_t)r * H;
 #pragma unroll
-            for (int j = 0; j < kRouter2MaxPerThread; j++) {
-                const int64_t i = threadIdx.x + (int64_t)j * kRouter2Threads;
-                if (j < per && i < H) acc = fma((double)wr[i], (double)xv[j], acc);
+            for (int q = 0; q < 2; q++) {
+                if (q < nrr) {
+                    const float4 *wr = reinterpret_cast<const float4 *>(w_sm + (int64_t)(r + q) * H);
+                    double c[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+                    for (int j = 0; j < kV; j++) {
+                        const int64_t f = threadIdx.x + (int64_t)j * kRouter2Threads;
+                        if (f < H4) {
+                            const float4 w4 = wr[f];
+                            c[0] = fma((double)w4.x, (double)xv[j].x, c[0]);
+                            c[1] = fma((double)w4.y, (double)xv[j].y, c[1]);
+                            c[2] = fma((double)w4.z, (double)xv[j].z, c[2]);
+                            c[3] = fma((double)w4.w, (double)xv[j].w, c[3]);
+                        }
+                    }
+                    acc[q] = (c[0] + c[1]) + (c[2] + c[3]);
+                }
             }
         }
-        acc = warp_sum_d(acc);
-        if (lane == 0) s_w[warp] = acc;
+        acc[0] = warp_sum_d(acc[0]);
+        acc[1] = warp_sum_d(acc[1]);
+        if (lane == 0) {
+            s_w[warp] = acc[0];
+            s_w2[warp] = acc[1];
+        }
         __syncthreads();
-        if (threadIdx.x == 0) {
+        RS(7);
+        if (warp == 0 && rl < nrr) {
+            const double *sw = rl == 0 ? s_w : s_w2;
             double t = 0.0;
-            for (int w = 0; w < kRouter2Threads / 32; w++) t += s_w[w];       // warp order
-            const int row = r0 + r;
+            for (int w = 0; w < kRouter2Threads / 32; w++) t += sw[w];       // warp order
+            const int row = r0 + r + rl;
             const float l = (float)t;
             logits[row] = l;
             const float score = row < L.n_routed ? __fadd_rn(sigmoid_ref(l), L.router_bias[row]) : 0.0f;
@@ -169,20 +216,21 @@ __global__ void __launch_bounds__(kRouter2Threads) k_router2(const MoeDev L, con
         }
         __syncthreads();
     }
+    RS(4);
     if (warp != 0) return;
     unsigned int last = 0;
     if (lane == 0) {
         __threadfence();     // release this CTA's writes before counting it
         last = (atomicAdd(counter, 1u) == gridDim.x - 1) ? 1u : 0u;
     }
+    RS(5);
     if (!__shfl_sync(0xffffffffu, last, 0)) return;
     __threadfence();
     if (L.n_routed <= 8 * 32) router_select<8>(L, row_out, topk_idx, weights, lane);
     else router_select<kRouterMaxExperts / 32>(L, row_out, topk_idx, weights, lane);
-    if (lane == 0) {
-        *counter = 0u;   // ready for the next launch
-        __threadfence();
-    }
+    // ready for the next launch (kernel completion publishes it)
+    if (lane == 0) *counter = 0u;
+    RS(6);
 }
 
 // Selection only (bit-exact part of the router): top-k of given scores.
@@ -568,7 +616,11 @@ __global__ void k_combine(const float *slots, int n_slots, int64_t hidden, float
 
 // Units: (slot, 8-row block of ff): MMA rows 0-7 are the gate rows, 8-15 the
 // matching up rows. Shared slots come first: they do not depend on the router.
+// The x tables are built before the dependency wait: x was written before
+// the router's predecessor completed, and the routers let this kernel launch
+// only after their own dependency wait.
 struct GuJob {
+    static constexpr bool kTabsEarly = true;
     MoeDev L;
     const int32_t *idx;
     const float *weights;
@@ -943,7 +995,7 @@ int launch_router(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaS
     const int sms = di.sm_count > 0 ? di.sm_count : 148;
     const int rpc = (n_total + sms - 1) / sms;
     const int64_t smem = (int64_t)rpc * L.hidden * 4;
-    if ((L.hidden * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(L.router_w) & 15) == 0 &&
+    if ((L.hidden * 4) % 16 == 0 && ((reinterpret_cast<uintptr_t>(L.router_w) | reinterpret_cast<uintptr_t>(x)) & 15) == 0 &&
         L.hidden <= (int64_t)kRouter2MaxPerThread * kRouter2Threads && smem <= di.smem_optin - 2048 &&
         smem < (1 << 20)) {
         if (!ensure_smem((const void *)k_router2, (int)smem)) return 0;
@@ -1136,6 +1188,11 @@ extern "C" int sepia_cuda_topk_select(const float *scores, int32_t n, int32_t to
     return check(cudaGetLastError(), "topk launch");
 }
 
+#ifdef SEPIA_ROUTER_STAMPS
+extern "C" __attribute__((visibility("default"))) int sepia_router_stamps(void *dst) {
+    return cudaMemcpyFromSymbol(dst, sepia::g_rstamps, sizeof(sepia::g_rstamps)) == cudaSuccess;
+}
+#endif
 #ifdef SEPIA_QE_STAMPS
 extern "C" __attribute__((visibility("default"))) int sepia_qe_stamps(void *dst) {
     return cudaMemcpyFromSymbol(dst, sepia::g_qe_stamps, sizeof(sepia::g_qe_stamps)) == cudaSuccess;

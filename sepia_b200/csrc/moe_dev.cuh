@@ -83,13 +83,20 @@ __device__ __forceinline__ uint32_t score_key(float f) {
 template <int KPL>
 __device__ __forceinline__ void router_select(const MoeDev &L, const float2 *row_out, int32_t *topk_idx,
                                               float *weights, int lane) {
+    // one round of loads: every entry's (score, log-sigmoid), plus the
+    // shared-sink log-sigmoids (lanes 0 .. n_shared-1)
     uint32_t key[KPL];
+    float lpv[KPL];
 #pragma unroll
     for (int j = 0; j < KPL; j++) {
         const int e = lane + 32 * j;
-        key[j] = e < L.n_routed ? score_key(__ldcg(&row_out[e].x)) : 0u;
+        const float2 ro = e < L.n_routed ? __ldcg(&row_out[e]) : make_float2(0.0f, 0.0f);
+        key[j] = e < L.n_routed ? score_key(ro.x) : 0u;
+        lpv[j] = ro.y;
     }
+    const float lp_sh = lane < L.n_shared ? __ldcg(&row_out[L.n_routed + lane].y) : 0.0f;
     int my_sel = -1;        // lane j < topk: the j-th pick
+    float my_lp = -INFINITY;
     for (int k = 0; k < L.topk; k++) {
         uint32_t m = 0;
 #pragma unroll
@@ -100,14 +107,25 @@ __device__ __forceinline__ void router_select(const MoeDev &L, const float2 *row
         for (int j = KPL - 1; j >= 0; j--)
             if (key[j] == m) cand = (uint32_t)(lane + 32 * j);
         const int e = (int)__reduce_min_sync(0xffffffffu, cand);
+        float lpe = 0.0f;
 #pragma unroll
-        for (int j = 0; j < KPL; j++)
+        for (int j = 0; j < KPL; j++) {
             if (lane + 32 * j == e) key[j] = 0u;
-        if (lane == k) my_sel = e;
+            if (j == (e >> 5)) lpe = lpv[j];
+        }
+        lpe = __shfl_sync(0xffffffffu, lpe, e & 31);
+        if (lane == k) {
+            my_sel = e;
+            my_lp = lpe;
+        }
     }
     const int n_sel = L.topk + L.n_shared;
     float lp = -INFINITY;
-    if (lane < n_sel) lp = __ldcg(&row_out[lane < L.topk ? my_sel : L.n_routed + (lane - L.topk)].y);
+    {
+        const float shv = __shfl_sync(0xffffffffu, lp_sh, (lane - L.topk) & 31);
+        if (lane < L.topk) lp = my_lp;
+        else if (lane < n_sel) lp = shv;
+    }
     float lmax = lp;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));

@@ -56,6 +56,11 @@ __host__ __device__ inline int qe_sb_bytes(int t) { return fmt_block_bytes(t); }
 // shared memory and compile the IQ tile walks.
 template <class J, class = void> struct JobIq { static constexpr int v = 0; };
 template <class J> struct JobIq<J, std::void_t<decltype(J::kIq)>> { static constexpr int v = J::kIq; };
+// Whether a job's activation tables may be built before its dependency wait
+// (Job::kTabsEarly): their sources were complete before the predecessor
+// kernel let this one launch.
+template <class J, class = void> struct JobTabsEarly { static constexpr bool v = false; };
+template <class J> struct JobTabsEarly<J, std::void_t<decltype(J::kTabsEarly)>> { static constexpr bool v = J::kTabsEarly; };
 // Row pitch in a stage for `bytes` bytes per row: 16-byte multiple with an
 // odd number of 16-byte granules (8 consecutive rows -> 8 distinct banks).
 __host__ __device__ inline uint32_t qe_pitch(uint32_t bytes) {
@@ -227,21 +232,8 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             iq_tabs_fill(smem + P.iq_off, P.iq, t, (n_cons + 1) * 32);
         }
     }
-    griddep_wait();
-    if (threadIdx.x == 0) {
-        QE_STAMP(1);
-        griddep_launch();
-    }
-    J.setup(jsm, threadIdx.x, true);
-    // The producer needs only warp 0's post-dependency job scratch (named
-    // barrier 1: warp 0 arrives, the producer waits); the other warps build
-    // the activation tables their units read and meet on barrier 2. The
-    // producer, possibly still blocked issuing its first copies, holds
-    // nobody up.
-    if (warp == prod) {
-        named_bar_sync(1, 64);
-    } else {
-        if (warp == 0) named_bar_arrive(1, 64);
+    // Build the activation tables this CTA's units read (non-producer warps).
+    auto build_tabs = [&]() {
         // superblock q of the needed tables (in table order) goes to warp
         // q % nbw; a warp loads up to kQeBuildBatch of them before it
         // computes any, so their L2 latencies overlap
@@ -268,6 +260,29 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             for (int i = 0; i < kQeBuildBatch; i++)
                 if (te[i]) xtab_emit(te[i], v[i], lane);
         }
+    };
+    // Jobs whose tables read only data that was final before their
+    // predecessor started (kTabsEarly) build them before the dependency
+    // wait, while the predecessor finishes.
+    if constexpr (JobTabsEarly<Job>::v) {
+        if (warp != prod) build_tabs();
+    }
+    griddep_wait();
+    if (threadIdx.x == 0) {
+        QE_STAMP(1);
+        griddep_launch();
+    }
+    J.setup(jsm, threadIdx.x, true);
+    // The producer needs only warp 0's post-dependency job scratch (named
+    // barrier 1: warp 0 arrives, the producer waits); the other warps build
+    // the activation tables their units read and meet on barrier 2. The
+    // producer, possibly still blocked issuing its first copies, holds
+    // nobody up.
+    if (warp == prod) {
+        named_bar_sync(1, 64);
+    } else {
+        if (warp == 0) named_bar_arrive(1, 64);
+        if constexpr (!JobTabsEarly<Job>::v) build_tabs();
         named_bar_sync(2, (n_cons + 1) * 32);
     }
 
