@@ -697,7 +697,7 @@ def abi_e2e(layers, args, shape):
     for b in bufs + [bx, bo]:
         G.sepia_gpu_free(b)
     return {"value": round(args.steps * s.token_bytes() / dt / 1e9, 1), "unit": "GB/s",
-            "h2d_bytes_per_step": 2 * s.hidden * 4, "d2h_bytes_per_step": s.hidden * 4,
+            "h2d_bytes_per_step": s.hidden * 4, "d2h_bytes_per_step": s.hidden * 4,
             "ms_per_step": round(1e3 * dt / args.steps, 4), "tok_s": round(args.steps / dt, 1),
             "path": "sepia_gpu_begin + sepia_gpu_moe_layer + sepia_gpu_end (host-buffer ABI)"}
 

@@ -117,6 +117,7 @@ struct Backend {
     bool batch_open = false;
     cudaStream_t stream = nullptr;
     cudaEvent_t done = nullptr;
+    unsigned *moe_counter = nullptr;   // the router's CTA counter (zeroed once; the router resets it)
     std::set<SepiaGpuBuf *> bufs;
     Arena arena;
     HostArena harena;
@@ -151,6 +152,16 @@ bool fits(SepiaGpuBuf *b, size_t off, size_t bytes, const char *op, const char *
         b->synced = true;
     }
     return true;
+}
+
+// An op's output that overwrites the whole of a Shared buffer: its mirror
+// need not be uploaded first.
+bool fits_out(SepiaGpuBuf *b, size_t bytes, const char *op, const char *what) {
+    if (b && b->dev && b->kind == kShared && g.batch_open && !b->synced && bytes == b->len) {
+        b->synced = true;
+        return true;
+    }
+    return fits(b, 0, bytes, op, what);
 }
 
 void mark(SepiaGpuBuf *b) {
@@ -214,6 +225,9 @@ extern "C" int sepia_gpu_init(const char *metal_dir) {
     snprintf(g.name, sizeof g.name, "%s", prop.name);
     g.stream = lib_stream();
     if (!check(cudaEventCreateWithFlags(&g.done, cudaEventDisableTiming), "cudaEventCreate")) return 0;
+    if (!check(cudaMalloc((void **)&g.moe_counter, 256), "init: cudaMalloc") ||
+        !check(cudaMemset(g.moe_counter, 0, 256), "init: cudaMemset"))
+        return 0;
     dev_info();
     g.ready = true;
     return 1;
@@ -228,6 +242,8 @@ extern "C" void sepia_gpu_shutdown(void) {
     g.harena.release();
     if (g.done) cudaEventDestroy(g.done);
     g.done = nullptr;
+    if (g.moe_counter) cudaFree(g.moe_counter);
+    g.moe_counter = nullptr;
     g.ready = false;
     g.name[0] = 0;
 }
@@ -544,7 +560,7 @@ extern "C" int sepia_gpu_moe_layer(const SepiaGpuMoeDesc *d, SepiaGpuBuf *x, Sep
     if (!need_batch("moe_layer")) return 0;
     if (!d || !d->router_w || !d->router_bias || !d->experts || (d->n_shared > 0 && !d->shared))
         return fail("moe_layer: incomplete descriptor");
-    if (!fits(x, 0, (size_t)d->hidden * 4, "moe_layer", "x") || !fits(out, 0, (size_t)d->hidden * 4, "moe_layer", "out"))
+    if (!fits(x, 0, (size_t)d->hidden * 4, "moe_layer", "x") || !fits_out(out, (size_t)d->hidden * 4, "moe_layer", "out"))
         return 0;
     SepiaMoeLayer L;
     memset(&L, 0, sizeof L);
@@ -588,9 +604,11 @@ extern "C" int sepia_gpu_moe_layer(const SepiaGpuMoeDesc *d, SepiaGpuBuf *x, Sep
     if (!wsmem) return fail("moe_layer: out of scratch memory");
     SepiaMoeWork ws;
     if (!sepia_cuda_moe_work_carve(&L, wsmem, wb, &ws)) return 0;
-    // the kernel chain below uses only the router's CTA counter (the fused
-    // kernel's counters are not touched on this path)
-    if (!check(cudaMemsetAsync(ws.counter, 0, sizeof(unsigned int), g.stream), "moe_layer: counter reset")) return 0;
+    // the kernel chain below uses only the router's CTA counter: a
+    // persistent one, zero between calls (the router's last CTA resets it),
+    // so no clearing op precedes the router (calls are serialised on the
+    // backend's one stream)
+    ws.counter = g.moe_counter;
     if (!sepia_cuda_moe_layer(&L, dptr(x), &ws, dptr(out), g.stream)) return 0;
     mark(out);
     if (topk_idx) {
