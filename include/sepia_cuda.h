@@ -114,7 +114,10 @@ int sepia_cuda_moe_router(const SepiaMoeLayer *L, const float *x, const SepiaMoe
 int sepia_cuda_moe_experts(const SepiaMoeLayer *L, const float *x, const SepiaMoeWork *ws, float *out,
                            int write_slots, void *stream);
 /* The two halves of sepia_cuda_moe_experts, separately launchable (used to
- * time each kernel): gate/up+SwiGLU into ws->h, then down + combine. */
+ * time each kernel): gate/up+SwiGLU into ws->h, then down + combine.
+ * Ordering: the expert kernels run after sepia_cuda_moe_router on the same
+ * stream, and x must not be rewritten between the router and them (the
+ * gate/up kernel reads x while the router is still finishing). */
 int sepia_cuda_moe_gateup(const SepiaMoeLayer *L, const float *x, const SepiaMoeWork *ws, void *stream);
 int sepia_cuda_moe_down(const SepiaMoeLayer *L, const SepiaMoeWork *ws, float *out, int write_slots, void *stream);
 int sepia_cuda_moe_combine(const SepiaMoeLayer *L, const SepiaMoeWork *ws, float *out, void *stream);
