@@ -61,6 +61,17 @@ template <class J> struct JobIq<J, std::void_t<decltype(J::kIq)>> { static const
 // kernel let this one launch.
 template <class J, class = void> struct JobTabsEarly { static constexpr bool v = false; };
 template <class J> struct JobTabsEarly<J, std::void_t<decltype(J::kTabsEarly)>> { static constexpr bool v = J::kTabsEarly; };
+// Whether a job's units carry two activation vectors (Job::kDual): tables
+// U.tab and U.tab + 1 feed MMA columns 0-3 and 4-7, so one pass over the
+// weights yields both vectors' rows (formats whose walks use only the
+// natural B layout and no group-sum MMA, which needs all 8 columns:
+// IQ2_XXS, IQ3_XXS, IQ1_S). finish() then sees 32 lanes: row lane % 16 of
+// vector lane / 16.
+template <class J, class = void> struct JobDual { static constexpr bool v = false; };
+template <class J> struct JobDual<J, std::void_t<decltype(J::kDual)>> { static constexpr bool v = J::kDual; };
+__host__ __device__ constexpr bool dual_format(int t) {
+    return t == T_IQ2_XXS || t == T_IQ3_XXS || t == T_IQ1_S;
+}
 // Row pitch in a stage for `bytes` bytes per row: 16-byte multiple with an
 // odd number of 16-byte granules (8 consecutive rows -> 8 distinct banks).
 __host__ __device__ inline uint32_t qe_pitch(uint32_t bytes) {
@@ -146,6 +157,8 @@ template <class Job>
 __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, const QeLayout P) {
     Job J = Jp;
     J.init();
+    constexpr bool DUAL = JobDual<Job>::v;
+    constexpr int RW = DUAL ? 32 : 16;          // reduction rows per consumer partial
     if (threadIdx.x == 0) QE_STAMP(0);
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -153,7 +166,7 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *ready = full + kQeMaxStages;
     uint64_t *empty = ready + kQeMaxStages;
-    double *red = reinterpret_cast<double *>(smem + P.red_off);      // [stages][cg][16]
+    double *red = reinterpret_cast<double *>(smem + P.red_off);      // [stages][cg][RW]
     uint8_t *tab = smem + P.tab_off;
     uint8_t *stage0 = smem + P.stage_off;
     const int64_t n_units = J.n_units();
@@ -324,9 +337,9 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
             bool ok = true;
             for (int sp = 0; sp < U.nsplit; sp++) {
                 if (!mbar_wait(&ready[ring.slot], ring.phase, P.err, P.wait_cycles)) { ok = false; break; }
-                if (lane < 16) {
-                    const double *rs = red + (size_t)ring.slot * P.cg * 16 + lane;
-                    for (int c = 0; c < P.cg; c++) acc += rs[c * 16];
+                if (lane < RW) {
+                    const double *rs = red + (size_t)ring.slot * P.cg * RW + lane;
+                    for (int c = 0; c < P.cg; c++) acc += rs[c * RW];
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[ring.slot]);
@@ -343,7 +356,15 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
     if (warp == 0 && lane == 0) QE_STAMP(2);
     bool first = true;
     const int grp = warp / P.cg, cw = warp % P.cg;
-    const LaneCtx C = lane_ctx(lane);
+    LaneCtx C = lane_ctx(lane);
+    if constexpr (DUAL) {
+        // columns 4-7 carry the second vector's limbs, not duplicates; a
+        // lane's B operand comes from the table of its column gid, its C
+        // columns (2tig, 2tig+1) belong to vector tig / 2, whose x unit
+        // scales them
+        C.lwn = C.lws;
+        C.unit_off = ((C.tig >= 2 ? 1 : 0) - (C.gid >= 4 ? 1 : 0)) * P.tab_nsb * kTabSB;
+    }
     QeRing ring;
     int g = 0;                        // group of the current item (item index % G)
     const float inv_cg = 1.0f / (float)P.cg;
@@ -357,7 +378,9 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
         }
         QUnit U;
         J.unit(jsm, u, U);
-        const uint8_t *te_base = tab + (size_t)U.tab * P.tab_nsb * kTabSB;
+        // DUAL: lanes that supply MMA columns 4-7 (gid >= 4) read the second
+        // vector's table
+        const uint8_t *te_base = tab + ((size_t)U.tab + ((DUAL && C.gid >= 4) ? 1 : 0)) * P.tab_nsb * kTabSB;
         const int sbB = qe_sb_bytes(U.type);
         const int rb = (int)U.rb;
         for (int sp = 0; sp < U.nsplit; sp++) {
@@ -390,11 +413,22 @@ __global__ void __launch_bounds__(kQeThreadsMax, 1) k_qengine(const Job Jp, cons
                                      : st + (C.gid + 8) * pitch + (a_hi & 15);
             tile_sbs_rt<JobIq<Job>::v>(U.type, rg, rg8, te_base + (size_t)s0 * kTabSB, i0, i1, (int)(a_lo & 2) >> 1,
                                        C, yg, yg8, smem + P.iq_off, &P.iq);
-            quad_sum(yg, yg8);
-            if (C.tig == 0) {
-                double *rs = red + ((size_t)slot * P.cg + cw) * 16;
-                rs[C.gid] = yg;
-                rs[C.gid + 8] = yg8;
+            if constexpr (DUAL) {
+                // lanes tig 0,1 hold the first vector's columns, tig 2,3 the second's
+                yg += __shfl_xor_sync(0xffffffffu, yg, 1);
+                yg8 += __shfl_xor_sync(0xffffffffu, yg8, 1);
+                if ((C.tig & 1) == 0) {
+                    double *rs = red + ((size_t)slot * P.cg + cw) * RW + (C.tig == 2 ? 16 : 0);
+                    rs[C.gid] = yg;
+                    rs[C.gid + 8] = yg8;
+                }
+            } else {
+                quad_sum(yg, yg8);
+                if (C.tig == 0) {
+                    double *rs = red + ((size_t)slot * P.cg + cw) * RW;
+                    rs[C.gid] = yg;
+                    rs[C.gid + 8] = yg8;
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&ready[slot]);   // release: the partials above are visible to the reducer
@@ -473,7 +507,7 @@ inline void qe_groups_fmt(int maxn, int a, int b, int &cg, int &G) {
 // Host: shared-memory layout for a launch. item_bytes_max = the largest
 // item's row bytes (one row); returns 0 if nothing fits.
 inline int qe_layout(QeLayout &P, int G, int cg, uint32_t item_row_bytes_max, int n_tab, int tab_nsb,
-                     int64_t smem_optin, int64_t &smem, const IqLayout *iq = nullptr) {
+                     int64_t smem_optin, int64_t &smem, const IqLayout *iq = nullptr, int red_w = 16) {
     const uint32_t iq_bytes = iq ? iq->bytes : 0u;
     if (iq) P.iq = *iq;
     P.G = G;
@@ -485,7 +519,7 @@ inline int qe_layout(QeLayout &P, int G, int cg, uint32_t item_row_bytes_max, in
     P.stages = kQeMaxStages;
     for (;;) {
         P.red_off = ((3 * kQeMaxStages + 1) * 8 + 127) & ~127u;
-        P.tab_off = P.red_off + ((P.stages * cg * 16 * 8 + 127) & ~127u);
+        P.tab_off = P.red_off + ((P.stages * cg * red_w * 8 + 127) & ~127u);
         P.stage_off = P.tab_off + (((uint32_t)n_tab * tab_nsb * kTabSB + 127) & ~127u);
         P.iq_off = iq_bytes ? P.stage_off : 0u;
         P.stage_off += (iq_bytes + 127) & ~127u;

@@ -240,6 +240,64 @@ static int launch_matvec_engine(int t, const void *w, const float *x, float *y, 
     return launch_mv_job(J, P, smem, out_dim, st);
 }
 
+// Two activation vectors per pass over the weights (formats with
+// dual_format): MMA columns 0-3 carry vector 0's limbs, 4-7 vector 1's, so
+// each codebook row unpacked into A serves both.
+template <int T>
+struct MvPairJob : MvJob {
+    static constexpr int kIq = T;
+    static constexpr bool kDual = true;
+    int64_t in_dim;
+    float *y2;
+    __device__ uint32_t tab_mask(const uint8_t *) const { return 3u; }
+    __device__ int n_tab() const { return 2; }
+    __device__ const float *tab_src(int t) const { return x + (int64_t)t * in_dim; }
+    __device__ void finish(const uint8_t *, int64_t u, const QUnit &, double v, int lane) const {
+        const int64_t r = u * 16 + (lane & 15);
+        if (r < out_dim) (lane < 16 ? y : y2)[r] = (float)v;
+    }
+};
+
+// n_vec >= 2 on the engine: vectors in pairs (one launch per pair; an odd
+// last vector runs alone). Each pair reads the weights once.
+static int launch_matvec_pairs(int t, const void *w, const float *x, float *y, int64_t out_dim, int64_t in_dim,
+                               int64_t rb, int64_t n_vec, cudaStream_t st) {
+    DevInfo &di = dev_info();
+    const IqLayout iql = iq_layout(t, t);
+    const int nsb = (int)(in_dim / kQK);
+    const int64_t tabs = 2 * (int64_t)nsb * kTabSB + iql.bytes;
+    int nsplit = 0;
+    const int sbs = qe_sbs(t, nsb, qe_row_budget(di.smem_optin, tabs, 3), nsplit);
+    if (!sbs) return fail("matvec_q: no tensor-core split for type %d (pairs)", t);
+    QeLayout P;
+    int cg, G;
+    mv_groups(t, sbs, (int64_t)sbs * qe_sb_bytes(t), tabs, (out_dim + 15) / 16, cg, G);
+    int64_t smem = 0;
+    if (!qe_layout(P, G, cg, (uint32_t)sbs * qe_sb_bytes(t), 2, nsb, di.smem_optin, smem, &iql, 32))
+        return fail("matvec_q: paired tile needs %lld B of shared memory", (long long)smem);
+    P.err = di.err;
+    for (int64_t v = 0; v < n_vec; v += 2) {
+        if (v + 1 == n_vec) {
+            if (!launch_matvec_engine(t, w, x + v * in_dim, y + v * out_dim, out_dim, in_dim, rb, st)) return 0;
+            break;
+        }
+        auto run = [&](auto J) {
+            J.w = reinterpret_cast<const uint8_t *>(w);
+            J.rb = rb; J.out_dim = out_dim; J.type = t; J.nsb = nsb; J.sbs = sbs; J.nsplit = nsplit;
+            J.x = x + v * in_dim; J.y = y + v * out_dim; J.y2 = y + (v + 1) * out_dim; J.in_dim = in_dim;
+            return launch_mv_job(J, P, smem, out_dim, st);
+        };
+        int ok = 0;
+        switch (t) {
+        case T_IQ2_XXS: ok = run(MvPairJob<T_IQ2_XXS>{}); break;
+        case T_IQ3_XXS: ok = run(MvPairJob<T_IQ3_XXS>{}); break;
+        default: ok = run(MvPairJob<T_IQ1_S>{}); break;
+        }
+        if (!ok) return 0;
+    }
+    return 1;
+}
+
 // Up to kMvMulti matrices of one format and input width sharing one input x
 // (the q/k/v/r projections of an attention layer) in one engine launch: the
 // matrices' 16-row tiles are numbered consecutively, so small matrices do
@@ -628,6 +686,10 @@ int launch_matvec_q(int t, const void *w, const float *x, float *y, int64_t out_
     if (!w || !x || !y) return fail("matvec_q: null pointer");
     // K-quants with aligned rows run on the integer tensor cores
     if (engine_ok(t, w, x, in_dim, rb, n_vec)) return launch_matvec_engine(t, w, x, y, out_dim, in_dim, rb, st);
+    // (with fewer rows the fixed cost of one launch per pair loses to the
+    // CUDA-core batch kernel: measured at 2048 rows x 16 vectors)
+    if (n_vec > 1 && out_dim >= 4096 && dual_format(t) && engine_ok(t, w, x, in_dim, rb, 1))
+        return launch_matvec_pairs(t, w, x, y, out_dim, in_dim, rb, n_vec, st);
     if (iqb_ok(t, w, x, in_dim, rb, n_vec)) return launch_matvec_iqb(t, w, x, y, out_dim, in_dim, rb, n_vec, st);
     DevInfo &di = dev_info();
     const int nsb = (int)((in_dim + kQK - 1) / kQK);

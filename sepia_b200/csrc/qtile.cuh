@@ -215,6 +215,7 @@ struct LaneCtx {
     float lwg;           // group-sum MMAs (8 limb columns): 256^(2 tig)
     uint32_t bsel;       // byte_perm selector of the lane's group scale byte (group 2p + tig/2)
     uint32_t ssel0, ssel1;   // prmt selectors: byte tig/2 (resp. 2 + tig/2), sign-extended
+    int unit_off;            // two-vector units: from the lane's B table to its C columns' table
 };
 __device__ __forceinline__ LaneCtx lane_ctx(int lane) {
     LaneCtx L;
@@ -233,6 +234,7 @@ __device__ __forceinline__ LaneCtx lane_ctx(int lane) {
     const uint32_t j0 = (uint32_t)(L.tig >> 1), j1 = j0 + 2;
     L.ssel0 = j0 | ((j0 | 8) << 4) | ((j0 | 8) << 8) | ((j0 | 8) << 12);
     L.ssel1 = j1 | ((j1 | 8) << 4) | ((j1 | 8) << 8) | ((j1 | 8) << 12);
+    L.unit_off = 0;
     return L;
 }
 
@@ -642,7 +644,7 @@ __device__ __forceinline__ void sb_iq2xxs(const uint8_t *bg, const uint8_t *bg8,
         acc[2] += s8 * cc[2];
         acc[3] += s8 * cc[3];
     }
-    const float u = ld_unit(te) * C.lwn * 0.125f;
+    const float u = ld_unit(te + C.unit_off) * C.lwn * 0.125f;
     yg += (double)(cvt16<true>(ldh(bg)) * u) * limb_pair(acc[0], acc[1], 1.0f);
     yg8 += (double)(cvt16<true>(ldh(bg8)) * u) * limb_pair(acc[2], acc[3], 1.0f);
 }
@@ -704,7 +706,7 @@ __device__ __forceinline__ void sb_iq3xxs(const uint8_t *bg, const uint8_t *bg8,
         acc[2] += s8 * cc[2];
         acc[3] += s8 * cc[3];
     }
-    const float u = ld_unit(te) * C.lwn * 0.25f;
+    const float u = ld_unit(te + C.unit_off) * C.lwn * 0.25f;
     yg += (double)(cvt16<true>(ldh(bg)) * u) * limb_pair(acc[0], acc[1], 1.0f);
     yg8 += (double)(cvt16<true>(ldh(bg8)) * u) * limb_pair(acc[2], acc[3], 1.0f);
 }
@@ -730,7 +732,7 @@ __device__ __forceinline__ void sb_iq1s(const uint8_t *bg, const uint8_t *bg8, c
         acc[2] += s8 * cc[2];
         acc[3] += s8 * cc[3];
     }
-    const float u = ld_unit(te) * C.lwn * 0.125f;
+    const float u = ld_unit(te + C.unit_off) * C.lwn * 0.125f;
     yg += (double)(cvt16<true>(ldh(bg)) * u) * limb_pair(acc[0], acc[1], 1.0f);
     yg8 += (double)(cvt16<true>(ldh(bg8)) * u) * limb_pair(acc[2], acc[3], 1.0f);
 }

@@ -122,6 +122,29 @@ def test_matvec_batched(torch_cuda, oracle, t, n_vec):
             assert oracle.rel_err(one, got[v]) <= TOL
 
 
+@pytest.mark.parametrize("t", [Q.IQ1_S, Q.IQ2_XXS, Q.IQ3_XXS])
+@pytest.mark.parametrize("n_vec", [3, 5])
+def test_matvec_vector_pairs(torch_cuda, oracle, t, n_vec):
+    """Batches of these formats with >= 4096 rows run on the tensor-core
+    engine two vectors per pass (MMA columns 0-3 and 4-7): odd counts leave
+    a last single vector, 4100 rows a partial tile. Every vector within the
+    tolerance of the oracle and of its own batch-1 call."""
+    from sepia_b200 import ops
+    torch = torch_cuda
+    rng = np.random.default_rng(40 + n_vec + t)
+    out_dim, in_dim = 4100, 7168
+    w = synth.matrix_host(rng, t, out_dim, in_dim)
+    X = rng.standard_normal((n_vec, in_dim)).astype(np.float32)
+    X[1] *= 1e3          # a different x exponent per vector
+    wd = _dev(torch, w)
+    got = ops.matvec_q(t, wd, _dev(torch, X), out_dim, in_dim).cpu().numpy()
+    for v in range(n_vec):
+        want = oracle.qlinear(t, w, out_dim, in_dim, X[v], nthreads=8)
+        assert oracle.rel_err(got[v], want) <= TOL, v
+        one = ops.matvec_q(t, wd, _dev(torch, np.ascontiguousarray(X[v])), out_dim, in_dim).cpu().numpy()
+        assert oracle.rel_err(got[v], one) <= TOL, v
+
+
 @pytest.mark.parametrize("rows", [2048, 7168, 16384])
 @pytest.mark.parametrize("t", [Q.IQ1_S, Q.IQ2_XXS])
 def test_config3_full_rows(torch_cuda, oracle, t, rows):
