@@ -244,11 +244,12 @@ __global__ void __launch_bounds__(128) k_attn_prep(const PrepArgs A) {
     const double tau = (A.is_sliding || !A.tau_table) ? 1.0 : A.tau_table[pos];
     if ((int)blockIdx.x < A.H) {
         const int h = blockIdx.x;
+        const float qw = d < A.Dh ? A.q_norm[d] : 0.0f;
         if (d < A.Dh) v_sm[d] = A.q_raw[(int64_t)h * A.Dh + d];
         __syncthreads();
         const float inv = rms_inv(v_sm, A.Dh, A.eps, sh);
         if (d < A.Dh) {
-            const float qn = __fmul_rn(A.q_norm[d], __fmul_rn(v_sm[d], inv));
+            const float qn = __fmul_rn(qw, __fmul_rn(v_sm[d], inv));
             A.q_out[(int64_t)h * A.Dh + d] = (float)((double)qn * tau);
         }
         if (h == 0 && d == 0) {
@@ -261,6 +262,7 @@ __global__ void __launch_bounds__(128) k_attn_prep(const PrepArgs A) {
     }
     const int hk = blockIdx.x - A.H;
     const int64_t c = (int64_t)hk * A.Dh + d;
+    const float kw = d < A.Dh ? A.k_norm[d] : 0.0f;
     float kv = 0.0f;
     if (d < A.Dh) {
         kv = sconv1(A.k_sconv, A.k_hist, A.kv_dim, A.K, c, A.k_raw[c]);
@@ -270,7 +272,7 @@ __global__ void __launch_bounds__(128) k_attn_prep(const PrepArgs A) {
     }
     __syncthreads();
     const float inv = rms_inv(v_sm, A.Dh, A.eps, sh);
-    if (d < A.Dh) A.k_cache[pos * A.kv_dim + c] = __fmul_rn(A.k_norm[d], __fmul_rn(kv, inv));
+    if (d < A.Dh) A.k_cache[pos * A.kv_dim + c] = __fmul_rn(kw, __fmul_rn(kv, inv));
 }
 
 // --------------------------------------------------------- residual join
@@ -303,13 +305,15 @@ __global__ void __launch_bounds__(kClThreads) k_residual(const ResArgs A) {
     const int64_t per = (A.C + nr - 1) / nr;
     const int64_t c0 = rank * per, c1 = imin64(A.C, c0 + per);
     constexpr int kMaxPer = 8;          // channels per thread (hidden <= 8 * 1024 * kClusterCtas)
-    float xs[kMaxPer];
+    float xs[kMaxPer], nw[kMaxPer];
     double sq = 0.0;
 #pragma unroll
     for (int k = 0; k < kMaxPer; k++) {
         const int64_t c = c0 + threadIdx.x + (int64_t)k * blockDim.x;
         xs[k] = 0.0f;
+        nw[k] = 0.0f;
         if (c < c1) {
+            nw[k] = A.norm_w[c];      // fetched with the inputs: one memory round trip less
             const float v = A.use_scale ? __fmul_rn(A.in[c], A.scale) : A.in[c];
             const float o = sconv1(A.w, A.hist, A.C, A.K, c, v);
             const float xv = __fadd_rn(A.x[c], o);
@@ -323,7 +327,7 @@ __global__ void __launch_bounds__(kClThreads) k_residual(const ResArgs A) {
     for (int k = 0; k < kMaxPer; k++) {
         const int64_t c = c0 + threadIdx.x + (int64_t)k * blockDim.x;
         if (c < c1) {
-            float v = __fmul_rn(A.norm_w[c], __fmul_rn(xs[k], inv));
+            float v = __fmul_rn(nw[k], __fmul_rn(xs[k], inv));
             if (A.mup > 0.0f) v = __fdiv_rn(v, A.mup);
             A.xn[c] = v;
         }
