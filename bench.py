@@ -357,11 +357,9 @@ def kernel_lines(args):
 
         def slab(i):
             k = i % len(g)
-            ok(L.sepia_cuda_matvec_q(Q.Q2_K, g[k].data_ptr(), x.data_ptr(), ga.data_ptr(), 2048, 7168, 1, None))
-            ok(L.sepia_cuda_matvec_q(Q.Q2_K, u[k].data_ptr(), x.data_ptr(), ua.data_ptr(), 2048, 7168, 1, None))
-            ok(L.sepia_cuda_silu_mul(ga.data_ptr(), ua.data_ptr(), h.data_ptr(), 2048, None))
-            ok(L.sepia_cuda_matvec_q(Q.Q2_K, d[k].data_ptr(), h.data_ptr(), y.data_ptr(), 7168, 2048, 1, None))
-        emit("config1_q2k_swiglu_slab", 14516224, timeit(slab, 100), {"launches": 4})
+            ok(L.sepia_cuda_expert_swiglu(Q.Q2_K, g[k].data_ptr(), Q.Q2_K, u[k].data_ptr(), Q.Q2_K, d[k].data_ptr(),
+                                          7168, 2048, x.data_ptr(), h.data_ptr(), y.data_ptr(), None))
+        emit("config1_q2k_swiglu_slab", 14516224, timeit(slab, 100), {"launches": 2, "entry": "sepia_cuda_expert_swiglu"})
         del g, u, d
     for t, name in ((Q.IQ1_S, "iq1_s"), (Q.IQ2_XXS, "iq2_xxs")):
         for rows in (2048, 7168, 16384):

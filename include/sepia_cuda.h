@@ -56,6 +56,14 @@ int sepia_cuda_matvec_q(int ggml_type, const void *w, const float *x, float *y,
 int sepia_cuda_matvec_f32(const float *w, const float *x, float *y, int64_t out_dim, int64_t in_dim, void *stream);
 int sepia_cuda_rmsnorm(const float *w, const float *x, float *y, int64_t rows, int64_t n, float eps, void *stream);
 int sepia_cuda_silu_mul(const float *g, const float *u, float *z, int64_t n, void *stream);
+/* One expert's SwiGLU slab, y = down(silu(gate x) * (up x)) with h the
+ * [ff] intermediate (real_expert_ffn, src/sepia.c:2993-3022): gate/up
+ * [ff, hidden] and down [hidden, ff] in a format of the tensor-core engine
+ * (Q2_K/Q3_K/Q4_K, IQ2_XXS/IQ2_XS/IQ3_XXS/IQ1_S), x and h 16-byte aligned.
+ * Two launches (gate+up with the SwiGLU epilogue, then down). */
+int sepia_cuda_expert_swiglu(int gate_type, const void *gate, int up_type, const void *up, int down_type,
+                             const void *down, int64_t hidden, int64_t ff, const float *x, float *h, float *y,
+                             void *stream);
 int sepia_cuda_sconv(const float *w, const float *hist, const float *in, float *out,
                      int64_t C, int64_t K, int64_t T, void *stream);
 int sepia_cuda_sconv_hist_roll(float *hist, const float *in, int64_t C, int64_t K, int64_t T, void *stream);

@@ -23,6 +23,8 @@
 #include "stream.cuh"
 
 #include <algorithm>
+#include <cstring>
+#include <mutex>
 
 namespace sepia {
 
@@ -773,6 +775,15 @@ struct GuIqJob : GuJob {
 struct DnIqJob : DnJob {
     static constexpr int kIq = -1;
 };
+// Gate/up whose x may be written by the kernel right before it (no router in
+// between): the tables wait for the dependency.
+struct GuLateJob : GuJob {
+    static constexpr bool kTabsEarly = false;
+};
+struct GuIqLateJob : GuJob {
+    static constexpr int kIq = -1;
+    static constexpr bool kTabsEarly = false;
+};
 
 static bool engine_format(int t) { return mma_format(t) || iq_format(t); }
 
@@ -894,7 +905,8 @@ bool engine_down_ok(const MoeDev &L, const SepiaMoeWork *ws) {
 }
 
 
-static int launch_gateup_engine(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaStream_t st) {
+static int launch_gateup_engine(const MoeDev &L, const float *x, const SepiaMoeWork *ws, cudaStream_t st,
+                                bool early = true) {
     DevInfo &di = dev_info();
     GuJob J;
     J.L = L; J.idx = ws->topk_idx; J.weights = ws->weights; J.h = ws->h;
@@ -921,16 +933,15 @@ static int launch_gateup_engine(const MoeDev &L, const float *x, const SepiaMoeW
     const int64_t units = (int64_t)J.n_slots * J.tpu;
     if (units >= kQeDivMax) return fail("moe: %lld gate/up units exceed the engine's index range", (long long)units);
     const unsigned grid = (unsigned)std::min<int64_t>(units, di.sm_count);
-    if (iqb) {
-        GuIqJob JI;
-        static_cast<GuJob &>(JI) = J;
-        if (!ensure_smem((const void *)k_qengine<GuIqJob>, (int)smem)) return 0;
-        return check(launch_pdl(k_qengine<GuIqJob>, grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, JI, P),
+    auto run = [&](auto JV) {
+        using JT = decltype(JV);
+        static_cast<GuJob &>(JV) = J;
+        if (!ensure_smem((const void *)k_qengine<JT>, (int)smem)) return 0;
+        return check(launch_pdl(k_qengine<JT>, grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, JV, P),
                      "moe gate/up (tensor cores) launch");
-    }
-    if (!ensure_smem((const void *)k_qengine<GuJob>, (int)smem)) return 0;
-    return check(launch_pdl(k_qengine<GuJob>, grid, (P.G * P.cg + 2) * 32, (size_t)smem, st, J, P),
-                 "moe gate/up (tensor cores) launch");
+    };
+    if (iqb) return early ? run(GuIqJob{}) : run(GuIqLateJob{});
+    return early ? run(GuJob{}) : run(GuLateJob{});
 }
 
 static int launch_down_engine(const MoeDev &L, const SepiaMoeWork *ws, float *out, float *slots_out, bool clear,
@@ -1180,6 +1191,65 @@ extern "C" int sepia_cuda_moe_layer(const SepiaMoeLayer *Lh, const float *x, con
     cudaStream_t st = as_stream(stream);
     if (!launch_router(L, x, ws, st)) return 0;
     return launch_experts(L, x, ws, out, nullptr, st);
+}
+
+// ------------------------------------------------ one expert's SwiGLU slab
+// The expert kernels with a fixed one-slot selection (expert 0, weight 1)
+// kept in device constants: the slab runs as two engine launches (gate+up
+// with the SwiGLU epilogue, then down writing y) instead of three matvecs
+// and an elementwise kernel.
+static __device__ int32_t g_slab_idx = 0;
+static __device__ float g_slab_w = 1.0f;
+
+extern "C" int sepia_cuda_expert_swiglu(int gate_type, const void *gate, int up_type, const void *up, int down_type,
+                                        const void *down, int64_t hidden, int64_t ff, const float *x, float *h,
+                                        float *y, void *stream) {
+    using namespace sepia;
+    if (!gate || !up || !down || !x || !h || !y || hidden <= 0 || ff <= 0) return fail("expert_swiglu: bad arguments");
+    cudaStream_t st = as_stream(stream);
+    MoeDev L;
+    memset(&L, 0, sizeof L);
+    L.hidden = hidden; L.ff = ff;
+    L.n_routed = 1; L.n_shared = 0; L.topk = 1;
+    L.route_scale = 1.0; L.global_scale = 1.0f;
+    L.gate_type = gate_type; L.up_type = up_type; L.down_type = down_type;
+    L.gate = (const uint8_t *)gate; L.up = (const uint8_t *)up; L.down = (const uint8_t *)down;
+    L.rb_gate = host_row_bytes(gate_type, hidden); L.rb_up = host_row_bytes(up_type, hidden);
+    L.rb_down = host_row_bytes(down_type, ff);
+    if (L.rb_gate <= 0 || L.rb_up <= 0 || L.rb_down <= 0) return fail("expert_swiglu: unsupported types or dims");
+    L.gate_stride = L.rb_gate * ff; L.up_stride = L.rb_up * ff; L.down_stride = L.rb_down * hidden;
+    L.rank = 0; L.world = 1; L.expert_slot = nullptr;
+    L.err = dev_info().err;
+    const bool eng = gate_type == up_type && engine_gateup_ok(L, nullptr) && engine_down_ok(L, nullptr) &&
+                     (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(h) & 15) == 0;
+    if (!eng)
+        return fail("expert_swiglu: types %d/%d/%d or alignment not on the tensor-core engine "
+                    "(use matvec_q + silu_mul)", gate_type, up_type, down_type);
+    // the one-slot selection, looked up once per device
+    static std::mutex mu;
+    static int32_t *idx_d[64] = {};
+    static float *w_d[64] = {};
+    int dev = 0;
+    if (!check(cudaGetDevice(&dev), "expert_swiglu: cudaGetDevice")) return 0;
+    if (dev < 0 || dev >= 64) return fail("expert_swiglu: device %d out of range", dev);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!idx_d[dev]) {
+            void *a = nullptr, *b = nullptr;
+            if (!check(cudaGetSymbolAddress(&a, g_slab_idx), "expert_swiglu: cudaGetSymbolAddress") ||
+                !check(cudaGetSymbolAddress(&b, g_slab_w), "expert_swiglu: cudaGetSymbolAddress"))
+                return 0;
+            idx_d[dev] = (int32_t *)a;
+            w_d[dev] = (float *)b;
+        }
+    }
+    SepiaMoeWork ws;
+    memset(&ws, 0, sizeof ws);
+    ws.topk_idx = idx_d[dev];
+    ws.weights = w_d[dev];
+    ws.h = h;
+    ws.slots = y;
+    return launch_gateup_engine(L, x, &ws, st, false) && launch_down_engine(L, &ws, y, y, false, st);
 }
 
 extern "C" int sepia_cuda_topk_select(const float *scores, int32_t n, int32_t topk, int32_t *idx, void *stream) {

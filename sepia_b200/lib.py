@@ -121,6 +121,7 @@ _PROTOS = {
     "sepia_cuda_matvec_f32": (C.c_int, [vp, vp, vp, i64, i64, vp]),
     "sepia_cuda_rmsnorm": (C.c_int, [vp, vp, vp, i64, i64, C.c_float, vp]),
     "sepia_cuda_silu_mul": (C.c_int, [vp, vp, vp, i64, vp]),
+    "sepia_cuda_expert_swiglu": (C.c_int, [C.c_int, vp, C.c_int, vp, C.c_int, vp, i64, i64, vp, vp, vp, vp]),
     "sepia_cuda_sconv": (C.c_int, [vp, vp, vp, vp, i64, i64, i64, vp]),
     "sepia_cuda_sconv_hist_roll": (C.c_int, [vp, vp, i64, i64, i64, vp]),
     "sepia_cuda_moe_work_bytes": (C.c_size_t, [C.POINTER(SepiaMoeLayer)]),

@@ -197,6 +197,31 @@ def test_config1_swiglu_slab(torch_cuda, oracle):
     assert oracle.rel_err(y, want) <= TOL
 
 
+@pytest.mark.parametrize("types", [(Q.Q2_K, Q.Q2_K, Q.Q2_K), (Q.IQ2_XS, Q.IQ2_XS, Q.IQ3_XXS)],
+                         ids=["q2k", "iq2xs_iq3xxs"])
+def test_expert_swiglu_entry(torch_cuda, oracle, types):
+    """sepia_cuda_expert_swiglu (two engine launches) on BASELINE
+    configuration 1's shapes, against the oracle's real_expert_ffn; run
+    twice (the fixed one-slot selection is reused)."""
+    from sepia_b200.lib import load, ok
+    torch = torch_cuda
+    tg, tu, td = types
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal(7168).astype(np.float32)
+    g = synth.matrix_host(rng, tg, 2048, 7168)
+    u = synth.matrix_host(rng, tu, 2048, 7168)
+    d = synth.matrix_host(rng, td, 7168, 2048)
+    want = oracle.expert_swiglu(tg, g, tu, u, td, d, 7168, 2048, x, nthreads=8)
+    gd, ud, dd, xd = _dev(torch, g), _dev(torch, u), _dev(torch, d), _dev(torch, x)
+    h = torch.empty(2048, dtype=torch.float32, device="cuda")
+    for _ in range(2):
+        y = torch.full((7168,), float("nan"), dtype=torch.float32, device="cuda")
+        ok(load().sepia_cuda_expert_swiglu(tg, gd.data_ptr(), tu, ud.data_ptr(), td, dd.data_ptr(), 7168, 2048,
+                                           xd.data_ptr(), h.data_ptr(), y.data_ptr(),
+                                           torch.cuda.current_stream().cuda_stream))
+        assert oracle.rel_err(y.cpu().numpy(), want) <= TOL
+
+
 def test_bad_arguments_rejected(torch_cuda):
     from sepia_b200.lib import load
     torch = torch_cuda
